@@ -1,0 +1,167 @@
+// Shared device helpers: element formats, bit tricks, bounded waits.
+//
+// All float-format conversions are written here from the format definitions
+// (IEEE-754 binary32, bfloat16, OCP FP8 e4m3fn / e5m2) with integer
+// arithmetic, so the rounding of every cast is explicit and matches the
+// reference's PyTorch / Triton casts bit for bit:
+//   * fp32 -> bf16: round to nearest even;
+//   * fp32 -> e4m3fn: round to nearest even, |x| > 464 -> NaN (0x7F), which
+//     is what torch's float8_e4m3fn cast does (c10 semantics);
+//   * fp8 / bf16 -> fp32: exact.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/bitsparse.h"
+
+namespace bs {
+
+constexpr int kTileM = 64;
+constexpr int kTileN = 64;
+constexpr int kTileNumel = 4096;
+constexpr int kTileBytes = 512;
+constexpr int kThreads = 256;
+
+// Upper bound on polls of another CTA's scan flag before giving up.  A poll
+// is a few hundred ns, so this is far above any legitimate wait (the CTAs
+// polled are already running) and well under a second.
+constexpr uint32_t kMaxPolls = 1u << 21;
+
+// ---------------------------------------------------------------------------
+// Format helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) {
+  return __uint_as_float(b << 16);
+}
+
+__device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return ((u >> 16) & 0x8000u) | 0x7FC0u;
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return u >> 16;
+}
+
+// e4m3fn: 1 sign, 4 exponent (bias 7), 3 mantissa; 0x7F/0xFF are NaN, no inf.
+__device__ __forceinline__ float e4m3_bits_to_f32(uint32_t b) {
+  uint32_t s = (b & 0x80u) << 24;
+  uint32_t e = (b >> 3) & 0xFu, m = b & 7u;
+  if ((b & 0x7Fu) == 0x7Fu) return __uint_as_float(0x7FC00000u | s);
+  if (e == 0) {  // subnormal: m * 2^-9
+    return __uint_as_float(s) + (s ? -1.f : 1.f) * (float)m * 0.001953125f;
+  }
+  return __uint_as_float(s | ((e + 120u) << 23) | (m << 20));
+}
+
+// e5m2: 1 sign, 5 exponent (bias 15), 2 mantissa; IEEE-style inf / NaN.
+__device__ __forceinline__ float e5m2_bits_to_f32(uint32_t b) {
+  uint32_t s = (b & 0x80u) << 24;
+  uint32_t e = (b >> 2) & 0x1Fu, m = b & 3u;
+  if (e == 0x1F) return __uint_as_float(s | 0x7F800000u | (m ? 0x400000u : 0u));
+  if (e == 0) {  // subnormal: m * 2^-16
+    return __uint_as_float(s) + (s ? -1.f : 1.f) * (float)m * 1.52587890625e-05f;
+  }
+  return __uint_as_float(s | ((e + 112u) << 23) | (m << 21));
+}
+
+template <int DT>
+__device__ __forceinline__ float store_bits_to_f32(uint32_t b) {
+  if constexpr (DT == BS_BF16) return bf16_bits_to_f32(b);
+  else if constexpr (DT == BS_E4M3) return e4m3_bits_to_f32(b);
+  else return e5m2_bits_to_f32(b);
+}
+
+// fp32 -> e4m3fn bits, round to nearest even (torch float8_e4m3fn cast).
+__device__ __forceinline__ uint32_t f32_to_e4m3_bits(float f) {
+  uint32_t u = __float_as_uint(f);
+  uint32_t s = (u >> 24) & 0x80u;
+  uint32_t a = u & 0x7FFFFFFFu;
+  if (a > 0x43E80000u) return s | 0x7Fu;  // > 464 (or NaN): NaN
+  if (a < 0x3C800000u) {                  // < 2^-6: subnormal range
+    // value = a_f; quantum 2^-9.  Round a_f / 2^-9 to nearest even integer.
+    float af = __uint_as_float(a) * 512.0f;  // exact (power of two scale)
+    // af < 8; split into integer and fraction exactly.
+    uint32_t i = (uint32_t)af;               // truncation
+    float frac = af - (float)i;              // exact
+    if (frac > 0.5f || (frac == 0.5f && (i & 1u))) ++i;
+    return s | i;  // i == 8 gives 0x08 = smallest normal, correct
+  }
+  // normal: keep 3 mantissa bits, RNE on the 20 dropped bits
+  uint32_t exp = (a >> 23) - 120u;  // biased e4m3 exponent, >= 1
+  uint32_t mant = a & 0x7FFFFFu;
+  uint32_t q = (exp << 3) | (mant >> 20);
+  uint32_t rem = mant & 0xFFFFFu;
+  if (rem > 0x80000u || (rem == 0x80000u && (q & 1u))) ++q;
+  // q can reach 0x7F only for values in (448, 464]: 464 ties to even (0x7E)
+  // is handled by RNE above; anything that rounds to 0x7F is > 464 and was
+  // already caught by the NaN test.
+  return s | q;
+}
+
+// Positive test on raw bits (x > 0.0 as a float; NaN and -0 are not).
+template <int DT>
+__device__ __forceinline__ bool is_pos(uint32_t b) {
+  if constexpr (DT == BS_BF16) return b - 1u < 0x7F80u;   // 1..0x7F80
+  else if constexpr (DT == BS_E4M3) return b - 1u < 0x7Eu;  // 1..0x7E
+  else if constexpr (DT == BS_E5M2) return b - 1u < 0x7Cu;  // 1..0x7C
+  else return b - 1u < 0x7F800000u;                          // fp32
+}
+
+template <int DT> struct Elt;
+template <> struct Elt<BS_BF16> { static constexpr int bytes = 2; };
+template <> struct Elt<BS_E4M3> { static constexpr int bytes = 1; };
+template <> struct Elt<BS_E5M2> { static constexpr int bytes = 1; };
+template <> struct Elt<BS_F32> { static constexpr int bytes = 4; };
+
+template <int DT>
+__device__ __forceinline__ constexpr int pack_bits() {
+  return DT == BS_BF16 ? 15 : 7;
+}
+
+// ---------------------------------------------------------------------------
+// Warp / memory helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t warp_incl_scan(uint32_t v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    uint32_t n = __shfl_up_sync(0xFFFFFFFFu, v, d);
+    if (lane >= d) v += n;
+  }
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void st_v4(void *p, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void status_or(int32_t *status, int bits) {
+  if (status) atomicOr(status, bits);
+}
+
+}  // namespace bs

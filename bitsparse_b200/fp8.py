@@ -1,0 +1,135 @@
+"""FP8 helpers: per-tensor e4m3 quantiser and the FP8 matmul autograd op.
+
+Mirrors lib_sparse/fp8.py (Maxzhu123/bitsparse).  ``to_fp8`` runs on this
+library's CUDA kernels (amax -> scale, then quantise).  The FP8 GEMMs are
+plain library GEMMs (cuBLASLt through ``F.scaled_mm``), as in the reference.
+
+Two deliberate differences from the reference, both bug fixes:
+
+* ``matmul`` passes the scales positionally: the reference's keyword call
+  (lib_sparse/fp8.py:120) is rejected by ``autograd.Function.apply`` on
+  current PyTorch because ``MatmulFp8`` defines no ``setup_context``;
+* operand B is made column-major whenever it is not (cuBLASLt's FP8 layout
+  rule on B200, compute capability 10.0); the reference only does this for
+  capability < 12 (lib_sparse/fp8.py:15-17), which includes B200 anyway.
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+from torch.autograd import Function
+from torch.nn import functional as F
+
+from .config import CACHE_FP8_MATMUl
+
+_FP8_DTYPES = (torch.float8_e4m3fn, torch.float8_e5m2)
+_FP8_DTYPE = torch.float8_e4m3fn
+_FP8_MAX = torch.finfo(_FP8_DTYPE).max
+
+
+def is_fp8(dtype) -> bool:
+    """True for the supported 8-bit float storage dtypes (e4m3fn, e5m2)."""
+    return dtype in _FP8_DTYPES
+
+
+@torch.no_grad()
+def fp8_scale(x: Tensor) -> Tensor:
+    """Per-tensor scale of to_fp8: max(amax(|x|) / 448, 1e-9), fp32 0-dim.
+
+    For bf16 input amax / 448 is rounded to bf16 first (the eager PyTorch
+    semantics of lib_sparse/fp8.py:126 on a bf16 tensor)."""
+    from . import _lib, _runtime as R
+
+    R.require_cuda(x, "x")
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("to_fp8 takes bfloat16 or float32 input")
+    x = x.contiguous()
+    scale = torch.empty((), dtype=torch.float32, device=x.device)
+    _lib.call("bs_fp8_scale", x.data_ptr(), R.dtype_code(x.dtype), x.numel(),
+              R.amax_scratch(x.device).data_ptr(), scale.data_ptr(),
+              R.stream_handle(x.device))
+    return scale
+
+
+@torch.no_grad()
+def quantize_e4m3(x: Tensor, scale: Tensor) -> Tensor:
+    """e4m3fn(x / scale), elementwise (bf16 input: quotient rounded to bf16)."""
+    from . import _lib, _runtime as R
+
+    x = x.contiguous()
+    q = torch.empty(x.shape, dtype=_FP8_DTYPE, device=x.device)
+    _lib.call("bs_quantize_e4m3", x.data_ptr(), R.dtype_code(x.dtype), x.numel(),
+              scale.data_ptr(), q.data_ptr(), R.stream_handle(x.device))
+    return q
+
+
+@torch.no_grad()
+def to_fp8(x: Tensor) -> tuple[Tensor, Tensor]:
+    """(x_fp8, scale): per-tensor e4m3fn quantisation (lib_sparse/fp8.py:123-129)."""
+    scale = fp8_scale(x)
+    return quantize_e4m3(x, scale), scale
+
+
+def _scaled_mm(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor,
+               output_dtype: torch.dtype) -> Tensor:
+    """FP8 GEMM with tensor-wise scales (lib_sparse/fp8.py:25-49)."""
+    if a.stride(1) != 1:
+        a = a.contiguous()
+    if b.stride(0) != 1:
+        b = b.T.contiguous().T
+    return F.scaled_mm(
+        mat_a=a, mat_b=b,
+        scale_a=a_scale, scale_b=b_scale, output_dtype=output_dtype,
+        scale_recipe_a=F.ScalingType.TensorWise, scale_recipe_b=F.ScalingType.TensorWise,
+    )
+
+
+class MatmulFp8(Function):
+    """a @ b through FP8 GEMMs in forward and backward (lib_sparse/fp8.py:52-115)."""
+
+    @staticmethod
+    def forward(ctx, a: Tensor, b: Tensor, a_scale: Tensor | None = None,
+                b_scale: Tensor | None = None) -> Tensor:
+        if not CACHE_FP8_MATMUl:
+            ctx.save_for_backward(a, b)
+            ctx.a_scale, ctx.b_scale = a_scale, b_scale
+        if a.dtype == torch.bfloat16:
+            assert a_scale is None
+            a_fp8, a_scale = to_fp8(a)
+        else:
+            assert a_scale is not None
+            a_fp8 = a
+        if b.dtype == torch.bfloat16:
+            assert b_scale is None
+            b_fp8, b_scale = to_fp8(b)
+        else:
+            assert b_scale is not None
+            b_fp8 = b
+        if CACHE_FP8_MATMUl:
+            ctx.save_for_backward(a_fp8, b_fp8, a_scale, b_scale)
+        return _scaled_mm(a_fp8.contiguous(), b_fp8, a_scale, b_scale,
+                          output_dtype=torch.bfloat16)
+
+    @staticmethod
+    def backward(ctx, grad_output: Tensor):
+        if CACHE_FP8_MATMUl:
+            a_fp8, b_fp8, a_scale, b_scale = ctx.saved_tensors
+        else:
+            a, b = ctx.saved_tensors
+            a_scale, b_scale = ctx.a_scale, ctx.b_scale
+            a_fp8, a_scale = to_fp8(a) if a.dtype == torch.bfloat16 else (a, a_scale)
+            b_fp8, b_scale = to_fp8(b) if b.dtype == torch.bfloat16 else (b, b_scale)
+        g_fp8, g_scale = to_fp8(grad_output.contiguous())
+        grad_a = grad_b = None
+        if ctx.needs_input_grad[0]:
+            grad_a = _scaled_mm(g_fp8, b_fp8.T, g_scale, b_scale, output_dtype=torch.bfloat16)
+        if ctx.needs_input_grad[1]:
+            grad_b = _scaled_mm(a_fp8.T.contiguous(), g_fp8, a_scale, g_scale,
+                                output_dtype=torch.bfloat16)
+        return grad_a, grad_b, None, None
+
+
+def matmul(a: Tensor, b: Tensor, fp8: bool, a_scale: Tensor | None = None,
+           b_scale: Tensor | None = None) -> Tensor:
+    """a @ b; FP8 GEMM when ``fp8`` (lib_sparse/fp8.py:118-120)."""
+    return MatmulFp8.apply(a, b, a_scale, b_scale) if fp8 else a @ b

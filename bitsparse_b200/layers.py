@@ -1,0 +1,140 @@
+"""Autograd layers that keep the MLP activation compressed between forward
+and backward (lib_sparse/layers.py, Maxzhu123/bitsparse).
+
+Weight convention (as in the reference's code): W1 [d_ff, d_in],
+W2 [d_out, d_ff], y = relu(x W1^T + b1) W2^T + b2.  Same classes, argument
+names and gradient tuples as the reference.
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+from torch.autograd import Function
+
+from .bitsparse import BitsparseTensor, TensorBuffer
+from .config import RELU2_SCALE
+from .fp8 import is_fp8, matmul, to_fp8
+from .src.functions import dense_to_tilesparse, relu_to_tilesparse_fp8
+from .src.operators import mask_with_bitmask_, relu2_grad_sparse_
+from .src.sparse_matmul import AspB, AspRelu2B
+
+
+class ReluLinear(Function):
+    """y = relu(z) @ W^T with relu(z) stored compressed (lib_sparse/layers.py:20-66)."""
+
+    @staticmethod
+    def forward(ctx, z, W, sparse_data: TensorBuffer | None = None, pack_sbit: bool = False,
+                dtype: torch.dtype = torch.bfloat16):
+        ctx.dtype = dtype
+        ctx.save_for_backward(W)
+        h = z.relu_()
+        if is_fp8(dtype):
+            h, h_sparse = relu_to_tilesparse_fp8(h, sparse_data, pack_sbit)
+            scale = h_sparse.scale
+        else:
+            scale = None
+            h_sparse = dense_to_tilesparse(h, scale, sparse_data, pack_sbit)
+        ctx.h_sparse = h_sparse
+        return matmul(h, W.T, is_fp8(dtype), a_scale=scale)
+
+    @staticmethod
+    @torch.compiler.disable
+    def backward(ctx, grad_output: Tensor):
+        W = ctx.saved_tensors[0]
+        needs_z = ctx.needs_input_grad[0]
+        h: BitsparseTensor = ctx.h_sparse
+        ctx.h_sparse = None
+        fp8 = is_fp8(ctx.dtype)
+        if fp8:
+            grad_output, scale = to_fp8(grad_output.contiguous())
+        else:
+            scale = None
+        grad_W2 = AspB(grad_output.T, h, A_scale=scale)
+        if needs_z:
+            grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
+            grad_z = mask_with_bitmask_(grad_h, h)
+        else:
+            grad_z = None
+        return grad_z, grad_W2, None, None, None
+
+
+class FFNRelu:
+    """Two-layer ReLU FFN with the hidden activation stored compressed
+    (lib_sparse/layers.py:69-94)."""
+
+    @staticmethod
+    def apply(x, W1, W2, b1=None, b2=None, *,
+              sparse_data: TensorBuffer | None = None, pack_sbit: bool = False,
+              dtype: torch.dtype = torch.bfloat16):
+        """x [*bs, d_in], W1 [d_ff, d_in], W2 [d_out, d_ff] -> [*bs, d_out]."""
+        bs_dims = x.shape[:-1]
+        x = x.reshape(-1, x.shape[-1])
+        z = matmul(x, W1.T, is_fp8(dtype))
+        if b1 is not None:
+            z = z + b1
+        y = ReluLinear.apply(z, W2, sparse_data, pack_sbit, dtype)
+        y = y.reshape(*bs_dims, y.shape[-1])
+        if b2 is not None:
+            y = y + b2
+        return y
+
+
+class Relu2Linear(Function):
+    """y = k relu(z)^2 @ W^T with relu(z) stored compressed
+    (lib_sparse/layers.py:100-151)."""
+
+    @staticmethod
+    def forward(ctx, z, W, sparse_data: TensorBuffer | None, pack_sbit: bool = False,
+                storage_dtype: torch.dtype = torch.bfloat16):
+        ctx.dtype = storage_dtype
+        ctx.save_for_backward(W)
+        h = z.relu_()
+        if is_fp8(storage_dtype):
+            _, h_sparse = relu_to_tilesparse_fp8(h, sparse_data, pack_sbit)
+        else:
+            h_sparse = dense_to_tilesparse(h, None, sparse_data, pack_sbit)
+        ctx.h_sparse = h_sparse
+        h.square_()
+        h.mul_(RELU2_SCALE)
+        return matmul(h, W.T, is_fp8(storage_dtype))
+
+    @staticmethod
+    @torch.compiler.disable
+    def backward(ctx, grad_output: Tensor):
+        W = ctx.saved_tensors[0]
+        needs_z = ctx.needs_input_grad[0]
+        h: BitsparseTensor = ctx.h_sparse
+        ctx.h_sparse = None
+        fp8 = is_fp8(ctx.dtype)
+        if fp8:
+            grad_output, scale = to_fp8(grad_output.contiguous())
+        else:
+            scale = None
+        grad_W2 = AspRelu2B(grad_output.T, h, A_scale=scale)
+        if needs_z:
+            grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
+            grad_z = relu2_grad_sparse_(grad_h, h)
+        else:
+            grad_z = None
+        return grad_z, grad_W2, None, None, None
+
+
+class FFNRelu2:
+    """Two-layer ReLU^2 FFN with the hidden activation stored compressed
+    (lib_sparse/layers.py:154-177)."""
+
+    @staticmethod
+    def apply(x, W1, W2, b1=None, b2=None, *,
+              sparse_data: TensorBuffer | None = None, pack_sbit: bool = False,
+              storage_dtype: torch.dtype = torch.bfloat16):
+        """x [*bs, d_in], W1 [d_ff, d_in], W2 [d_out, d_ff] -> [*bs, d_out]."""
+        bs_dims = x.shape[:-1]
+        x = x.reshape(-1, x.shape[-1])
+        z = matmul(x, W1.T, is_fp8(storage_dtype))
+        if b1 is not None:
+            z = z + b1
+        y = Relu2Linear.apply(z, W2, sparse_data, pack_sbit, storage_dtype)
+        y = y.reshape(*bs_dims, y.shape[-1])
+        if b2 is not None:
+            y = y + b2
+        return y

@@ -1,0 +1,247 @@
+"""Operator boundary: the reference's triton_operators API on CUDA kernels.
+
+Same function names, arguments, in-place semantics and return values as
+lib_sparse/src/triton_operators.py (Maxzhu123/bitsparse); every function
+is a thin launcher of a C-ABI entry point of libbitsparse_b200.so.  All
+work is enqueued on the current CUDA stream.  There is no CPU path: CPU
+tensors are rejected.
+
+Plus the fused single-pass compressor ``compress`` used by
+``dense_to_tilesparse``.
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from .. import _lib
+from .. import _runtime as R
+from ..bitsparse import BitsparseTensor, bits_per_value, tile_grid
+from ..config import BLOCK_M as _BM, BLOCK_N as _BN, RELU2_SCALE
+from ..fp8 import is_fp8
+from .bitpacking import packed_storage_nbytes
+
+if RELU2_SCALE != 1:  # the kernels take k as a parameter fixed to 1.0 below
+    raise NotImplementedError("RELU2_SCALE other than 1 is not wired to the kernels")
+
+
+def _check_tiles(BLOCK_M: int, BLOCK_N: int) -> None:
+    if (BLOCK_M, BLOCK_N) != (64, 64):
+        raise ValueError("bitsparse_b200 kernels are built for 64x64 tiles")
+
+
+def _row_major(t: Tensor, name: str) -> tuple[Tensor, int]:
+    """(tensor, row stride in elements) for a 2-D tensor with unit column stride."""
+    R.require_cuda(t, name)
+    if t.dim() != 2:
+        raise ValueError(f"{name} must be 2-D")
+    if t.stride(1) != 1 or t.stride(0) < t.shape[1]:
+        t = t.contiguous()
+    return t, max(t.stride(0), t.shape[1])
+
+
+def _stream(t: Tensor) -> int:
+    return R.stream_handle(t.device)
+
+
+# ---------------------------------------------------------------------------
+# Compression
+# ---------------------------------------------------------------------------
+def tile_pack(
+    dense: Tensor, tile_counts: Tensor, tile_bitmasks: Tensor,
+    M: int, N: int, grid_m: int, grid_n: int,
+    BLOCK_M: int, BLOCK_N: int, TILE_NUMEL: int, TILE_BYTES: int,
+) -> None:
+    """Bitmask + per-tile nonzero counts, in place (triton_operators.py:21-33)."""
+    _check_tiles(BLOCK_M, BLOCK_N)
+    dense, ld = _row_major(dense, "dense")
+    _lib.call("bs_tile_pack", dense.data_ptr(), R.dtype_code(dense.dtype), M, N, ld,
+              tile_counts.data_ptr(), tile_bitmasks.data_ptr(), _stream(dense))
+
+
+def compact_vals(
+    dense: Tensor, tile_bitmasks: Tensor, tile_prefix: Tensor,
+    vals: Tensor | None, vals_offset: Tensor | None,
+    M: int, N: int, grid_n: int, num_tiles: int,
+    BLOCK_M: int, BLOCK_N: int, TILE_NUMEL: int, pack_sbit: bool,
+) -> tuple[Tensor, Tensor]:
+    """Compact positives into standalone or preallocated storage
+    (triton_operators.py:36-115).  Standalone storage syncs once for nnz,
+    as the reference does (triton_operators.py:50)."""
+    _check_tiles(BLOCK_M, BLOCK_N)
+    dense, ld = _row_major(dense, "dense")
+    dt = dense.dtype
+    if vals is None:
+        nnz = int(tile_prefix[-1].item())
+        if pack_sbit:
+            vals = torch.zeros(packed_storage_nbytes(nnz, bits_per_value(dt)),
+                               device=dense.device, dtype=torch.uint8)
+        else:
+            vals = torch.empty(nnz, device=dense.device, dtype=dt)
+        vals_offset = torch.zeros((), device=dense.device, dtype=torch.int64)
+    cap = vals.numel() * (vals.element_size() if pack_sbit else 1)
+    _lib.call("bs_compact_vals", dense.data_ptr(), R.dtype_code(dt), M, N, ld,
+              tile_prefix.data_ptr(), vals.data_ptr(), cap, int(pack_sbit),
+              R.ptr(vals_offset), R.status_word(dense.device).data_ptr(), _stream(dense))
+    return vals, vals_offset
+
+
+def compress(dense: Tensor, scale: Tensor | None = None, sparse_data=None,
+             pack_sbit: bool = False, quant_scale: Tensor | None = None,
+             quant_out: Tensor | None = None) -> BitsparseTensor:
+    """Fused single-pass compression of a 2-D dense tensor.
+
+    One kernel writes the bitmask, the prefix and the values (and advances a
+    TensorBuffer's offset on the device).  With ``quant_scale`` (fp32 0-dim
+    device tensor) a bf16 / fp32 input is quantised to e4m3fn in the same
+    pass, exactly as ``to_fp8`` would, and ``quant_out`` (optional, e4m3
+    [M, N]) receives the dense quantised tensor.
+
+    Standalone storage (``sparse_data is None``): the values are compacted
+    into a worst-case scratch tensor, the total is read back (one host sync,
+    like the reference's compact_vals) and copied into an exactly sized
+    tensor.  With a TensorBuffer there is no sync.
+    """
+    dense, ld = _row_major(dense, "dense")
+    M, N = dense.shape
+    grid_m, grid_n, T, _, TB = tile_grid(M, N, _BM, _BN)
+    dev = dense.device
+    stored = torch.float8_e4m3fn if quant_scale is not None else dense.dtype
+    if quant_scale is None and stored not in (torch.bfloat16,) and not is_fp8(stored):
+        raise TypeError("BitsparseTensor supports bfloat16 and FP8 (e4m3fn/e5m2) values")
+    bits = bits_per_value(stored)
+    bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
+    prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
+    ws = R.workspace(dev, T)
+    status = R.status_word(dev)
+    qs = R.ptr(quant_scale)
+    qo = R.ptr(quant_out)
+    if quant_out is not None and (quant_out.dtype != torch.float8_e4m3fn
+                                  or not quant_out.is_contiguous()
+                                  or tuple(quant_out.shape) != (M, N)):
+        raise ValueError("quant_out must be a contiguous float8_e4m3fn [M, N] tensor")
+    st = _stream(dense)
+    if sparse_data is None:
+        if T == 0:
+            prefix.zero_()
+            vals = torch.empty(packed_storage_nbytes(0, bits) if pack_sbit else 0,
+                               device=dev, dtype=torch.uint8 if pack_sbit else stored)
+            if pack_sbit:
+                vals.zero_()
+            vals_offset = torch.zeros((), device=dev, dtype=torch.int64)
+        else:
+            if pack_sbit:
+                tmp = torch.empty(packed_storage_nbytes(M * N, bits), device=dev,
+                                  dtype=torch.uint8)
+                cap = tmp.numel()
+            else:
+                tmp = torch.empty(M * N, device=dev, dtype=stored)
+                cap = M * N
+            nnz_t = torch.empty((), device=dev, dtype=torch.int64)
+            _lib.call("bs_compress", dense.data_ptr(), R.dtype_code(dense.dtype), M, N, ld,
+                      qs, qo, bitmask.data_ptr(), prefix.data_ptr(), tmp.data_ptr(), cap,
+                      int(pack_sbit), None, None, nnz_t.data_ptr(), ws.data_ptr(),
+                      ws.numel(), status.data_ptr(), st)
+            nnz = int(nnz_t.item())  # host sync (triton_operators.py:50)
+            size = packed_storage_nbytes(nnz, bits) if pack_sbit else nnz
+            vals = tmp[:size].clone()
+            vals_offset = torch.zeros((), device=dev, dtype=torch.int64)
+    else:
+        vals = sparse_data.vals
+        if pack_sbit != bool(sparse_data.pack_sbit):
+            raise ValueError("pack_sbit must match the TensorBuffer's pack_sbit")
+        if not pack_sbit and vals.dtype != stored:
+            raise TypeError(f"TensorBuffer holds {vals.dtype}, values are {stored}")
+        R.require_cuda(vals, "TensorBuffer.vals")
+        cap = vals.numel()
+        vals_offset = torch.empty(1, device=dev, dtype=torch.int64)
+        if T == 0:
+            prefix.zero_()
+            off = sparse_data.offset
+            vals_offset.copy_((off + 7) // 8 * 8 if pack_sbit else off)
+        else:
+            _lib.call("bs_compress", dense.data_ptr(), R.dtype_code(dense.dtype), M, N, ld,
+                      qs, qo, bitmask.data_ptr(), prefix.data_ptr(), vals.data_ptr(), cap,
+                      int(pack_sbit), sparse_data.offset.data_ptr(), vals_offset.data_ptr(),
+                      None, ws.data_ptr(), ws.numel(), status.data_ptr(), st)
+    return BitsparseTensor(vals, bitmask, prefix, dense.shape, stored,
+                           grid_m, grid_n, _BM, _BN, scale=scale,
+                           vals_offset=vals_offset, pack_sbit=pack_sbit)
+
+
+# ---------------------------------------------------------------------------
+# Reconstruction and gradient masks
+# ---------------------------------------------------------------------------
+def _unpack(sparse: BitsparseTensor, output: Tensor, first_m_tile: int, grid_n: int, K: int,
+            batch_rows: int, num_tiles_in_batch: int, relu2: bool) -> Tensor:
+    _check_tiles(sparse.BLOCK_M, sparse.BLOCK_N)
+    R.require_cuda(output, "output")
+    want = torch.bfloat16 if relu2 else sparse.dtype
+    if output.dtype != want:
+        raise TypeError(f"output must be {want}, got {output.dtype}")
+    if output.dim() != 2 or output.stride(1) != 1:
+        raise ValueError("output must be a 2-D tensor with unit column stride")
+    if output.shape[0] < batch_rows or output.shape[1] < K:
+        raise ValueError("output is smaller than [batch_rows, K]")
+    scale = sparse.scale if relu2 else None
+    if scale is not None:
+        scale = scale.to(device=output.device, dtype=torch.float32)
+    _lib.call("bs_unpack", sparse.vals.data_ptr(), sparse.bitmask.data_ptr(),
+              sparse.prefix.data_ptr(), sparse.vals_offset.data_ptr(),
+              R.dtype_code(sparse.dtype), int(sparse.pack_sbit), output.data_ptr(),
+              output.stride(0), first_m_tile, grid_n, K, batch_rows, num_tiles_in_batch,
+              int(relu2), R.ptr(scale), _stream(output))
+    return output
+
+
+def unpack_batch_(
+    sparse: BitsparseTensor, output: Tensor,
+    first_m_tile: int, grid_n: int, K: int, batch_rows: int,
+    num_tiles_in_batch: int,
+) -> Tensor:
+    """Unpack a slice of tiles into a dense [batch_rows, K] slice, in place
+    (triton_operators.py:118-138).  ``output`` has the stored dtype."""
+    return _unpack(sparse, output, first_m_tile, grid_n, K, batch_rows,
+                   num_tiles_in_batch, relu2=False)
+
+
+def unpack_relu2_batch_(
+    sparse: BitsparseTensor, output: Tensor,
+    first_m_tile: int, grid_n: int, K: int, batch_rows: int,
+    num_tiles_in_batch: int,
+) -> Tensor:
+    """Unpack stored r = relu(a) as bf16 k * r^2 (times scale^2 when the
+    tensor has an FP8 scale), in place (triton_operators.py:141-162)."""
+    return _unpack(sparse, output, first_m_tile, grid_n, K, batch_rows,
+                   num_tiles_in_batch, relu2=True)
+
+
+def mask_with_bitmask_(grad: Tensor, sparse: BitsparseTensor) -> Tensor:
+    """grad <- grad * bitmask, in place (triton_operators.py:165-175)."""
+    _check_tiles(sparse.BLOCK_M, sparse.BLOCK_N)
+    R.require_cuda(grad, "grad")
+    M, N = sparse.shape
+    if tuple(grad.shape) != (M, N) or grad.stride(1) != 1:
+        raise ValueError("grad must be [M, N] with unit column stride")
+    _lib.call("bs_mask_with_bitmask", grad.data_ptr(), R.dtype_code(grad.dtype), M, N,
+              grad.stride(0), sparse.bitmask.data_ptr(), _stream(grad))
+    return grad
+
+
+def relu2_grad_sparse_(grad: Tensor, sparse_z: BitsparseTensor) -> Tensor:
+    """grad <- grad * 2 k r under the mask, then * scale, in place
+    (triton_operators.py:178-202)."""
+    _check_tiles(sparse_z.BLOCK_M, sparse_z.BLOCK_N)
+    R.require_cuda(grad, "grad")
+    M, N = sparse_z.shape
+    if tuple(grad.shape) != (M, N) or grad.stride(1) != 1:
+        raise ValueError("grad must be [M, N] with unit column stride")
+    scale = sparse_z.scale
+    if scale is not None:
+        scale = scale.to(device=grad.device, dtype=torch.float32)
+    _lib.call("bs_relu2_grad", grad.data_ptr(), R.dtype_code(grad.dtype), M, N,
+              grad.stride(0), sparse_z.vals.data_ptr(), sparse_z.bitmask.data_ptr(),
+              sparse_z.prefix.data_ptr(), sparse_z.vals_offset.data_ptr(),
+              R.dtype_code(sparse_z.dtype), int(sparse_z.pack_sbit), R.ptr(scale),
+              _stream(grad))
+    return grad

@@ -1,0 +1,84 @@
+"""Dense x BitsparseTensor GEMMs (lib_sparse/src/sparse_matmul.py).
+
+``AspB`` / ``AspRelu2B`` compute ``A @ B`` / ``A @ (k * B^2)`` with B stored
+sparse: B is reconstructed by the CUDA unpack kernel, then multiplied.
+``row_batch > 0`` unpacks tile-aligned row batches and accumulates, trading
+time for peak memory, as in the reference.
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from ..bitsparse import BitsparseTensor
+from ..fp8 import matmul
+from .operators import unpack_batch_, unpack_relu2_batch_
+
+
+def _row_batches(grid_m: int, BLOCK_M: int, N: int, row_batch: int):
+    row_tiles = max(1, row_batch // BLOCK_M)
+    for first_tile in range(0, grid_m, row_tiles):
+        start = first_tile * BLOCK_M
+        end = min(start + row_tiles * BLOCK_M, N)
+        rows = end - start
+        yield first_tile, start, end, rows, (rows + BLOCK_M - 1) // BLOCK_M
+
+
+def AspB(A: Tensor, B_sparse: BitsparseTensor, A_scale: Tensor | None = None,
+         row_batch: int = 0) -> Tensor:
+    """A[M, N] @ sparse B[N, K] -> [M, K] (lib_sparse/src/sparse_matmul.py:9-47)."""
+    BLOCK_M = B_sparse.BLOCK_M
+    grid_m, grid_n = B_sparse.grid_m, B_sparse.grid_n
+    N, K = B_sparse.shape
+    M = A.shape[0]
+    if row_batch <= 0:
+        dense = torch.empty(N, K, device=A.device, dtype=B_sparse.dtype)
+        unpack_batch_(B_sparse, dense, 0, grid_n, K, N, grid_m * grid_n)
+        return matmul(A, dense, B_sparse.fp8, a_scale=A_scale, b_scale=B_sparse.scale)
+    out = torch.zeros(M, K, device=A.device, dtype=A.dtype)
+    for first, start, end, rows, nrt in _row_batches(grid_m, BLOCK_M, N, row_batch):
+        dense_batch = torch.empty(rows, K, device=A.device, dtype=B_sparse.dtype)
+        unpack_batch_(B_sparse, dense_batch, first, grid_n, K, rows, nrt * grid_n)
+        out.addmm_(A[:, start:end], dense_batch)
+    return out
+
+
+def spAB(A_sparse: BitsparseTensor, B: Tensor, out: Tensor | None = None,
+         row_batch: int = 0) -> Tensor:
+    """sparse A[M, N] @ B[N, K] -> [M, K] (lib_sparse/src/sparse_matmul.py:50-88)."""
+    BLOCK_M = A_sparse.BLOCK_M
+    grid_m, grid_n = A_sparse.grid_m, A_sparse.grid_n
+    M, N = A_sparse.shape
+    K = B.shape[1]
+    if row_batch <= 0:
+        dense = torch.empty(M, N, device=B.device, dtype=A_sparse.dtype)
+        unpack_batch_(A_sparse, dense, 0, grid_n, N, M, grid_m * grid_n)
+        return matmul(dense, B, A_sparse.fp8, a_scale=A_sparse.scale)
+    out = torch.zeros(M, K, device=B.device, dtype=B.dtype) if out is None else out
+    for first, start, end, rows, nrt in _row_batches(grid_m, BLOCK_M, M, row_batch):
+        dense_batch = torch.empty(rows, N, device=B.device, dtype=A_sparse.dtype)
+        unpack_batch_(A_sparse, dense_batch, first, grid_n, N, rows, nrt * grid_n)
+        torch.mm(dense_batch, B, out=out[start:end])
+    return out
+
+
+def AspRelu2B(A: Tensor, B_sparse: BitsparseTensor, A_scale: Tensor | None = None,
+              row_batch: int = 0) -> Tensor:
+    """A @ (k * B^2) with sparse B = relu(preact) (lib_sparse/src/sparse_matmul.py:91-132).
+
+    The squared reconstruction is bf16 (squaring overflows FP8 storage); in
+    FP8 mode it is re-quantised by the FP8 matmul."""
+    BLOCK_M = B_sparse.BLOCK_M
+    grid_m, grid_n = B_sparse.grid_m, B_sparse.grid_n
+    N, K = B_sparse.shape
+    M = A.shape[0]
+    if row_batch <= 0:
+        dense = torch.empty(N, K, device=A.device, dtype=torch.bfloat16)
+        unpack_relu2_batch_(B_sparse, dense, 0, grid_n, K, N, grid_m * grid_n)
+        return matmul(A, dense, B_sparse.fp8, a_scale=A_scale)
+    out = torch.zeros(M, K, device=A.device, dtype=A.dtype)
+    for first, start, end, rows, nrt in _row_batches(grid_m, BLOCK_M, N, row_batch):
+        dense_batch = torch.empty(rows, K, device=A.device, dtype=torch.bfloat16)
+        unpack_relu2_batch_(B_sparse, dense_batch, first, grid_n, K, rows, nrt * grid_n)
+        out.addmm_(A[:, start:end], dense_batch)
+    return out

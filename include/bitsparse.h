@@ -1,0 +1,188 @@
+/*
+ * bitsparse.h -- C ABI of the B200 (sm_100a) BitSparse activation-compression
+ * library (libbitsparse_b200.so).
+ *
+ * The format is the reference's tile-wise bitmask format (Maxzhu123/bitsparse,
+ * lib_sparse/src/triton_kernels.py:1-17): a dense row-major [M, N] matrix is
+ * cut into 64x64 tiles in grid-row-major order; each tile has a 512-byte
+ * bitmask (bit j of byte b <=> tile element 8b+j, row-major in the tile, set
+ * iff the element is > 0); `prefix` is uint32[T+1] with prefix[0] = 0 and
+ * prefix[t+1] = prefix[t] + popcount(tile t); `vals` holds the positive
+ * elements in (tile, row, column) order starting at logical index
+ * `vals_offset`, either raw (bf16 / fp8 bytes) or as a continuous 15-bit
+ * (bf16) / 7-bit (fp8) sign-dropped bitstream (lib_sparse/src/bitpacking.py).
+ *
+ * Conventions of every entry point:
+ *  - all pointers are DEVICE pointers on the current CUDA device, except
+ *    where stated; nothing is allocated and nothing is freed;
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default);
+ *    all work is stream ordered and asynchronous, there is no host sync;
+ *  - the return value is BS_OK or a BS_ERR_* code for argument errors
+ *    found on the host; errors found on the device (capacity overflow, a
+ *    bounded wait that gave up) are OR-ed into the optional `status` word
+ *    (device int32*), which the caller reads when it chooses to.
+ * Each declaration names the reference interface it replaces (file:line in
+ * Maxzhu123/bitsparse).
+ */
+#ifndef BITSPARSE_B200_H
+#define BITSPARSE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+enum {
+  BS_OK = 0,
+  BS_ERR_SHAPE = 1,     /* negative / too large sizes, bad batch slice      */
+  BS_ERR_DTYPE = 2,     /* unsupported dtype or dtype combination           */
+  BS_ERR_ALIGN = 3,     /* a pointer that must be aligned is not            */
+  BS_ERR_CAPACITY = 4,  /* host-detectable capacity problem                 */
+  BS_ERR_LAUNCH = 5,    /* a CUDA launch failed (cudaGetLastError)          */
+  BS_ERR_ARG = 6,       /* NULL where a pointer is required, bad flag       */
+  BS_ERR_WORKSPACE = 7  /* workspace too small                              */
+};
+
+/* Device status bits (OR-ed into *status by kernels). */
+enum {
+  BS_STATUS_CAPACITY = 1, /* vals storage too small: writes were clipped    */
+  BS_STATUS_TIMEOUT = 2   /* a bounded inter-CTA wait gave up               */
+};
+
+/* Element types.  Codes 1/2 equal the reference's pack codecs
+ * (lib_sparse/bitsparse.py:8-18). */
+enum {
+  BS_BF16 = 0,
+  BS_E4M3 = 1, /* float8_e4m3fn */
+  BS_E5M2 = 2, /* float8_e5m2   */
+  BS_F32 = 3
+};
+
+/* Tile geometry (lib_sparse/config.py:5-6, lib_sparse/bitsparse.py:120-127). */
+#define BS_BLOCK_M 64
+#define BS_BLOCK_N 64
+#define BS_TILE_NUMEL 4096
+#define BS_TILE_BYTES 512
+
+/* Library version string, e.g. "bitsparse_b200 0.1 sm_100a". Host pointer. */
+const char *bs_version(void);
+
+/* Bytes of scan workspace bs_compress needs for `num_tiles` tiles.  The
+ * workspace must be zero-filled once when it is first allocated; after that
+ * every launch leaves it ready for the next one.  Launches that may overlap
+ * on the GPU (different streams) must use different workspaces. */
+size_t bs_compress_workspace_bytes(int64_t num_tiles);
+
+/* Fused compress: dense [M, N] (row stride `ld` elements) -> bitmask
+ * uint8[T*512], prefix uint32[T+1] and the compacted values, in ONE pass
+ * over the dense input with a single-pass device-wide scan.
+ *
+ * Replaces the whole of dense_to_tilesparse (lib_sparse/src/functions.py:55-99):
+ * tile_pack (lib_sparse/src/triton_operators.py:21-33), the torch.cumsum
+ * prefix (lib_sparse/src/functions.py:33-40), compact_vals
+ * (lib_sparse/src/triton_operators.py:36-115, raw and pack_sbit paths) and
+ * the TensorBuffer offset update (lib_sparse/src/functions.py:73-92).
+ *
+ *  in_dtype     BS_BF16, BS_E4M3, BS_E5M2 (stored as-is) or, with
+ *               `quant_scale` != NULL, BS_BF16 / BS_F32 quantised in the
+ *               kernel to e4m3fn as to_fp8 does (lib_sparse/fp8.py:123-129):
+ *               q = e4m3(x / scale) (bf16 input: x / scale rounded to bf16
+ *               first); the bitmask is taken from q (q > 0).
+ *  quant_scale  device float* (fp32 scale) or NULL.
+ *  quant_out    with quant_scale: optional device uint8* [M, N] (row stride
+ *               N) receiving the dense e4m3 tensor, or NULL.
+ *  vals         raw: element storage (bf16 or 1-byte fp8); pack_sbit:
+ *               byte stream addressed as 32-bit words (4-byte aligned).
+ *  vals_capacity  raw: elements; pack_sbit: bytes.
+ *  arena_offset NULL for standalone storage (values start at 0; in
+ *               pack_sbit mode the bytes after the payload up to
+ *               vals_capacity are zeroed) or a device int64* holding the
+ *               TensorBuffer's running offset: values start at
+ *               off = *arena_offset (rounded up to a multiple of 8 when
+ *               pack_sbit) and *arena_offset becomes off + nnz.
+ *  vals_offset_out optional device int64*: receives `off`.
+ *  nnz_out      optional device int64*: receives the total nonzero count.
+ */
+int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N,
+                int64_t ld, const float *quant_scale, uint8_t *quant_out,
+                uint8_t *bitmask, uint32_t *prefix, void *vals,
+                int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
+                int64_t *vals_offset_out, int64_t *nnz_out, void *workspace,
+                size_t workspace_bytes, int32_t *status, void *stream);
+
+/* Per-tile bitmask and nonzero counts only (no values): the reference's
+ * tile_pack (lib_sparse/src/triton_operators.py:21-33,
+ * lib_sparse/src/triton_kernels.py:63-97).  counts is int32[T]. */
+int bs_tile_pack(const void *dense, int dtype, int64_t M, int64_t N,
+                 int64_t ld, int32_t *counts, uint8_t *bitmask, void *stream);
+
+/* Reconstruct a batch of tiles into a dense [batch_rows, K] slice.
+ * Replaces unpack_batch_ (lib_sparse/src/triton_operators.py:118-138) and,
+ * with relu2 = 1, unpack_relu2_batch_ (:141-162).
+ *
+ *  store_dtype  BS_BF16 / BS_E4M3 / BS_E5M2 (the BitsparseTensor dtype).
+ *  out          relu2 = 0: elements of store_dtype; relu2 = 1: bf16.
+ *  out_ld       row stride of `out` in elements.
+ *  vals_offset  device int64* (the BitsparseTensor's vals_offset).
+ *  scale        relu2 = 1 only: optional device float*; the output is then
+ *               multiplied by scale^2 exactly as the reference's separate
+ *               `output.mul_(scale.square())` does (fused here).
+ *  Tile pid of the batch is tile (first_m_tile + pid / grid_n) * grid_n +
+ *  pid % grid_n; its elements go to rows (pid / grid_n) * 64 + r < batch_rows
+ *  and columns (pid % grid_n) * 64 + c < K of `out`.
+ */
+int bs_unpack(const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
+              const int64_t *vals_offset, int store_dtype, int pack_sbit,
+              void *out, int64_t out_ld, int64_t first_m_tile, int64_t grid_n,
+              int64_t K, int64_t batch_rows, int64_t num_tiles_in_batch,
+              int relu2, const float *scale, void *stream);
+
+/* In place grad <- bit ? grad : 0 for a bf16 [M, N] gradient (row stride
+ * ld).  Replaces mask_with_bitmask_ (lib_sparse/src/triton_operators.py:165-175,
+ * lib_sparse/src/triton_kernels.py:249-276). */
+int bs_mask_with_bitmask(void *grad, int grad_dtype, int64_t M, int64_t N,
+                         int64_t ld, const uint8_t *bitmask, void *stream);
+
+/* In place grad <- bit ? grad * (2 * k * r) : 0, r gathered from the stored
+ * values, then (scale != NULL) grad *= scale.  Replaces relu2_grad_sparse_
+ * (lib_sparse/src/triton_operators.py:178-202,
+ * lib_sparse/src/triton_kernels.py:288-330). */
+int bs_relu2_grad(void *grad, int grad_dtype, int64_t M, int64_t N, int64_t ld,
+                  const void *vals, const uint8_t *bitmask,
+                  const uint32_t *prefix, const int64_t *vals_offset,
+                  int store_dtype, int pack_sbit, const float *scale,
+                  void *stream);
+
+/* Per-tensor fp8 scale of to_fp8 (lib_sparse/fp8.py:123-129):
+ * *scale_out = max(amax(|x|) / 448, 1e-9), with the amax / 448 rounded to
+ * bf16 for bf16 input (eager PyTorch semantics).  `amax_ws` is a device
+ * uint32 the caller zero-fills before the call (one word of scratch). */
+int bs_fp8_scale(const void *x, int dtype, int64_t numel, uint32_t *amax_ws,
+                 float *scale_out, void *stream);
+
+/* q = e4m3fn(x / *scale) elementwise over `numel` elements of a bf16 or
+ * fp32 tensor (bf16: the quotient is rounded to bf16 first) -- the quantise
+ * step of to_fp8 (lib_sparse/fp8.py:127).  x 16-byte aligned, q 8-byte
+ * aligned. */
+int bs_quantize_e4m3(const void *x, int dtype, int64_t numel, const float *scale,
+                     uint8_t *q, void *stream);
+
+/* Values only, with tile offsets from an existing prefix: the reference's
+ * compact_vals (lib_sparse/src/triton_operators.py:36-115,
+ * lib_sparse/src/triton_kernels.py:105-146, lib_sparse/src/bitpacking.py:58-117).
+ * The bitmask is recomputed from `dense` (it is a function of it).
+ * vals_offset: device int64* logical start of the values (NULL = 0).
+ * vals_capacity: elements (raw) or bytes (pack_sbit). */
+int bs_compact_vals(const void *dense, int dtype, int64_t M, int64_t N, int64_t ld,
+                    const uint32_t *prefix, void *vals, int64_t vals_capacity,
+                    int pack_sbit, const int64_t *vals_offset, int32_t *status,
+                    void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BITSPARSE_B200_H */

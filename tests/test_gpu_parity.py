@@ -1,0 +1,267 @@
+"""GPU parity: the CUDA path against the reference's golden outputs and the
+pinned CPU oracle, bit for bit.
+
+Every case goes through the public operators, which call the C ABI of
+libbitsparse_b200.so.  In-kernel fp32 -> bf16 casts (ReLU^2 reconstruct /
+gradient) are compared with the oracle's round-to-nearest-even mode, which
+is what the reference's Triton kernels do on a GPU; the golden fixtures of
+those two fields come from the Triton CPU interpreter, which truncates (the
+oracle reproduces them in its "trunc" mode, tests/test_oracle.py).
+"""
+import numpy as np
+import pytest
+import torch
+
+import bitsparse_b200 as B
+from bitsparse_b200 import TensorBuffer, bits_per_value
+from bitsparse_b200.fp8 import to_fp8
+from bitsparse_b200.src.functions import (_prepare_tiles, dense_to_tilesparse,
+                                          relu_to_tilesparse_fp8)
+from bitsparse_b200.src.operators import (compact_vals, mask_with_bitmask_,
+                                          relu2_grad_sparse_, unpack_batch_,
+                                          unpack_relu2_batch_)
+from oracle import bitsparse_oracle as O
+from tests.conftest import golden_cases, parse_case
+from tests.golden.fixtures import arena_inputs, case_inputs, check, digest, has
+from tests.golden.make_golden import SHAPES_FULL, SPARSITIES
+from tests.gpu_util import TORCH_DT, bits, oracle_sparse, payload, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _reconstruct(sp, relu2=False):
+    M, N = sp.shape
+    if relu2:
+        out = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+        return unpack_relu2_batch_(sp, out, 0, sp.grid_n, N, M, sp.grid_m * sp.grid_n)
+    out = torch.empty((M, N), device="cuda", dtype=sp.dtype)
+    return unpack_batch_(sp, out, 0, sp.grid_n, N, M, sp.grid_m * sp.grid_n)
+
+
+@pytest.fixture(scope="module")
+def cases(golden):
+    return sorted(golden_cases(golden, "v/").items())
+
+
+def test_golden_round_trip(cases):
+    """All 78 reference cases: bitmask, prefix, vals, reconstruct, masks."""
+    for case, f in cases:
+        dtype, pack, (M, N), sp_ = parse_case(case)
+        dense_b, grad_b = case_inputs(f, dtype, (M, N), sp_)
+        dense = to_dev(dense_b, dtype, (M, N))
+        sp = dense_to_tilesparse(dense, None, None, pack)
+        check(f, "bitmask", bits(sp.bitmask), case)
+        check(f, "prefix", bits(sp.prefix), case)
+        nnz = int(sp.prefix[-1].item())
+        if pack:
+            v = bits(sp.vals)
+            assert v.size == O.packed_storage_nbytes(nnz, bits_per_value(sp.dtype)), case
+            check(f, "vals", payload(v, 0, nnz, bits_per_value(sp.dtype)), case)
+            # our stream is zero outside the payload (the reference leaves garbage)
+            np.testing.assert_array_equal(v, payload(v, 0, nnz, bits_per_value(sp.dtype)))
+        else:
+            check(f, "vals", bits(sp.vals), case)
+        check(f, "recon", bits(_reconstruct(sp)), case)
+        osp = O.dense_to_tilesparse(dense_b, dtype, None, pack)
+        np.testing.assert_array_equal(bits(_reconstruct(sp, relu2=True)),
+                                      O.reconstruct_relu2(osp, "rne"), err_msg=case)
+        g = to_dev(grad_b, O.DT_BF16, (M, N))
+        check(f, "mask_grad", bits(mask_with_bitmask_(g.clone(), sp)), case)
+        np.testing.assert_array_equal(bits(relu2_grad_sparse_(g.clone(), sp)),
+                                      O.relu2_grad_sparse(grad_b.copy(), osp, "rne"),
+                                      err_msg=case)
+    B.check_status()
+
+
+def test_golden_shared_arena(golden):
+    """Eight tensors in one TensorBuffer (experiments/validate.py:128-139)."""
+    for dtype in (O.DT_BF16, O.DT_E4M3, O.DT_E5M2):
+        for pack in (0, 1):
+            k = f"a/{dtype}/{pack}/"
+            buf = TensorBuffer(int(golden[k + "size"]), device="cuda", dtype=TORCH_DT[dtype],
+                               pack_sbit=bool(pack))
+            dense = [to_dev(d, dtype) for d in
+                     arena_inputs(golden, k, dtype, SHAPES_FULL, SPARSITIES)]
+            sps = [dense_to_tilesparse(d, None, buf, bool(pack)) for d in dense]
+            offs = [int(s.vals_offset.item()) for s in sps]
+            np.testing.assert_array_equal(offs, golden[k + "vals_offsets"])
+            assert int(buf.offset.item()) == int(golden[k + "final_offset"])
+            sub = {kk[len(k):]: v for kk, v in golden.items() if kk.startswith(k)}
+            check(sub, "arena", bits(buf.vals), k)
+            for d, s in zip(dense, sps):  # decompress after all writes
+                assert s.vals is buf.vals
+                np.testing.assert_array_equal(bits(_reconstruct(s)), bits(d))
+    B.check_status()
+
+
+def test_config1_fp8_and_bf16(golden):
+    """x ~ N(0,1) [1024, 3072] fp32 seed 0, to_fp8(relu(x))."""
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1024, 3072, generator=g, dtype=torch.float32)
+    assert digest(x.numpy()) == str(golden["c1/x_sha"])
+    h = torch.relu(x).cuda()
+    q, scale = to_fp8(h)
+    assert scale.item() == float(golden["c1/scale"])
+    assert digest(bits(q)) == str(golden["c1/q_sha"])
+    for name, dense in (("fp8", q), ("bf16", h.to(torch.bfloat16))):
+        for pack in (0, 1):
+            k = f"c1/{name}/{pack}/"
+            sp = dense_to_tilesparse(dense, scale if name == "fp8" else None, None, bool(pack))
+            nnz = int(sp.prefix[-1].item())
+            assert nnz == int(golden[k + "nnz"])
+            assert digest(bits(sp.bitmask)) == str(golden[k + "bitmask_sha"])
+            assert digest(bits(sp.prefix)) == str(golden[k + "prefix_sha"])
+            v = bits(sp.vals)
+            if pack:
+                v = payload(v, 0, nnz, bits_per_value(sp.dtype))
+            assert digest(v) == str(golden[k + "vals_sha"]), k
+            assert digest(bits(_reconstruct(sp))) == str(golden[k + "recon_sha"])
+
+
+def test_fused_quantise_matches_to_fp8_then_compress():
+    """relu_to_tilesparse_fp8 (one amax pass + one fused pass) equals the
+    reference's to_fp8 then dense_to_tilesparse, bit for bit (oracle)."""
+    g = torch.Generator().manual_seed(11)
+    for (M, N) in ((1024, 3072), (129, 131), (64, 64), (1, 8)):
+        z = (torch.randn(M, N, generator=g) * 2.5).to(torch.bfloat16)
+        h = torch.relu(z).cuda()
+        for pack in (False, True):
+            h_fp8, sp = relu_to_tilesparse_fp8(h.clone(), None, pack)
+            q_o, s_o = O.to_fp8(bits(h), "bfloat16")
+            assert sp.scale.item() == s_o
+            np.testing.assert_array_equal(bits(h_fp8).reshape(-1), q_o.reshape(-1))
+            osp = O.dense_to_tilesparse(q_o.reshape(M, N), O.DT_E4M3, None, pack)
+            np.testing.assert_array_equal(bits(sp.bitmask), osp.bitmask)
+            np.testing.assert_array_equal(bits(sp.prefix), osp.prefix)
+            nv = bits(sp.vals)
+            if pack:
+                np.testing.assert_array_equal(nv, osp.vals)
+            else:
+                np.testing.assert_array_equal(nv, osp.vals)
+            # ReLU^2 reconstruct with the scale fused (output *= scale^2)
+            r2 = bits(_reconstruct(sp, relu2=True))
+            osp.scale = s_o
+            np.testing.assert_array_equal(r2, O.reconstruct_relu2(osp, "rne"))
+            gr = torch.randn(M, N, generator=g).to(torch.bfloat16)
+            np.testing.assert_array_equal(
+                bits(relu2_grad_sparse_(gr.cuda(), sp)),
+                O.relu2_grad_sparse(bits(gr).copy(), osp, "rne"))
+
+
+def test_scalar_mul_semantics_match_torch_cuda():
+    """The oracle's ``bf16_tensor.mul_(fp32 0-dim)`` rule is torch CUDA's."""
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(4096, generator=g).to(torch.bfloat16).cuda()
+    for s in (0.0123456789, 3.3e-3, 1.7, 448.1):
+        st = torch.tensor(s, dtype=torch.float32, device="cuda")
+        ref = bits(x.clone().mul_(st))
+        np.testing.assert_array_equal(O._mul_bf16_by_scalar(bits(x), np.float32(s)), ref)
+        ref2 = bits(x.clone().mul_(st.square()))
+        np.testing.assert_array_equal(
+            O._mul_bf16_by_scalar(bits(x), np.float32(s) * np.float32(s)), ref2)
+
+
+def test_two_step_api(cases):
+    """_prepare_tiles + compact_vals (the reference's unfused API)."""
+    for case, f in cases[::3]:
+        dtype, pack, (M, N), sp_ = parse_case(case)
+        dense_b, _ = case_inputs(f, dtype, (M, N), sp_)
+        dense = to_dev(dense_b, dtype, (M, N))
+        pt = _prepare_tiles(dense)
+        check(f, "bitmask", bits(pt.bitmasks), case)
+        check(f, "prefix", bits(pt.prefix), case)
+        vals, off = compact_vals(dense, pt.bitmasks, pt.prefix, None, None, M, N, pt.grid_n,
+                                 pt.num_tiles, 64, 64, 4096, pack)
+        nnz = int(pt.prefix[-1].item())
+        v = bits(vals)
+        if pack:
+            v = payload(v, 0, nnz, bits_per_value(dense.dtype))
+        check(f, "vals", v, case)
+
+
+def test_unpack_row_batches():
+    """unpack_batch_ over tile-row batches, incl. a ragged last batch."""
+    g = torch.Generator().manual_seed(2)
+    M, N = 333, 200
+    d = torch.randn(M, N, generator=g).relu().to(torch.bfloat16).cuda()
+    for pack in (False, True):
+        sp = dense_to_tilesparse(d, None, None, pack)
+        for first, rows in ((0, 64), (1, 128), (4, M - 256), (5, M - 320)):
+            out = torch.zeros(rows, N, dtype=torch.bfloat16, device="cuda")
+            nrt = (rows + 63) // 64
+            unpack_batch_(sp, out, first, sp.grid_n, N, rows, nrt * sp.grid_n)
+            torch.testing.assert_close(out, d[first * 64: first * 64 + rows], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float8_e4m3fn, torch.float8_e5m2])
+def test_edge_values_and_shapes(dtype):
+    """Empty, 1x1, single row/column, all-zero, all-positive, special values."""
+    specials = torch.tensor([0.0, -0.0, float("inf"), float("-inf"), float("nan"), 1e-30,
+                             -1e-30, 3.0], dtype=torch.float32)
+    for (M, N) in ((0, 5), (5, 0), (1, 1), (1, 1000), (1000, 1), (64, 65), (65, 64)):
+        for fill in ("zero", "pos", "special", "rand"):
+            if fill == "zero":
+                x = torch.zeros(M, N)
+            elif fill == "pos":
+                x = torch.ones(M, N)
+            elif fill == "special":
+                x = specials[torch.arange(M * N) % specials.numel()].reshape(M, N)
+            else:
+                x = torch.randn(M, N, generator=torch.Generator().manual_seed(M + N))
+            xd = x.to(dtype)
+            xb = bits(xd)
+            odt = {torch.bfloat16: O.DT_BF16, torch.float8_e4m3fn: O.DT_E4M3,
+                   torch.float8_e5m2: O.DT_E5M2}[dtype]
+            for pack in (False, True):
+                sp = dense_to_tilesparse(xd.cuda(), None, None, pack)
+                osp = O.dense_to_tilesparse(xb.reshape(M, N), odt, None, pack)
+                np.testing.assert_array_equal(bits(sp.bitmask), osp.bitmask)
+                np.testing.assert_array_equal(bits(sp.prefix), osp.prefix)
+                np.testing.assert_array_equal(bits(sp.vals), osp.vals)
+                if M * N:
+                    np.testing.assert_array_equal(bits(_reconstruct(sp)).reshape(-1),
+                                                  O.reconstruct(osp).reshape(-1))
+    B.check_status()
+
+
+def test_strided_input_rows():
+    """A row-strided view (ld > N) compresses like its contiguous copy."""
+    g = torch.Generator().manual_seed(3)
+    big = torch.randn(300, 512, generator=g).to(torch.bfloat16).cuda()
+    for view in (big[:, :200], big[:, 8:264], big[:, 3:131]):
+        a = dense_to_tilesparse(view, None)
+        b = dense_to_tilesparse(view.contiguous(), None)
+        assert torch.equal(a.bitmask, b.bitmask) and torch.equal(a.prefix, b.prefix)
+        assert torch.equal(a.vals, b.vals)
+
+
+def test_capacity_overflow_is_reported():
+    """An undersized TensorBuffer: writes are clipped and the status says so."""
+    d = torch.ones(256, 256, dtype=torch.bfloat16, device="cuda")
+    buf = TensorBuffer(1000 * 2, device="cuda", dtype=torch.bfloat16)
+    dense_to_tilesparse(d, None, buf)
+    with pytest.raises(RuntimeError, match="too small"):
+        B.check_status()
+    assert torch.count_nonzero(buf.vals).item() == 1000  # clipped, nothing beyond
+    B.check_status()  # cleared
+
+
+def test_workspace_reuse_many_launches():
+    """The self-resetting scan workspace across many launches of varying size."""
+    g = torch.Generator().manual_seed(9)
+    sizes = [(64, 64), (4096, 4096), (1, 1), (2000, 3000), (128, 64 * 300), (7, 9)] * 4
+    for (M, N) in sizes:
+        d = torch.randn(M, N, generator=g).relu().to(torch.bfloat16).cuda()
+        sp = dense_to_tilesparse(d, None)
+        assert int(sp.prefix[-1].item()) == int((d > 0).sum().item())
+        torch.testing.assert_close(_reconstruct(sp), d, rtol=0, atol=0)
+    B.check_status()
+
+
+def test_deterministic():
+    d = torch.randn(3000, 4000, generator=torch.Generator().manual_seed(4)).relu()
+    d = d.to(torch.bfloat16).cuda()
+    for pack in (False, True):
+        a = dense_to_tilesparse(d, None, None, pack)
+        b = dense_to_tilesparse(d, None, None, pack)
+        assert torch.equal(a.vals, b.vals) and torch.equal(a.prefix, b.prefix)
