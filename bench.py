@@ -430,6 +430,28 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def profile_case():
+    """Small case for ncu captures: compress + reconstruct of one [8192, 8192]
+    bf16 relu(N(0,1)) tensor (134 MB, above L2) into a TensorBuffer, 3 times."""
+    import torch
+    from bitsparse_b200 import TensorBuffer
+    from bitsparse_b200.src.functions import dense_to_tilesparse
+    from bitsparse_b200.src.operators import unpack_batch_
+
+    M = N = 8192
+    x = make_relu_bf16(M, N, 0.0, 0, torch.device("cuda", 0))
+    buf = TensorBuffer(M * N * 2, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(x)
+    for _ in range(3):
+        buf.offset.zero_()
+        sp = dense_to_tilesparse(x, None, buf)
+        unpack_batch_(sp, out, 0, sp.grid_n, N, M, sp.grid_m * sp.grid_n)
+    torch.cuda.synchronize()
+    if not torch.equal(out, x):
+        raise RuntimeError("round trip mismatch")
+    print("profile case ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -438,7 +460,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the sweep, MLP and CPU-baseline extras")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="run only the small ncu capture case and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case()
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

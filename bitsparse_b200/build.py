@@ -52,6 +52,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
               "--expt-relaxed-constexpr", "-I", str(ROOT / "include")]
     if verbose:
         common += ["-Xptxas", "-v"]
+    common += os.environ.get("BS_NVCC_EXTRA", "").split()
     for src in sources():
         obj = build_dir / (src.stem + ".o")
         cmd = common + ["-c", str(src), "-o", str(obj)]

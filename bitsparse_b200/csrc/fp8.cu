@@ -1,0 +1,156 @@
+// to_fp8 on the GPU: per-tensor amax -> scale, and the e4m3 quantiser
+// (lib_sparse/fp8.py:123-129).  Both follow eager PyTorch's arithmetic for a
+// bf16 / fp32 tensor: scale = max(amax / 448, 1e-9) with the quotient
+// rounded to the input dtype, q = e4m3(x / scale) with the quotient rounded
+// to the input dtype first.
+#include "common.cuh"
+
+namespace bs {
+
+// ---------------------------------------------------------------------------
+// to_fp8 scale: amax(|x|) -> scale (lib_sparse/fp8.py:123-129)
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(kThreads)
+amax_kernel(const uint8_t *x, int64_t n, uint32_t *amax_ws) {
+  constexpr int EB = Elt<DT>::bytes;
+  const int64_t nvec = (n * EB) / 16;
+  float m = 0.f;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nvec; i += stride) {
+    const uint4 v = ld_nc_v4(x + 16 * i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if constexpr (DT == BS_BF16) {
+        m = fmaxf(m, fabsf(bf16_bits_to_f32(w[q] & 0xFFFFu)));
+        m = fmaxf(m, fabsf(bf16_bits_to_f32(w[q] >> 16)));
+      } else {
+        m = fmaxf(m, fabsf(__uint_as_float(w[q])));
+      }
+    }
+  }
+  // scalar tail
+  for (int64_t e = nvec * (16 / EB) + (int64_t)blockIdx.x * kThreads + threadIdx.x; e < n;
+       e += stride) {
+    if constexpr (DT == BS_BF16)
+      m = fmaxf(m, fabsf(bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(x)[e])));
+    else
+      m = fmaxf(m, fabsf(reinterpret_cast<const float *>(x)[e]));
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, d));
+  __shared__ float s_m[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) s_m[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.f;
+    for (int i = 0; i < kThreads / 32; ++i) b = fmaxf(b, s_m[i]);
+    atomicMax(amax_ws, __float_as_uint(b));  // non-negative floats order as uints
+  }
+}
+
+// Finalise the scale and reset the scratch word for the next call.
+template <int DT>
+__global__ void scale_kernel(uint32_t *amax_ws, float *scale_out) {
+  const float amax = __uint_as_float(*amax_ws);
+  float s = __fdiv_rn(amax, 448.0f);
+  if constexpr (DT == BS_BF16) s = bf16_bits_to_f32(f32_to_bf16_bits(s));
+  *scale_out = fmaxf(s, 1e-9f);  // clamp(min=1e-9)
+  *amax_ws = 0u;
+}
+
+// q = e4m3(x / scale) over a flat tensor (the quantise half of to_fp8).
+template <int DT>
+__global__ void __launch_bounds__(kThreads)
+quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q) {
+  const float s = *scale;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i * 8 < n; i += stride) {
+    uint32_t o[2] = {0, 0};
+    const int64_t e0 = i * 8;
+    const bool full = e0 + 8 <= n;
+    uint32_t b[8];
+    if constexpr (DT == BS_BF16) {
+      if (full) {
+        const uint4 v = ld_nc_v4(x + e0 * 2);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) b[e] = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+      } else {
+        for (int e = 0; e < 8; ++e)
+          b[e] = e0 + e < n ? reinterpret_cast<const uint16_t *>(x)[e0 + e] : 0u;
+      }
+    } else {
+      if (full) {
+        const uint4 v0 = ld_nc_v4(x + e0 * 4), v1 = ld_nc_v4(x + e0 * 4 + 16);
+        b[0] = v0.x; b[1] = v0.y; b[2] = v0.z; b[3] = v0.w;
+        b[4] = v1.x; b[5] = v1.y; b[6] = v1.z; b[7] = v1.w;
+      } else {
+        for (int e = 0; e < 8; ++e)
+          b[e] = e0 + e < n ? reinterpret_cast<const uint32_t *>(x)[e0 + e] : 0u;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float xv = DT == BS_BF16 ? bf16_bits_to_f32(b[e]) : __uint_as_float(b[e]);
+      float y = __fdiv_rn(xv, s);
+      if constexpr (DT == BS_BF16) y = bf16_bits_to_f32(f32_to_bf16_bits(y));
+      o[e >> 2] |= f32_to_e4m3_bits(y) << (8 * (e & 3));
+    }
+    if (full) {
+      *reinterpret_cast<uint2 *>(q + e0) = make_uint2(o[0], o[1]);
+    } else {
+      for (int e = 0; e < 8 && e0 + e < n; ++e) q[e0 + e] = (o[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+    }
+  }
+}
+
+}  // namespace bs
+
+using namespace bs;
+
+namespace {
+int launch_err() { return cudaGetLastError() == cudaSuccess ? BS_OK : BS_ERR_LAUNCH; }
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+}  // namespace
+
+extern "C" int bs_fp8_scale(const void *x, int dtype, int64_t numel, uint32_t *amax_ws,
+                            float *scale_out, void *stream) {
+  if (dtype != BS_BF16 && dtype != BS_F32) return BS_ERR_DTYPE;
+  if (numel < 0) return BS_ERR_SHAPE;
+  if (!amax_ws || !scale_out || (numel > 0 && !x)) return BS_ERR_ARG;
+  if (!aligned16(x)) return BS_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int eb = dtype == BS_BF16 ? 2 : 4;
+  int64_t blocks = (numel * eb / 16 + kThreads - 1) / kThreads;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  const uint8_t *xb = static_cast<const uint8_t *>(x);
+  if (dtype == BS_BF16) {
+    amax_kernel<BS_BF16><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, amax_ws);
+    scale_kernel<BS_BF16><<<1, 1, 0, st>>>(amax_ws, scale_out);
+  } else {
+    amax_kernel<BS_F32><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, amax_ws);
+    scale_kernel<BS_F32><<<1, 1, 0, st>>>(amax_ws, scale_out);
+  }
+  return launch_err();
+}
+
+extern "C" int bs_quantize_e4m3(const void *x, int dtype, int64_t numel, const float *scale,
+                                uint8_t *q, void *stream) {
+  if (dtype != BS_BF16 && dtype != BS_F32) return BS_ERR_DTYPE;
+  if (numel < 0) return BS_ERR_SHAPE;
+  if (numel == 0) return BS_OK;
+  if (!x || !scale || !q) return BS_ERR_ARG;
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7)) return BS_ERR_ALIGN;
+  int64_t blocks = ((numel + 7) / 8 + kThreads - 1) / kThreads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t *xb = static_cast<const uint8_t *>(x);
+  if (dtype == BS_BF16) quant_kernel<BS_BF16><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, scale, q);
+  else quant_kernel<BS_F32><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, scale, q);
+  return launch_err();
+}
+
+extern "C" const char *bs_version(void) { return "bitsparse_b200 0.1 sm_100a"; }
