@@ -12,7 +12,7 @@ from pathlib import Path
 _LIB_PATH = Path(__file__).resolve().parent / "libbitsparse_b200.so"
 
 BS_OK, BS_ERR_SHAPE, BS_ERR_DTYPE, BS_ERR_ALIGN, BS_ERR_CAPACITY = 0, 1, 2, 3, 4
-BS_ERR_LAUNCH, BS_ERR_ARG, BS_ERR_WORKSPACE = 5, 6, 7
+BS_ERR_LAUNCH, BS_ERR_ARG, BS_ERR_WORKSPACE, BS_ERR_TOO_LARGE = 5, 6, 7, 8
 BS_STATUS_CAPACITY, BS_STATUS_TIMEOUT = 1, 2
 BS_BF16, BS_E4M3, BS_E5M2, BS_F32 = 0, 1, 2, 3
 
@@ -24,6 +24,7 @@ _ERRORS = {
     BS_ERR_LAUNCH: "CUDA launch failed",
     BS_ERR_ARG: "bad argument",
     BS_ERR_WORKSPACE: "workspace too small",
+    BS_ERR_TOO_LARGE: "tensor exceeds the fixed maximum of the no-allocation entry point",
 }
 
 _vp, _i64, _i32, _sz = C.c_void_p, C.c_int64, C.c_int, C.c_size_t
@@ -34,6 +35,9 @@ _SIGS = {
     "bs_compress_workspace_bytes": (_sz, [_i64]),
     "bs_compress": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i32,
                            _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
+    "bs_compress_noalloc": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i64,
+                                   _i32, _vp, _vp, _vp, _vp, _vp]),
+    "bs_compress_noalloc_max_tiles": (_sz, []),
     "bs_tile_pack": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
     "bs_compact_vals": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _i64, _i32, _vp, _vp,
                                _vp]),

@@ -47,6 +47,8 @@
 // and `done` for the next launch.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace bs {
 
 #ifdef BS_PHASE_PROFILE
@@ -689,3 +691,68 @@ extern "C" int bs_debug_phases(unsigned long long *host_out) {
   return cudaMemcpyFromSymbol(host_out, bs::g_phase, sizeof(bs::g_phase)) == cudaSuccess ? 0 : 5;
 }
 #endif
+
+// ---------------------------------------------------------------------------
+// Compress without any allocation: scan scratch in a fixed device array.
+//
+// For callers that cannot call cudaMalloc (or must not, e.g. code running
+// inside an allocator or a framework hook that forbids allocation, and hosts
+// that have no device allocator of their own): the fused compressor's scan
+// workspace lives in this file-scope array, which every GPU that loads the
+// library holds until the process exits.  Inputs and outputs are still the
+// caller's.  All calls share the array, so calls that overlap on the GPU
+// (different streams, or different host threads on one device) race.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocMaxTiles = 262144;  // e.g. 16384 x 65536 elements
+constexpr size_t kNoAllocScratchBytes =
+    sizeof(bs::WsHeader) + (size_t)kNoAllocMaxTiles * sizeof(unsigned long long);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+void *g_scratch_ptr[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+// Device address of the scratch array on the current device.  The symbol's
+// host-side name is only a stand-in; the address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+int noalloc_scratch(void **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BS_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return BS_ERR_LAUNCH;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return BS_OK;
+}
+
+}  // namespace
+
+extern "C" size_t bs_compress_noalloc_max_tiles(void) { return (size_t)kNoAllocMaxTiles; }
+
+extern "C" int bs_compress_noalloc(const void *dense, int in_dtype, int64_t M, int64_t N,
+                                   int64_t ld, const float *quant_scale, uint8_t *quant_out,
+                                   uint8_t *bitmask, uint32_t *prefix, void *vals,
+                                   int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
+                                   int64_t *vals_offset_out, int64_t *nnz_out, int32_t *status,
+                                   void *stream) {
+  if (M < 0 || N < 0) return BS_ERR_SHAPE;
+  const int64_t tiles = ((M + kTileM - 1) / kTileM) * ((N + kTileN - 1) / kTileN);
+  if (tiles > kNoAllocMaxTiles) return BS_ERR_TOO_LARGE;
+  void *scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // The compressor leaves its scratch zeroed, but a call that gave up (a
+  // bounded wait that expired) may not have; start every call from zero.
+  const size_t used = bs_compress_workspace_bytes(tiles);
+  if (cudaMemsetAsync(scratch, 0, used, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return BS_ERR_LAUNCH;
+  return bs_compress(dense, in_dtype, M, N, ld, quant_scale, quant_out, bitmask, prefix, vals,
+                     vals_capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out, scratch,
+                     kNoAllocScratchBytes, status, stream);
+}

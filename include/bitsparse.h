@@ -43,7 +43,8 @@ enum {
   BS_ERR_CAPACITY = 4,  /* host-detectable capacity problem                 */
   BS_ERR_LAUNCH = 5,    /* a CUDA launch failed (cudaGetLastError)          */
   BS_ERR_ARG = 6,       /* NULL where a pointer is required, bad flag       */
-  BS_ERR_WORKSPACE = 7  /* workspace too small                              */
+  BS_ERR_WORKSPACE = 7, /* workspace too small                              */
+  BS_ERR_TOO_LARGE = 8  /* beyond a fixed maximum (bs_compress_noalloc)     */
 };
 
 /* Device status bits (OR-ed into *status by kernels). */
@@ -112,6 +113,28 @@ int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N,
                 int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
                 int64_t *vals_offset_out, int64_t *nnz_out, void *workspace,
                 size_t workspace_bytes, int32_t *status, void *stream);
+
+/* bs_compress without any device allocation, for callers that cannot call
+ * cudaMalloc (code running inside an allocator or a hook where allocating is
+ * forbidden, hosts without a device allocator).  No counterpart in the
+ * reference.  Same arguments and results as bs_compress minus the workspace:
+ * the scan scratch is a fixed 2 MiB + 128 B device array inside the library
+ * (held on every GPU that loads it until the process exits), so the tensor
+ * may have at most bs_compress_noalloc_max_tiles() 64x64 tiles (262144, e.g.
+ * 16384 x 65536 elements); larger tensors return BS_ERR_TOO_LARGE.  The
+ * first call on a device looks up the array's device address (make that
+ * first call before any stream capture).  Each call clears the scratch it
+ * uses with cudaMemsetAsync on `stream`; all calls share the array, so calls
+ * that overlap on the GPU race -- serialise them. */
+int bs_compress_noalloc(const void *dense, int in_dtype, int64_t M, int64_t N,
+                        int64_t ld, const float *quant_scale, uint8_t *quant_out,
+                        uint8_t *bitmask, uint32_t *prefix, void *vals,
+                        int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
+                        int64_t *vals_offset_out, int64_t *nnz_out, int32_t *status,
+                        void *stream);
+
+/* Largest tile count bs_compress_noalloc accepts. */
+size_t bs_compress_noalloc_max_tiles(void);
 
 /* Per-tile bitmask and nonzero counts only (no values): the reference's
  * tile_pack (lib_sparse/src/triton_operators.py:21-33,
