@@ -68,7 +68,8 @@ def ncu_traffic(kernel: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """nvidia-smi clock / throttle sampling during the timed region: a thread
+    runs one-shot queries back to back (about every 100 ms)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -76,32 +77,34 @@ class ClockSampler:
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
         self.lines = []
+        self._stop = threading.Event()
+
+    def _query(self):
+        try:
+            out = subprocess.run(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits"],
+                capture_output=True, text=True, timeout=5).stdout
+            self.lines.extend(l.strip() for l in out.splitlines() if l.strip())
+        except (OSError, subprocess.SubprocessError):
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._query()
+            self._stop.wait(0.1)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except OSError:
-            self.proc = None
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(2)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        self.t.join(10)
+        if not self.lines:  # a very short timed region: take one sample anyway
+            self._query()
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -455,8 +458,8 @@ def profile_case():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the sweep, MLP and CPU-baseline extras")
