@@ -1,4 +1,4 @@
-// K1 -- fused single-pass compress: dense -> bitmask, prefix, compacted values.
+// K1 -- fused compress: dense -> bitmask, prefix, compacted values.
 //
 // Reference behaviour replaced (Maxzhu123/bitsparse):
 //   _tile_pack_kernel     lib_sparse/src/triton_kernels.py:63-97
@@ -6,80 +6,53 @@
 //   _compact_vals_kernel  lib_sparse/src/triton_kernels.py:105-146
 //   _pack_kernel          lib_sparse/src/bitpacking.py:58-117
 //   arena offset update   lib_sparse/src/functions.py:73-92
-// The reference reads the dense tensor twice (tile_pack, then compact) with a
-// library scan in between; this kernel reads it once.
 //
 // Work decomposition.  A CTA of 256 threads owns a "partition" of TPP
-// consecutive tiles (tile id order = output order), handed out by an atomic
-// ticket: partition p is only processed by a CTA that started after the
-// CTAs of partitions < p, so the look-back below only waits on CTAs that are
-// already running.  Each thread owns 32-byte chunks (16 bf16 / 32 fp8 / 8
-// fp32 elements of one tile row), read with one 256-bit load; a warp covers
-// whole tile rows, so every DRAM sector is used in full.  A chunk's mask bits
-// are exactly its 2 / 4 / 1 bitmask bytes in the reference's LSB-first,
-// row-major-in-tile order; they are computed with SWAR integer arithmetic
-// on the raw bits (x > 0 <=> 0 < bits <= +inf / max-finite).
+// consecutive tiles (tile id order = output order).  Each thread owns 32-byte
+// chunks (16 bf16 / 32 fp8 / 8 fp32 elements of one tile row), read with one
+// 256-bit load; a warp covers whole tile rows, so every DRAM sector is used in
+// full.  All of a thread's loads are issued before any is consumed.  A
+// chunk's mask bits are exactly its 2 / 4 / 1 bitmask bytes in the
+// reference's LSB-first, row-major-in-tile order; they are computed with SWAR
+// integer arithmetic on the raw bits (x > 0 <=> 0 < bits <= +inf /
+// max-finite).
 //
-// Offsets.  A block-wide exclusive scan of chunk popcounts in (tile, chunk)
-// order gives each chunk's offset inside the partition.  The partition's
-// total is published as a packed 64-bit status word {state, value} and the
-// WHOLE CTA looks back over 256 predecessors per round (single-pass scan
-// with decoupled look-back).  A look-back round costs about one L2 round
-// trip; the rate at which partitions can retire is bounded by window / round
-// time, and on B200 a one-warp window of 32 would cap this kernel well below
-// HBM bandwidth -- 256 keeps the scan off the critical path.  Waits are
-// bounded (kMaxPolls): on expiry the CTA records BS_STATUS_TIMEOUT and goes
-// on, so no CTA spins forever.
+// The fused compress (MODE 0) is two wait-free kernels:
+//  1. count_kernel, partitions in order: loads the dense tiles from DRAM,
+//     writes the bitmask bytes (and the dense e4m3 tensor when quantising),
+//     stores the partition's nonzero count and adds it to its segment total
+//     (a segment = 256 partitions); block 0 snapshots the TensorBuffer offset.
+//  2. compact_kernel, partitions in REVERSE order: the partitions counted last
+//     are still resident in the 126 MB L2, so a large share of this second
+//     read never reaches DRAM.  While its loads are in flight, warp 0 sums the
+//     preceding segment totals and the preceding counts of its own segment to
+//     get the partition's base; the CTA reads its masks back from the bitmask,
+//     scans them, writes the tile prefixes and the values.  The last
+//     partition publishes the totals (arena offset, vals_offset, nnz).
+// No CTA ever waits for another one; ordering comes from the stream.  An
+// earlier single-kernel design with a decoupled look-back made every CTA
+// wait on the slowest of the hundreds of partitions between it and the
+// inclusive frontier and reached only ~20% of HBM bandwidth on B200.
 //
 // Values.  Raw storage: staged in shared memory already shifted by the
 // destination's misalignment, then written with aligned 16-byte stores
 // (element stores only for the two edge vectors shared with neighbouring
-// partitions).  Packed storage (15/7-bit): the staged values are re-packed
-// into 32-bit words of the continuous bitstream; words shared with a
-// neighbouring partition are merged with atomicAnd / atomicOr on disjoint
-// bit masks (order independent), the rest are plain stores.
-//
-// Workspace (caller owned, zero-filled once).  Header {ticket, done} plus one
-// status word per partition.  Invariant: all zero between launches.  Each
-// CTA increments `done` when its look-back is over; the CTA that brings it
-// to the partition count (so no CTA can still be reading a status word)
-// writes the arena offset / totals and zeroes the status words, the ticket
-// and `done` for the next launch.
+// partitions).  Packed storage (15/7-bit): re-packed into 32-bit words of the
+// continuous bitstream; words shared with a neighbouring partition are merged
+// with atomicAnd / atomicOr on disjoint bit masks (order independent).
 #include "common.cuh"
 
 #include <mutex>
 
 namespace bs {
 
-#ifdef BS_PHASE_PROFILE
-// Debug-only build: per-partition phase timestamps (globaltimer, ns).
-constexpr int kProfParts = 1 << 16, kProfPhases = 10;
-__device__ unsigned long long g_phase[kProfParts * kProfPhases];
-__device__ __forceinline__ void phase_mark(long long part, int ph) {
-  if (threadIdx.x == 0 && part >= 0 && part < kProfParts) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g_phase[part * kProfPhases + ph] = t;
-  }
-}
-#define PHASE(part, ph) phase_mark(part, ph)
-#define PHASE_SYNC(part, ph) do { __syncthreads(); phase_mark(part, ph); } while (0)
-#define PHASE_VAL(part, ph, v) do { if (threadIdx.x == 0 && part >= 0 && part < kProfParts) g_phase[(part) * kProfPhases + (ph)] = (v); } while (0)
-#else
-#define PHASE_VAL(part, ph, v) ((void)0)
-#define PHASE(part, ph) ((void)0)
-#define PHASE_SYNC(part, ph) ((void)0)
-#endif
-
+// Workspace: header {off0}, uint64 segment totals (zeroed by a memset before
+// the count kernel), uint32 per-partition counts.
 struct WsHeader {
-  unsigned long long ticket;
-  unsigned long long done;
-  unsigned long long pad[14];
+  long long off0;  // logical index of this tensor's first value
+  unsigned long long pad[15];
 };
-
-// status word: [63:62] state, [61:0] value
-constexpr unsigned long long kAgg = 1ull << 62, kIncl = 2ull << 62;
-constexpr unsigned long long kValMask = (1ull << 62) - 1;
+constexpr int kSeg = 256;  // partitions per segment
 
 struct CompressParams {
   const uint8_t *dense;
@@ -95,7 +68,8 @@ struct CompressParams {
   int64_t *nnz_out;
   int32_t *counts;  // MODE 2 only
   WsHeader *hdr;
-  unsigned long long *flags;
+  unsigned long long *seg_ws;  // MODE 0: per-segment totals
+  uint32_t *counts_ws;         // MODE 0: per-partition counts
   int32_t *status;
   int64_t grid_n, num_tiles, num_parts;
   int vec_ok;    // dense base / row stride allow 32-byte vector loads
@@ -159,41 +133,47 @@ __device__ __forceinline__ uint32_t mask_of_words(const uint32_t *w) {
 }
 
 // ---------------------------------------------------------------------------
-// One chunk: load (32 B), optional quantisation, stored words + mask.
+// Chunks: load 32 B raw (issued early), then stored words + mask.
 // ---------------------------------------------------------------------------
-template <int DT_IN, bool QUANT, int TPP>
-__device__ __forceinline__ uint32_t load_chunk(const CompressParams &P, int64_t grow,
-                                               int64_t gcol, float qs,
-                                               uint32_t (&sv)[Cfg<DT_IN, QUANT, TPP>::SW]) {
-  using C = Cfg<DT_IN, QUANT, TPP>;
-  uint32_t raw[8];
+template <int EB>
+__device__ __forceinline__ void load_raw(const CompressParams &P, int64_t grow, int64_t gcol,
+                                         uint32_t (&raw)[8]) {
+  constexpr int VEC = 32 / EB;
 #pragma unroll
   for (int i = 0; i < 8; ++i) raw[i] = 0;
-  if (grow < P.M) {
-    const uint8_t *src = P.dense + (grow * P.ld + gcol) * C::EB;
-    if (P.vec_ok && gcol + C::VEC <= P.N) {
-      asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                   : "=r"(raw[0]), "=r"(raw[1]), "=r"(raw[2]), "=r"(raw[3]), "=r"(raw[4]),
-                     "=r"(raw[5]), "=r"(raw[6]), "=r"(raw[7])
-                   : "l"(src));
-    } else {
+  if (grow >= P.M) return;
+  const uint8_t *src = P.dense + (grow * P.ld + gcol) * EB;
+  if (P.vec_ok && gcol + VEC <= P.N) {
+    asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(raw[0]), "=r"(raw[1]), "=r"(raw[2]), "=r"(raw[3]), "=r"(raw[4]),
+                   "=r"(raw[5]), "=r"(raw[6]), "=r"(raw[7])
+                 : "l"(src));
+  } else {
 #pragma unroll
-      for (int e = 0; e < C::VEC; ++e) {
-        if (gcol + e < P.N) {
-          uint32_t b;
-          if constexpr (C::EB == 1) b = src[e];
-          else if constexpr (C::EB == 2) b = reinterpret_cast<const uint16_t *>(src)[e];
-          else b = reinterpret_cast<const uint32_t *>(src)[e];
-          raw[e * C::EB / 4] |= b << (8 * ((e * C::EB) & 3));
-        }
+    for (int e = 0; e < VEC; ++e) {
+      if (gcol + e < P.N) {
+        uint32_t b;
+        if constexpr (EB == 1) b = src[e];
+        else if constexpr (EB == 2) b = reinterpret_cast<const uint16_t *>(src)[e];
+        else b = reinterpret_cast<const uint32_t *>(src)[e];
+        raw[e * EB / 4] |= b << (8 * ((e * EB) & 3));
       }
     }
   }
+}
+
+// raw (in place) -> stored words (first SW words) + mask.  With QUANT the
+// input is quantised to e4m3 as to_fp8 does; `side_outputs` also writes the
+// dense e4m3 tensor.
+template <int DT_IN, bool QUANT, int TPP>
+__device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64_t grow,
+                                                  int64_t gcol, float qs, uint32_t (&raw)[8],
+                                                  bool side_outputs) {
+  using C = Cfg<DT_IN, QUANT, TPP>;
   if constexpr (!QUANT) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) sv[i] = raw[i];
     return mask_of_words<C::SDT, 8>(raw);
   } else {
+    uint32_t sv[C::SW];
 #pragma unroll
     for (int i = 0; i < C::SW; ++i) sv[i] = 0;
 #pragma unroll
@@ -206,7 +186,7 @@ __device__ __forceinline__ uint32_t load_chunk(const CompressParams &P, int64_t 
       if constexpr (DT_IN == BS_BF16) y = bf16_bits_to_f32(f32_to_bf16_bits(y));
       sv[e >> 2] |= f32_to_e4m3_bits(y) << (8 * (e & 3));
     }
-    if (P.qout && grow < P.M) {
+    if (side_outputs && P.qout && grow < P.M) {
       uint8_t *dst = P.qout + grow * P.N + gcol;
       if (P.qout_vec && gcol + C::VEC <= P.N) {
         if constexpr (C::SW == 2) *reinterpret_cast<uint2 *>(dst) = make_uint2(sv[0], sv[1]);
@@ -217,6 +197,8 @@ __device__ __forceinline__ uint32_t load_chunk(const CompressParams &P, int64_t 
           if (gcol + e < P.N) dst[e] = (sv[e >> 2] >> (8 * (e & 3))) & 0xFFu;
       }
     }
+#pragma unroll
+    for (int i = 0; i < C::SW; ++i) raw[i] = sv[i];
     return mask_of_words<BS_E4M3, C::SW>(sv);
   }
 }
@@ -231,109 +213,92 @@ __device__ __forceinline__ void merge_word(uint32_t *dst, uint32_t val, uint32_t
   }
 }
 
-__device__ __forceinline__ unsigned long long ld_rlx_u64(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_rlx_u64(unsigned long long *p, unsigned long long v) {
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// Block-wide min / sum (every thread calls; every thread gets the result).
-__device__ __forceinline__ int block_min_int(int v, int *s_red) {
-  v = __reduce_min_sync(0xFFFFFFFFu, v);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) s_red[warp] = v;
-  __syncthreads();
-  int r = s_red[0];
-#pragma unroll
-  for (int i = 1; i < kThreads / 32; ++i) r = min(r, s_red[i]);
-  __syncthreads();
-  return r;
-}
-__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v,
-                                                            unsigned long long *s_red) {
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, d);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) s_red[warp] = v;
-  __syncthreads();
-  unsigned long long r = 0;
-#pragma unroll
-  for (int i = 0; i < kThreads / 32; ++i) r += s_red[i];
-  __syncthreads();
-  return r;
-}
-
-// MODE 0: fused single pass (look-back scan, writes bitmask + prefix + vals).
-// MODE 1: compact only -- partition bases come from a given prefix[] (the
-//         reference's compact_vals); bitmask / prefix are not written.
-// MODE 2: tile_pack only -- bitmask + per-tile counts, no scan, no values.
-template <int DT_IN, bool QUANT, bool PACK, int TPP, int MODE>
-__global__ void __launch_bounds__(kThreads)
-compress_kernel(const CompressParams P) {
-  using C = Cfg<DT_IN, QUANT, TPP>;
-  constexpr int NW = C::S * 8;  // warp-total slots
-  extern __shared__ __align__(128) uint8_t smem_dyn[];
-  __shared__ uint32_t s_wt[NW];
-  __shared__ uint32_t s_tile_incl[TPP];
-  __shared__ long long s_part;
-  __shared__ long long s_off0;
-  __shared__ long long s_excl;
-  __shared__ uint32_t s_total;
-  __shared__ int s_clean;
-  __shared__ int s_red_i[kThreads / 32];
-  __shared__ unsigned long long s_red_u[kThreads / 32];
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
-  if (tid == 0) {
-    long long part = blockIdx.x;
-    if (MODE == 0) part = (long long)atomicAdd(&P.hdr->ticket, 1ull);
-    s_part = part;
-    long long off = 0;
-    if (P.arena_offset) {
-      off = *(volatile long long *)P.arena_offset;
-      if (PACK && MODE == 0) off = (off + 7) / 8 * 8;  // functions.py:78-81
-    }
-    s_off0 = off;
-    s_clean = 0;
+// Grid position of the TPP consecutive tiles of a partition: one 32-bit
+// division per thread (num_tiles < 2^31), a bounded wrap per tile.
+template <int TPP>
+struct PartTiles {
+  uint32_t tm0, tn0, gn;
+  long long t0, nt;
+  __device__ __forceinline__ PartTiles(const CompressParams &P, long long part) {
+    gn = (uint32_t)P.grid_n;
+    t0 = part * TPP;
+    nt = P.num_tiles;
+    tm0 = (uint32_t)t0 / gn;
+    tn0 = (uint32_t)t0 - tm0 * gn;
   }
-  __syncthreads();
-  const long long part = s_part;
-  const float qs = QUANT ? *P.qscale : 1.f;
-  if (MODE == 0) PHASE(part, 0);
+  __device__ __forceinline__ bool valid(int j) const { return t0 + j < nt; }
+  __device__ __forceinline__ void pos(int j, uint32_t &tm, uint32_t &tn) const {
+    tm = tm0;
+    tn = tn0 + (uint32_t)j;
+    while (tn >= gn) { tn -= gn; ++tm; }
+  }
+};
 
-  // ---- load + mask ---------------------------------------------------------
-  uint32_t sv[C::S][C::SW];
-  uint32_t msk[C::S];
+// Issue the loads of a partition (all slots), no use yet.
+template <int DT_IN, bool QUANT, int TPP>
+__device__ __forceinline__ void issue_partition(const CompressParams &P, const PartTiles<TPP> &pt,
+                                                uint32_t (&raw)[Cfg<DT_IN, QUANT, TPP>::S][8]) {
+  using C = Cfg<DT_IN, QUANT, TPP>;
 #pragma unroll
   for (int s = 0; s < C::S; ++s) {
-    const int c = s * kThreads + tid;
+    const int c = s * kThreads + threadIdx.x;
+    const int j = c / C::CPT, cc = c % C::CPT;
+    const int row = cc / C::CPR, colc = cc % C::CPR;
+    uint32_t tm, tn;
+    pt.pos(j, tm, tn);
+    // out-of-range tiles: a row past M loads nothing (zeros)
+    load_raw<C::EB>(P, pt.valid(j) ? (int64_t)tm * kTileM + row : P.M,
+                    (int64_t)tn * kTileN + colc * C::VEC, raw[s]);
+  }
+}
+
+// Masks (+ bitmask bytes, + quantisation) of a loaded partition.  With
+// MASK_FROM_BITMASK (raw storage) the masks are read back from the bitmask
+// the counting pass wrote instead of being recomputed.
+template <int DT_IN, bool QUANT, int TPP, bool WRITE_BITMASK, bool MASK_FROM_BITMASK = false>
+__device__ __forceinline__ void process_partition(const CompressParams &P, long long part,
+                                                  const PartTiles<TPP> &pt,
+                                                  uint32_t (&raw)[Cfg<DT_IN, QUANT, TPP>::S][8],
+                                                  uint32_t (&msk)[Cfg<DT_IN, QUANT, TPP>::S]) {
+  using C = Cfg<DT_IN, QUANT, TPP>;
+  const float qs = QUANT ? *P.qscale : 1.f;
+#pragma unroll
+  for (int s = 0; s < C::S; ++s) {
+    const int c = s * kThreads + threadIdx.x;
     const int j = c / C::CPT, cc = c % C::CPT;
     const long long tile = part * TPP + j;
-    if (tile < P.num_tiles) {
-      const long long tm = tile / P.grid_n, tn = tile % P.grid_n;
+    msk[s] = 0;
+    if (!pt.valid(j)) continue;
+    uint8_t *bm = P.bitmask + tile * kTileBytes + cc * (C::VEC / 8);
+    if constexpr (MASK_FROM_BITMASK && !QUANT) {
+      if constexpr (C::VEC == 8) msk[s] = *bm;
+      else if constexpr (C::VEC == 16) msk[s] = *reinterpret_cast<const uint16_t *>(bm);
+      else msk[s] = *reinterpret_cast<const uint32_t *>(bm);
+    } else {
       const int row = cc / C::CPR, colc = cc % C::CPR;
-      msk[s] = load_chunk<DT_IN, QUANT, TPP>(P, tm * kTileM + row, tn * kTileN + colc * C::VEC,
-                                             qs, sv[s]);
-      if (MODE != 1) {
-        uint8_t *bm = P.bitmask + tile * kTileBytes + cc * (C::VEC / 8);
+      uint32_t tm, tn;
+      pt.pos(j, tm, tn);
+      msk[s] = process_chunk<DT_IN, QUANT, TPP>(P, (int64_t)tm * kTileM + row,
+                                                (int64_t)tn * kTileN + colc * C::VEC, qs,
+                                                raw[s], WRITE_BITMASK);
+      if (WRITE_BITMASK) {
         if constexpr (C::VEC == 8) *bm = (uint8_t)msk[s];
         else if constexpr (C::VEC == 16) *reinterpret_cast<uint16_t *>(bm) = (uint16_t)msk[s];
         else *reinterpret_cast<uint32_t *>(bm) = msk[s];
       }
-    } else {
-      msk[s] = 0;
-#pragma unroll
-      for (int i = 0; i < C::SW; ++i) sv[s][i] = 0;
     }
   }
+}
 
-  // ---- block scan of chunk counts in (slot, warp, lane) order ---------------
-  uint32_t lex[C::S];
-  if (MODE == 0) PHASE_SYNC(part, 1);
+// Block scan of chunk counts in (slot, warp, lane) order: per-thread
+// exclusive offsets in `lex` + s_wt (exclusive per warp slot); returns the
+// partition total and fills s_tile_incl (inclusive count after each tile).
+template <typename C, int TPP>
+__device__ __forceinline__ uint32_t partition_scan(const uint32_t (&msk)[C::S],
+                                                   uint32_t (&lex)[C::S], uint32_t *s_wt,
+                                                   uint32_t *s_tile_incl, uint32_t *s_total) {
+  constexpr int NW = C::S * 8;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 #pragma unroll
   for (int s = 0; s < C::S; ++s) {
     const uint32_t cnt = __popc(msk[s]);
@@ -352,98 +317,28 @@ compress_kernel(const CompressParams P) {
       if (idx < NW) s_wt[idx] = inc - v;
       carry = __shfl_sync(0xFFFFFFFFu, inc, 31);
     }
-    if (lane == 0) s_total = carry;
+    if (lane == 0) *s_total = carry;
   }
   __syncthreads();
-  const uint32_t total = s_total;
+  const uint32_t total = *s_total;
   if (tid < TPP) {
-    // chunk (tid+1)*CPT starts tile tid+1; its warp slot is that index / 32
-    const int nxt = (tid + 1) * C::CPT / 32;
+    const int nxt = (tid + 1) * C::CPT / 32;  // warp slot that starts tile tid+1
     s_tile_incl[tid] = nxt < NW ? s_wt[nxt] : total;
   }
   __syncthreads();
+  return total;
+}
 
-  if (MODE == 2) {
-    if (tid < TPP && part * TPP + tid < P.num_tiles)
-      P.counts[part * TPP + tid] =
-          (int32_t)(s_tile_incl[tid] - (tid ? s_tile_incl[tid - 1] : 0u));
-    return;
-  }
-
-  // ---- partition offset: block-wide decoupled look-back --------------------
-  if (MODE == 0) {
-    PHASE(part, 2);
-    unsigned long long *F = P.flags;
-    if (tid == 0) st_rlx_u64(&F[part], (part == 0 ? kIncl : kAgg) | total);
-    long long excl = 0;
-    if (part > 0) {
-      long long idx = part - 1;
-      uint32_t polls = 0;
-      while (true) {
-        const long long q = idx - tid;
-        unsigned long long w = kIncl;  // before partition 0: inclusive 0
-        if (q >= 0) w = ld_rlx_u64(&F[q]);
-        const unsigned long long st = w & ~kValMask;
-        const int first_incl = block_min_int(st == kIncl ? tid : kThreads, s_red_i);
-        const int first_empty = block_min_int(st == 0 ? tid : kThreads, s_red_i);
-        if (first_empty < kThreads && first_empty <= first_incl) {
-          if (++polls > kMaxPolls) {  // give up: record it, do not hang
-            if (tid == 0) status_or(P.status, BS_STATUS_TIMEOUT);
-            break;
-          }
-          __nanosleep(64);
-          continue;
-        }
-        const unsigned long long contrib = (tid <= first_incl) ? (w & kValMask) : 0ull;
-        excl += (long long)block_sum_u64(contrib, s_red_u);
-        if (first_incl < kThreads) break;
-        idx -= kThreads;
-      }
-      PHASE(part, 6);
-      PHASE_VAL(part, 8, polls);
-      PHASE_VAL(part, 9, (unsigned long long)(part - 1 - idx) / kThreads + 1);
-      if (tid == 0) st_rlx_u64(&F[part], kIncl | ((unsigned long long)excl + total));
-    }
-    if (tid == 0) {
-      s_excl = excl;
-      if (part == 0) P.prefix[0] = 0;
-      __threadfence();
-      const unsigned long long d = atomicAdd(&P.hdr->done, 1ull) + 1;
-      PHASE(part, 7);
-      if (d == (unsigned long long)P.num_parts) {
-        // Last CTA out of its look-back: every CTA has read the arena
-        // offset and no CTA reads a status word any more.
-        __threadfence();
-        const long long nnz = (long long)(ld_rlx_u64(&F[P.num_parts - 1]) & kValMask);
-        if (P.arena_offset) *P.arena_offset = s_off0 + nnz;
-        if (P.vals_offset_out) *P.vals_offset_out = s_off0;
-        if (P.nnz_out) *P.nnz_out = nnz;
-        s_clean = 1;
-      }
-    }
-  } else {
-    if (tid == 0) s_excl = (long long)P.prefix[part * TPP];
-  }
-  __syncthreads();
-  const long long excl = s_excl;
-  if (MODE == 0) PHASE(part, 3);
-  if (MODE == 0) {
-    if (s_clean) {  // zero the status words, the ticket and done
-      for (long long i = tid; i < P.num_parts; i += kThreads) st_rlx_u64(&P.flags[i], 0ull);
-      if (tid == 0) {
-        P.hdr->ticket = 0;
-        P.hdr->done = 0;
-      }
-    }
-    if (tid < TPP && part * TPP + tid < P.num_tiles)
-      P.prefix[part * TPP + tid + 1] = (uint32_t)(excl + s_tile_incl[tid]);
-  }
-  if (P.vals == nullptr) return;
-
-  // ---- values ----------------------------------------------------------------
-  const long long gbase = s_off0 + excl;  // logical index of first value
-  const long long n = total;
-  uint8_t *stage = smem_dyn;
+// Stage a partition's values (chunk order) in shared memory and write them
+// out.  `own_tail`: this partition owns (and zeroes) the packed stream after
+// its payload up to packed_storage_nbytes(nnz) (standalone, last partition).
+template <typename C, bool PACK>
+__device__ __forceinline__ void write_values(const CompressParams &P, uint8_t *stage,
+                                             const uint32_t (&msk)[C::S],
+                                             const uint32_t (&sv)[C::S][8],
+                                             const uint32_t (&lex)[C::S], const uint32_t *s_wt,
+                                             long long gbase, long long n, bool own_tail) {
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int shift = PACK ? 0 : (int)(gbase % C::EPV);
 #pragma unroll
   for (int s = 0; s < C::S; ++s) {
@@ -462,7 +357,6 @@ compress_kernel(const CompressParams P) {
     }
   }
   __syncthreads();
-  if (MODE == 0) PHASE(part, 4);
 
   if constexpr (!PACK) {
     if (n == 0) return;
@@ -486,18 +380,13 @@ compress_kernel(const CompressParams P) {
         }
       }
     }
-    if (MODE == 0) PHASE_SYNC(part, 5);
   } else {
     constexpr int B = C::BITS;
     const long long bit0 = gbase * B;
     const long long bit1 = (gbase + n) * B;
-    const bool last = (part == P.num_parts - 1);
     const long long cap_words = P.cap / 4;
-    // Standalone stream: the last partition owns (and zeroes) the bits after
-    // the payload up to the end of packed_storage_nbytes(nnz) (payload
-    // rounded to a word, plus one guard word; bitpacking.py:32-34).
     long long own_end = bit1;
-    if (MODE == 0 && last && P.arena_offset == nullptr) {
+    if (own_tail) {  // payload rounded to a word plus one guard word (bitpacking.py:32-34)
       const long long words = ((bit1 + 31) >> 5) + 1;
       own_end = (words < cap_words ? words : cap_words) * 32;
     }
@@ -510,31 +399,139 @@ compress_kernel(const CompressParams P) {
       const long long wb = w * 32;
       unsigned long long acc = 0;
       const long long rel = wb - bit0;  // bit offset of the word inside our range
-      long long k = rel > 0 ? rel / B : 0;
-      for (; k < n; ++k) {
+      for (long long k = rel > 0 ? rel / B : 0; k < n; ++k) {
         const long long sb = bit0 + k * B - wb;  // start of value k rel. to word
         if (sb >= 32) break;
         uint32_t v;
         if constexpr (C::SB == 1) v = stage[k];
         else v = reinterpret_cast<const uint16_t *>(stage)[k];
-        v &= (1u << B) - 1u;
-        acc |= (unsigned long long)v << (sb + 32);  // sb > -B >= -15
+        acc |= (unsigned long long)(v & ((1u << B) - 1u)) << (sb + 32);  // sb > -B
       }
-      const uint32_t val = (uint32_t)(acc >> 32);
       const long long lo = bit0 > wb ? bit0 - wb : 0;
       const long long hi = own_end < wb + 32 ? own_end - wb : 32;
       const uint32_t own = (hi >= 32 ? 0xFFFFFFFFu : ((1u << hi) - 1u)) & ~((1u << lo) - 1u);
-      merge_word(words + w, val, own);
+      merge_word(words + w, (uint32_t)(acc >> 32), own);
     }
   }
 }
 
 // ---------------------------------------------------------------------------
+// MODE 1: compact only -- bases from a given prefix[] (the reference's
+//         compact_vals); bitmask / prefix are not written.
+// MODE 2: tile_pack only -- bitmask + per-tile counts, no values.
+// ---------------------------------------------------------------------------
+template <int DT_IN, bool QUANT, bool PACK, int TPP, int MODE>
+__global__ void __launch_bounds__(kThreads) compress_kernel(const CompressParams P) {
+  using C = Cfg<DT_IN, QUANT, TPP>;
+  extern __shared__ __align__(128) uint8_t smem_dyn[];
+  __shared__ uint32_t s_wt[C::S * 8];
+  __shared__ uint32_t s_tile_incl[TPP];
+  __shared__ uint32_t s_total;
+  const long long part = blockIdx.x;
+  uint32_t sv[C::S][8], msk[C::S], lex[C::S];
+  const PartTiles<TPP> pt(P, part);
+  issue_partition<DT_IN, QUANT, TPP>(P, pt, sv);
+  process_partition<DT_IN, QUANT, TPP, MODE == 2>(P, part, pt, sv, msk);
+  const uint32_t total = partition_scan<C, TPP>(msk, lex, s_wt, s_tile_incl, &s_total);
+  const int tid = threadIdx.x;
+  if (MODE == 2) {
+    if (tid < TPP && part * TPP + tid < P.num_tiles)
+      P.counts[part * TPP + tid] =
+          (int32_t)(s_tile_incl[tid] - (tid ? s_tile_incl[tid - 1] : 0u));
+    return;
+  }
+  const long long off = P.arena_offset ? *P.arena_offset : 0;  // vals_offset
+  const long long gbase = off + (long long)P.prefix[part * TPP];
+  write_values<C, PACK>(P, smem_dyn, msk, sv, lex, s_wt, gbase, total, false);
+}
+
+// ---------------------------------------------------------------------------
+// MODE 0: count pass, then compact pass (see the file comment).
+// ---------------------------------------------------------------------------
+template <int DT_IN, bool QUANT, bool PACK, int TPP>
+__global__ void __launch_bounds__(kThreads) count_kernel(const CompressParams P) {
+  using C = Cfg<DT_IN, QUANT, TPP>;
+  __shared__ uint32_t s_red[kThreads / 32];
+  const long long part = blockIdx.x;
+  uint32_t raw[C::S][8], msk[C::S];
+  const PartTiles<TPP> pt(P, part);
+  issue_partition<DT_IN, QUANT, TPP>(P, pt, raw);
+  process_partition<DT_IN, QUANT, TPP, true>(P, part, pt, raw, msk);
+  uint32_t c = 0;
+#pragma unroll
+  for (int s = 0; s < C::S; ++s) c += __popc(msk[s]);
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, d);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) s_red[warp] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+#pragma unroll
+    for (int i = 0; i < kThreads / 32; ++i) t += s_red[i];
+    P.counts_ws[part] = t;
+    atomicAdd(&P.seg_ws[part / kSeg], (unsigned long long)t);
+    if (part == 0) {
+      long long off = 0;
+      if (P.arena_offset) {
+        off = *P.arena_offset;
+        if (PACK) off = (off + 7) / 8 * 8;  // functions.py:78-81
+      }
+      P.hdr->off0 = off;
+    }
+  }
+}
+
+template <int DT_IN, bool QUANT, bool PACK, int TPP>
+__global__ void __launch_bounds__(kThreads) compact_kernel(const CompressParams P) {
+  using C = Cfg<DT_IN, QUANT, TPP>;
+  extern __shared__ __align__(128) uint8_t smem_dyn[];
+  __shared__ uint32_t s_wt[C::S * 8];
+  __shared__ uint32_t s_tile_incl[TPP];
+  __shared__ uint32_t s_total;
+  __shared__ long long s_excl;
+  const long long part = P.num_parts - 1 - blockIdx.x;  // reverse: L2-resident first
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t raw[C::S][8], msk[C::S], lex[C::S];
+  const PartTiles<TPP> pt(P, part);
+  issue_partition<DT_IN, QUANT, TPP>(P, pt, raw);
+  if (warp == 0) {  // this partition's base, while the loads are in flight
+    const long long sg = part / kSeg;
+    unsigned long long sum = 0;
+    for (long long i = lane; i < sg; i += 32) sum += P.seg_ws[i];
+    for (long long i = sg * kSeg + lane; i < part; i += 32) sum += P.counts_ws[i];
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, d);
+    if (lane == 0) s_excl = (long long)sum;
+  }
+  process_partition<DT_IN, QUANT, TPP, false, true>(P, part, pt, raw, msk);
+  const uint32_t total = partition_scan<C, TPP>(msk, lex, s_wt, s_tile_incl, &s_total);
+  const long long excl = s_excl;  // written before the scan's barriers
+  const long long off0 = P.hdr->off0;
+  if (tid < TPP && part * TPP + tid < P.num_tiles)
+    P.prefix[part * TPP + tid + 1] = (uint32_t)(excl + s_tile_incl[tid]);
+  if (tid == 0) {
+    if (part == 0) P.prefix[0] = 0;
+    if (part == P.num_parts - 1) {
+      const long long nnz = excl + total;
+      if (P.arena_offset) *P.arena_offset = off0 + nnz;
+      if (P.vals_offset_out) *P.vals_offset_out = off0;
+      if (P.nnz_out) *P.nnz_out = nnz;
+    }
+  }
+  if (P.vals != nullptr)
+    write_values<C, PACK>(P, smem_dyn, msk, raw, lex, s_wt, off0 + excl, total,
+                          part == P.num_parts - 1 && P.arena_offset == nullptr);
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-// Tiles per partition.  MODE 0 wants big partitions (fewer look-back rounds
-// per byte); 1-byte inputs need an even count (128 chunks per tile).
-constexpr int tpp_for(int eb, int mode) { return mode == 0 ? 4 : (eb == 1 ? 2 : 1); }
+// Tiles per partition (a partition is 32 KB of bf16 / fp8 input, 8 KB per
+// thread-slot row); MODE 1 / 2 use small partitions.
+constexpr int tpp_for(int eb, int mode) {
+  return mode == 0 ? (eb == 1 ? 8 : 4) : (eb == 1 ? 2 : 1);
+}
 
 template <int DT_IN, bool QUANT, bool PACK, int MODE>
 static int launch_t(const CompressParams &P, cudaStream_t st) {
@@ -542,7 +539,17 @@ static int launch_t(const CompressParams &P, cudaStream_t st) {
   using C = Cfg<DT_IN, QUANT, TPP>;
   constexpr size_t smem = (MODE == 2) ? 0 : (size_t)TPP * kTileNumel * C::SB + 16;
   static_assert(smem <= 48 * 1024, "stage fits the default dynamic shared memory");
-  compress_kernel<DT_IN, QUANT, PACK, TPP, MODE><<<(unsigned)P.num_parts, kThreads, smem, st>>>(P);
+  const unsigned grid = (unsigned)P.num_parts;
+  if constexpr (MODE == 0) {
+    const size_t nseg = (size_t)((P.num_parts + kSeg - 1) / kSeg);
+    if (cudaMemsetAsync(P.seg_ws, 0, nseg * sizeof(unsigned long long), st) != cudaSuccess)
+      return BS_ERR_LAUNCH;
+    count_kernel<DT_IN, QUANT, PACK, TPP><<<grid, kThreads, 0, st>>>(P);
+    if (cudaGetLastError() != cudaSuccess) return BS_ERR_LAUNCH;
+    compact_kernel<DT_IN, QUANT, PACK, TPP><<<grid, kThreads, smem, st>>>(P);
+  } else {
+    compress_kernel<DT_IN, QUANT, PACK, TPP, MODE><<<grid, kThreads, smem, st>>>(P);
+  }
   return cudaGetLastError() == cudaSuccess ? BS_OK : BS_ERR_LAUNCH;
 }
 
@@ -601,8 +608,9 @@ using namespace bs;
 
 extern "C" size_t bs_compress_workspace_bytes(int64_t num_tiles) {
   if (num_tiles < 0) num_tiles = 0;
-  // One status word per partition; a partition is never smaller than a tile.
-  return sizeof(WsHeader) + (size_t)num_tiles * sizeof(unsigned long long);
+  // Per partition a 4-byte count and per 256 partitions an 8-byte total; a
+  // partition holds at least four tiles.
+  return sizeof(WsHeader) + 8 * ((size_t)num_tiles / 1024 + 1) + (size_t)num_tiles + 4;
 }
 
 extern "C" int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N, int64_t ld,
@@ -637,8 +645,9 @@ extern "C" int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N
   P.vals_offset_out = vals_offset_out;
   P.nnz_out = nnz_out;
   P.hdr = static_cast<WsHeader *>(workspace);
-  P.flags = reinterpret_cast<unsigned long long *>(static_cast<uint8_t *>(workspace) +
-                                                   sizeof(WsHeader));
+  P.seg_ws = reinterpret_cast<unsigned long long *>(static_cast<uint8_t *>(workspace) +
+                                                     sizeof(WsHeader));
+  P.counts_ws = reinterpret_cast<uint32_t *>(P.seg_ws + (P.num_parts + kSeg - 1) / kSeg);
   P.status = status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (P.num_tiles == 0) {
@@ -686,11 +695,6 @@ extern "C" int bs_tile_pack(const void *dense, int dtype, int64_t M, int64_t N, 
   return dispatch<2>(P, dtype, false, 0, static_cast<cudaStream_t>(stream));
 }
 
-#ifdef BS_PHASE_PROFILE
-extern "C" int bs_debug_phases(unsigned long long *host_out) {
-  return cudaMemcpyFromSymbol(host_out, bs::g_phase, sizeof(bs::g_phase)) == cudaSuccess ? 0 : 5;
-}
-#endif
 
 // ---------------------------------------------------------------------------
 // Compress without any allocation: scan scratch in a fixed device array.
