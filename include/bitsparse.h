@@ -50,7 +50,7 @@ enum {
 /* Device status bits (OR-ed into *status by kernels). */
 enum {
   BS_STATUS_CAPACITY = 1, /* vals storage too small: writes were clipped    */
-  BS_STATUS_TIMEOUT = 2   /* a bounded inter-CTA wait gave up               */
+  BS_STATUS_TIMEOUT = 2   /* reserved: a bounded device-side wait gave up    */
 };
 
 /* Element types.  Codes 1/2 equal the reference's pack codecs
@@ -71,15 +71,17 @@ enum {
 /* Library version string, e.g. "bitsparse_b200 0.1 sm_100a". Host pointer. */
 const char *bs_version(void);
 
-/* Bytes of scan workspace bs_compress needs for `num_tiles` tiles.  The
- * workspace must be zero-filled once when it is first allocated; after that
- * every launch leaves it ready for the next one.  Launches that may overlap
- * on the GPU (different streams) must use different workspaces. */
+/* Bytes of workspace bs_compress needs for `num_tiles` tiles (per-partition
+ * counts and running totals; no initial contents are required).  Launches
+ * that may overlap on the GPU (different streams) must use different
+ * workspaces. */
 size_t bs_compress_workspace_bytes(int64_t num_tiles);
 
 /* Fused compress: dense [M, N] (row stride `ld` elements) -> bitmask
- * uint8[T*512], prefix uint32[T+1] and the compacted values, in ONE pass
- * over the dense input with a single-pass device-wide scan.
+ * uint8[T*512], prefix uint32[T+1] and the compacted values: a count kernel
+ * (bitmask, per-partition counts) followed by a compact kernel (bases,
+ * prefix, values) that re-reads the input in reverse order so its most
+ * recently counted part comes from L2; no CTA waits on another.
  *
  * Replaces the whole of dense_to_tilesparse (lib_sparse/src/functions.py:55-99):
  * tile_pack (lib_sparse/src/triton_operators.py:21-33), the torch.cumsum
