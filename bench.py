@@ -233,8 +233,16 @@ def mlp_bench(cfg, steps, warmup, device):
     gy = torch.randn(T, d, generator=g, device=device).to(torch.bfloat16)
     params = [t.requires_grad_() for t in (x, W1, W2, b1, b2)]
 
-    def sparse_step():
+    from bitsparse_b200 import TensorBuffer
+
+    elt = 1 if storage != torch.bfloat16 else 2
+    arena = TensorBuffer(T * H * elt, device=device, dtype=storage)
+
+    def sparse_step(buf=None):
         kw = {"storage_dtype": storage} if relu2 else {"dtype": storage}
+        if buf is not None:
+            buf.offset.zero_()  # one activation per step: reuse the arena
+            kw["sparse_data"] = buf
         y = (FFNRelu2 if relu2 else FFNRelu).apply(*params, **kw)
         y.backward(gy)
 
@@ -246,7 +254,8 @@ def mlp_bench(cfg, steps, warmup, device):
         y.backward(gy)
 
     out = {}
-    for name, fn in (("sparse", sparse_step), ("dense", dense_step)):
+    for name, fn in (("sparse", sparse_step), ("sparse_arena", lambda: sparse_step(arena)),
+                     ("dense", dense_step)):
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
@@ -265,6 +274,8 @@ def mlp_bench(cfg, steps, warmup, device):
         sparsity = (torch.relu(x @ W1.T + b1) == 0).float().mean().item()
     out["sparsity"] = sparsity
     out["speedup_vs_dense"] = out["sparse"]["tokens_per_s"] / out["dense"]["tokens_per_s"]
+    out["speedup_arena_vs_dense"] = (out["sparse_arena"]["tokens_per_s"]
+                                     / out["dense"]["tokens_per_s"])
     return out
 
 
@@ -413,14 +424,7 @@ def run_ours(args):
         line["sweep"] = sweep
         del xs, bufs, outs
         torch.cuda.empty_cache()
-        line["mlp"] = {
-            "config2_gpt2_small_relu_bf16": mlp_bench(
-                {"tokens": 8 * 1024, "d": 768, "H": 3072, "relu2": False,
-                 "storage": torch.bfloat16, "bias_sigma": 1.0}, 10, 3, dev),
-            "config4_nemotron_relu2_fp8": mlp_bench(
-                {"tokens": 16384, "d": 4096, "H": 16384, "relu2": True,
-                 "storage": torch.float8_e4m3fn, "bias_sigma": 0.0}, 5, 2, dev),
-        }
+        line["mlp"] = mlp_suite(dev)
         if world == 1:
             gbs, dt, cores = cpu_baseline(2048, 1, 1)
             line["cpu_baseline"] = {
@@ -431,6 +435,22 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def mlp_suite(dev):
+    import torch
+
+    return {
+            "config2_gpt2_small_relu_bf16": mlp_bench(
+                {"tokens": 8 * 1024, "d": 768, "H": 3072, "relu2": False,
+                 "storage": torch.bfloat16, "bias_sigma": 1.0}, 10, 3, dev),
+            "config2_relu_bf16_90pct_sparse": mlp_bench(
+                {"tokens": 8 * 1024, "d": 768, "H": 3072, "relu2": False,
+                 "storage": torch.bfloat16, "bias_sigma": 1.2816}, 10, 3, dev),
+            "config4_nemotron_relu2_fp8": mlp_bench(
+                {"tokens": 16384, "d": 4096, "H": 16384, "relu2": True,
+                 "storage": torch.float8_e4m3fn, "bias_sigma": 0.0}, 5, 2, dev),
+    }
 
 
 def profile_case():
@@ -463,11 +483,18 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the sweep, MLP and CPU-baseline extras")
+    ap.add_argument("--mlp-only", action="store_true",
+                    help="run only the sparse-MLP fwd+bwd comparison (configs 2 and 4)")
     ap.add_argument("--profile-case", action="store_true",
                     help="run only the small ncu capture case and exit")
     args = ap.parse_args()
     if args.profile_case:
         profile_case()
+        return
+    if args.mlp_only:
+        import torch
+        dev = torch.device("cuda", 0)
+        print(json.dumps(mlp_suite(dev)), flush=True)
         return
     if args.warmup < 3:
         args.warmup = 3
