@@ -97,6 +97,31 @@ __device__ __forceinline__ uint32_t f32_to_e4m3_bits(float f) {
   return s | q;
 }
 
+// bf16(x / s) as fp32 with the quotient rounded exactly as IEEE division then
+// round-to-nearest-even bf16 would: y1 = x*r corrected by one FMA residual
+// step is within 1 fp32 ulp of the true quotient, so rounding it to bf16 can
+// only differ from rounding the exact quotient when it lies within an ulp or
+// two of a bf16 rounding midpoint (low 16 bits near 0x8000); those rare
+// quotients are recomputed with the exact division.  r = 1/s rounded.
+__device__ __forceinline__ float div_round_bf16(float x, float s, float r) {
+  const float y0 = x * r;
+  const float e = fmaf(-y0, s, x);  // exact residual
+  const float y1 = fmaf(e, r, y0);
+  const uint32_t lo = __float_as_uint(y1) & 0xFFFFu;
+  // s > 0: the quotient has x's sign (keeps -0, which the residual loses)
+  const float y = (lo - 0x7FFCu <= 8u) ? __fdiv_rn(x, s) : copysignf(y1, x);
+  return bf16_bits_to_f32(f32_to_bf16_bits(y));
+}
+
+// Two fp32 values that are already representable-range e4m3 inputs (|v| <=
+// 464, not NaN) -> two e4m3fn codes, round to nearest even, low byte = a.
+// In that range the hardware conversion matches the torch cast exactly.
+__device__ __forceinline__ uint32_t e4m3x2_bits(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+
 // Positive test on raw bits (x > 0.0 as a float; NaN and -0 are not).
 template <int DT>
 __device__ __forceinline__ bool is_pos(uint32_t b) {

@@ -176,15 +176,21 @@ __device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64
     uint32_t sv[C::SW];
 #pragma unroll
     for (int i = 0; i < C::SW; ++i) sv[i] = 0;
+    if constexpr (DT_IN == BS_BF16) {
+      // |x / scale| <= 448 * (1 + 2^-8): the fast paths are exact here
+      const float r = __frcp_rn(qs);
 #pragma unroll
-    for (int e = 0; e < C::VEC; ++e) {
-      uint32_t b;
-      if constexpr (C::EB == 2) b = (raw[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
-      else b = raw[e];
-      const float x = (DT_IN == BS_BF16) ? bf16_bits_to_f32(b) : __uint_as_float(b);
-      float y = __fdiv_rn(x, qs);
-      if constexpr (DT_IN == BS_BF16) y = bf16_bits_to_f32(f32_to_bf16_bits(y));
-      sv[e >> 2] |= f32_to_e4m3_bits(y) << (8 * (e & 3));
+      for (int e = 0; e < C::VEC; e += 2) {
+        const float y0 = div_round_bf16(bf16_bits_to_f32((raw[e >> 1] & 0xFFFFu)), qs, r);
+        const float y1 = div_round_bf16(bf16_bits_to_f32(raw[e >> 1] >> 16), qs, r);
+        sv[e >> 2] |= e4m3x2_bits(y0, y1) << (8 * (e & 3));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < C::VEC; ++e) {
+        const float y = __fdiv_rn(__uint_as_float(raw[e]), qs);
+        sv[e >> 2] |= f32_to_e4m3_bits(y) << (8 * (e & 3));
+      }
     }
     if (side_outputs && P.qout && grow < P.M) {
       uint8_t *dst = P.qout + grow * P.N + gcol;

@@ -265,3 +265,17 @@ def test_deterministic():
         a = dense_to_tilesparse(d, None, None, pack)
         b = dense_to_tilesparse(d, None, None, pack)
         assert torch.equal(a.vals, b.vals) and torch.equal(a.prefix, b.prefix)
+
+
+def test_to_fp8_many_values_and_scales():
+    """The bf16 quantiser (reciprocal + residual-corrected quotient, exact
+    division near bf16 rounding midpoints, hardware e4m3 cast) equals the
+    oracle's eager-PyTorch to_fp8 on random data over many magnitudes."""
+    g = torch.Generator().manual_seed(17)
+    for mag in (1e-6, 1e-3, 0.37, 1.0, 3.3, 250.0, 1e4):
+        x = (torch.randn(1 << 20, generator=g) * mag).to(torch.bfloat16)
+        x[:7] = torch.tensor([0.0, -0.0, mag, -mag, 1e-30, mag * 1e-4, -mag * 3])
+        q, s = to_fp8(x.cuda())
+        qo, so = O.to_fp8(bits(x), "bfloat16")
+        assert s.item() == so
+        np.testing.assert_array_equal(bits(q), qo)
