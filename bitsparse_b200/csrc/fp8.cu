@@ -116,6 +116,49 @@ quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q) {
   }
 }
 
+// dst[c][r] = src[r][c] for 1-byte elements (fp8 operands that cuBLASLt
+// wants in the other major order).  A CTA moves a 64 x 64 byte tile through
+// shared memory: 16-byte coalesced loads of source rows, 16-byte stores of
+// destination rows.
+__global__ void __launch_bounds__(kThreads)
+transpose_b8_kernel(const uint8_t *src, int64_t rows, int64_t cols, int64_t lds, uint8_t *dst,
+                    int64_t ldd, int vec) {
+  __shared__ uint8_t t[64][64 + 4];
+  const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
+  const int tid = threadIdx.x;
+  {  // load: row tid/4, 16 bytes at column (tid%4)*16
+    const int r = tid >> 2, q = (tid & 3) * 16;
+    const int64_t gr = r0 + r, gc = c0 + q;
+    uint32_t w[4] = {0, 0, 0, 0};
+    if (gr < rows) {
+      if (vec && gc + 16 <= cols) {
+        const uint4 v = ld_nc_v4(src + gr * lds + gc);
+        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+      } else {
+        for (int e = 0; e < 16; ++e)
+          if (gc + e < cols) w[e >> 2] |= (uint32_t)src[gr * lds + gc + e] << (8 * (e & 3));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<uint32_t *>(&t[r][q + 4 * i]) = w[i];
+  }
+  __syncthreads();
+  {  // store: destination row c = tid/4 (source column), 16 source rows
+    const int c = tid >> 2, q = (tid & 3) * 16;
+    const int64_t gr = c0 + c, gc = r0 + q;  // destination coordinates
+    if (gr >= cols) return;
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w[e >> 2] |= (uint32_t)t[q + e][c] << (8 * (e & 3));
+    if (vec && gc + 16 <= rows) {
+      *reinterpret_cast<uint4 *>(dst + gr * ldd + gc) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      for (int e = 0; e < 16; ++e)
+        if (gc + e < rows) dst[gr * ldd + gc + e] = (w[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+    }
+  }
+}
+
 }  // namespace bs
 
 using namespace bs;
@@ -160,6 +203,20 @@ extern "C" int bs_quantize_e4m3(const void *x, int dtype, int64_t numel, const f
   const uint8_t *xb = static_cast<const uint8_t *>(x);
   if (dtype == BS_BF16) quant_kernel<BS_BF16><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, scale, q);
   else quant_kernel<BS_F32><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, scale, q);
+  return launch_err();
+}
+
+extern "C" int bs_transpose_b8(const void *src, int64_t rows, int64_t cols, int64_t ld_src,
+                               void *dst, int64_t ld_dst, void *stream) {
+  if (rows < 0 || cols < 0 || ld_src < cols || ld_dst < rows) return BS_ERR_SHAPE;
+  if (rows == 0 || cols == 0) return BS_OK;
+  if (!src || !dst) return BS_ERR_ARG;
+  const int vec = aligned16(src) && aligned16(dst) && ld_src % 16 == 0 && ld_dst % 16 == 0;
+  const dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
+  if (grid.y > 65535) return BS_ERR_SHAPE;
+  transpose_b8_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t *>(src), rows, cols, ld_src, static_cast<uint8_t *>(dst), ld_dst,
+      vec);
   return launch_err();
 }
 

@@ -32,6 +32,19 @@ def is_fp8(dtype) -> bool:
     return dtype in _FP8_DTYPES
 
 
+def _dense_layout(x: Tensor) -> tuple[Tensor, bool]:
+    """(a contiguous tensor with x's elements, whether it is x transposed).
+
+    A 2-D tensor whose transpose is contiguous (e.g. ``W.T``) is processed as
+    that transpose, so no transposed copy is made; the result is transposed
+    back as a view, keeping x's layout."""
+    if x.is_contiguous():
+        return x, False
+    if x.dim() == 2 and x.T.is_contiguous():
+        return x.T, True
+    return x.contiguous(), False
+
+
 @torch.no_grad()
 def fp8_scale(x: Tensor) -> Tensor:
     """Per-tensor scale of to_fp8: max(amax(|x|) / 448, 1e-9), fp32 0-dim.
@@ -43,7 +56,7 @@ def fp8_scale(x: Tensor) -> Tensor:
     R.require_cuda(x, "x")
     if x.dtype not in (torch.bfloat16, torch.float32):
         raise TypeError("to_fp8 takes bfloat16 or float32 input")
-    x = x.contiguous()
+    x, _ = _dense_layout(x)  # the amax does not depend on the layout
     scale = torch.empty((), dtype=torch.float32, device=x.device)
     _lib.call("bs_fp8_scale", x.data_ptr(), R.dtype_code(x.dtype), x.numel(),
               R.amax_scratch(x.device).data_ptr(), scale.data_ptr(),
@@ -56,11 +69,11 @@ def quantize_e4m3(x: Tensor, scale: Tensor) -> Tensor:
     """e4m3fn(x / scale), elementwise (bf16 input: quotient rounded to bf16)."""
     from . import _lib, _runtime as R
 
-    x = x.contiguous()
-    q = torch.empty(x.shape, dtype=_FP8_DTYPE, device=x.device)
-    _lib.call("bs_quantize_e4m3", x.data_ptr(), R.dtype_code(x.dtype), x.numel(),
+    xc, transposed = _dense_layout(x)
+    q = torch.empty(xc.shape, dtype=_FP8_DTYPE, device=x.device)
+    _lib.call("bs_quantize_e4m3", xc.data_ptr(), R.dtype_code(xc.dtype), xc.numel(),
               scale.data_ptr(), q.data_ptr(), R.stream_handle(x.device))
-    return q
+    return q.T if transposed else q
 
 
 @torch.no_grad()
@@ -70,13 +83,33 @@ def to_fp8(x: Tensor) -> tuple[Tensor, Tensor]:
     return quantize_e4m3(x, scale), scale
 
 
+def _transposed_b8(x: Tensor) -> Tensor:
+    """A contiguous copy of x.T for a 2-D contiguous 1-byte tensor (CUDA kernel)."""
+    from . import _lib, _runtime as R
+
+    rows, cols = x.shape
+    out = torch.empty((cols, rows), dtype=x.dtype, device=x.device)
+    _lib.call("bs_transpose_b8", x.data_ptr(), rows, cols, cols, out.data_ptr(), rows,
+              R.stream_handle(x.device))
+    return out
+
+
+def _row_major_fp8(x: Tensor) -> Tensor:
+    """x with unit column stride (row-major), transposing on the GPU if needed."""
+    if x.stride(1) == 1 and x.stride(0) >= x.shape[1]:
+        return x
+    if x.T.is_contiguous():
+        return _transposed_b8(x.T)
+    return x.contiguous()
+
+
 def _scaled_mm(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor,
                output_dtype: torch.dtype) -> Tensor:
     """FP8 GEMM with tensor-wise scales (lib_sparse/fp8.py:25-49)."""
     if a.stride(1) != 1:
-        a = a.contiguous()
+        a = _row_major_fp8(a)
     if b.stride(0) != 1:
-        b = b.T.contiguous().T
+        b = _row_major_fp8(b.T).T
     return F.scaled_mm(
         mat_a=a, mat_b=b,
         scale_a=a_scale, scale_b=b_scale, output_dtype=output_dtype,
@@ -124,7 +157,7 @@ class MatmulFp8(Function):
         if ctx.needs_input_grad[0]:
             grad_a = _scaled_mm(g_fp8, b_fp8.T, g_scale, b_scale, output_dtype=torch.bfloat16)
         if ctx.needs_input_grad[1]:
-            grad_b = _scaled_mm(a_fp8.T.contiguous(), g_fp8, a_scale, g_scale,
+            grad_b = _scaled_mm(_row_major_fp8(a_fp8.T), g_fp8, a_scale, g_scale,
                                 output_dtype=torch.bfloat16)
         return grad_a, grad_b, None, None
 

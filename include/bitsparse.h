@@ -195,6 +195,14 @@ int bs_fp8_scale(const void *x, int dtype, int64_t numel, uint32_t *amax_ws,
 int bs_quantize_e4m3(const void *x, int dtype, int64_t numel, const float *scale,
                      uint8_t *q, void *stream);
 
+/* dst[c][r] = src[r][c] for 1-byte elements (fp8): the operand transposes
+ * that the reference's FP8 GEMM wrapper makes with .T.contiguous()
+ * (lib_sparse/fp8.py:39-43, :107-110) because cuBLASLt's FP8 GEMM takes A
+ * row-major and B column-major.  src [rows, cols] row stride ld_src, dst
+ * [cols, rows] row stride ld_dst. */
+int bs_transpose_b8(const void *src, int64_t rows, int64_t cols, int64_t ld_src,
+                    void *dst, int64_t ld_dst, void *stream);
+
 /* Values only, with tile offsets from an existing prefix: the reference's
  * compact_vals (lib_sparse/src/triton_operators.py:36-115,
  * lib_sparse/src/triton_kernels.py:105-146, lib_sparse/src/bitpacking.py:58-117).

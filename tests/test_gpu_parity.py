@@ -279,3 +279,12 @@ def test_to_fp8_many_values_and_scales():
         qo, so = O.to_fp8(bits(x), "bfloat16")
         assert s.item() == so
         np.testing.assert_array_equal(bits(q), qo)
+
+
+@pytest.mark.parametrize("rows, cols", [(1, 1), (64, 64), (100, 37), (4096, 768), (33, 4100)])
+def test_transpose_b8(rows, cols):
+    from bitsparse_b200.fp8 import _transposed_b8
+    x = torch.randint(0, 256, (rows, cols), dtype=torch.uint8, device="cuda")
+    assert torch.equal(_transposed_b8(x), x.T.contiguous())
+    xf = x.view(torch.float8_e4m3fn)
+    assert torch.equal(_transposed_b8(xf).view(torch.uint8), x.T.contiguous())
