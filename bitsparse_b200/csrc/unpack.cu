@@ -201,8 +201,22 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     const uint32_t mm = m[s];
     uint32_t r = ex[s];
+    if constexpr (OUT == 0 && !PACK) {
+      // Branch-free expand: every element loads the value at its rank (the
+      // stage has slack past the last value) and keeps it only if its bit
+      // is set; divergent per-element branches cost more than the loads.
+#pragma unroll
+      for (int e = 0; e < G::VEC; ++e) {
+        const uint32_t bit = (mm >> e) & 1u;
+        const uint32_t v = staged_value<SDT, PACK>(stage, first, r) & (0u - bit);
+        r += bit;
+        if constexpr (OB == 1) w[e >> 2] |= v << (8 * (e & 3));
+        else w[e >> 1] |= v << (16 * (e & 1));
+      }
+    }
 #pragma unroll
     for (int e = 0; e < G::VEC; ++e) {  // static indices keep w[] in registers
+      if constexpr (OUT == 0 && !PACK) break;
       if (!((mm >> e) & 1u)) continue;
       uint32_t v = staged_value<SDT, PACK>(stage, first, r++);
       if constexpr (OUT == 1) {
