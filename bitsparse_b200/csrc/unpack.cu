@@ -157,6 +157,21 @@ __device__ __forceinline__ int tiles_here(const UnpackParams &P, int64_t pid0) {
   return (int)(left < kUT ? left : kUT);
 }
 
+// Grid position of the CTA's tiles: one division for its first tile, then a
+// wrapping step per tile (a 64-bit divide per chunk costs ~70 instructions).
+struct PidPos {
+  int64_t r0, c0, gn;
+  __device__ __forceinline__ PidPos(int64_t pid0, int64_t grid_n)
+      : r0(pid0 / grid_n), c0(pid0 % grid_n), gn(grid_n) {}
+  __device__ __forceinline__ void pos(int j, int64_t &tr, int64_t &tc) const {
+    tr = r0;
+    tc = c0 + j;
+#pragma unroll
+    for (int i = 0; i < kUT - 1; ++i)
+      if (tc >= gn) { tc -= gn; ++tr; }
+  }
+};
+
 // OUT: 0 = elements of SDT (plain reconstruct), 1 = bf16 k*r^2 (ReLU^2).
 template <int SDT, bool PACK, int OUT, bool SCALE>
 __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) {
@@ -167,6 +182,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
 
   const int64_t pid0 = (int64_t)blockIdx.x * kUT;
   const int nt = tiles_here(P, pid0);
+  const PidPos pp(pid0, P.grid_n);
   const int tid = threadIdx.x;
   const uint32_t first = stage_values<SDT, PACK>(P, P.first_tile + pid0, nt, stage);
 
@@ -193,10 +209,11 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
     const int c = s * kThreads + tid;
     const int j = c / G::CPT, cc = c % G::CPT;
     if (j >= nt) continue;
-    const int64_t pid = pid0 + j;
     const int row = cc / G::CPR, colc = cc % G::CPR;
-    const int64_t grow = (pid / P.grid_n) * kTileM + row;
-    const int64_t gcol = (pid % P.grid_n) * kTileN + colc * G::VEC;
+    int64_t tr, tc;
+    pp.pos(j, tr, tc);
+    const int64_t grow = tr * kTileM + row;
+    const int64_t gcol = tc * kTileN + colc * G::VEC;
     if (grow >= P.batch_rows) continue;
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     const uint32_t mm = m[s];
@@ -253,6 +270,7 @@ __global__ void __launch_bounds__(kThreads) mask_kernel(const UnpackParams P) {
   using G = Chunk<GB>;
   const int64_t pid0 = (int64_t)blockIdx.x * kUT;
   const int nt = tiles_here(P, pid0);
+  const PidPos pp(pid0, P.grid_n);
 #pragma unroll
   for (int s = 0; s < G::S; ++s) {
     const int c = s * kThreads + threadIdx.x;
@@ -260,8 +278,10 @@ __global__ void __launch_bounds__(kThreads) mask_kernel(const UnpackParams P) {
     if (j >= nt) continue;
     const int64_t tile = pid0 + j;
     const int row = cc / G::CPR, colc = cc % G::CPR;
-    const int64_t grow = (tile / P.grid_n) * kTileM + row;
-    const int64_t gcol = (tile % P.grid_n) * kTileN + colc * G::VEC;
+    int64_t tr, tc;
+    pp.pos(j, tr, tc);
+    const int64_t grow = tr * kTileM + row;
+    const int64_t gcol = tc * kTileN + colc * G::VEC;
     if (grow >= P.batch_rows) continue;
     const uint32_t mb = load_mask<G::VEC>(P.bitmask + tile * kTileBytes + cc * (G::VEC / 8));
     constexpr uint32_t full = G::VEC == 16 ? 0xFFFFu : 0xFFu;
@@ -300,6 +320,7 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
   __shared__ uint32_t s_wt[G::S * 8];
   const int64_t pid0 = (int64_t)blockIdx.x * kUT;
   const int nt = tiles_here(P, pid0);
+  const PidPos pp(pid0, P.grid_n);
   const int tid = threadIdx.x;
   const uint32_t first = stage_values<SDT, PACK>(P, pid0, nt, stage);
   uint32_t m[G::S], cnt[G::S], ex[G::S];
@@ -322,8 +343,10 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
     if (j >= nt) continue;
     const int64_t tile = pid0 + j;
     const int row = cc / G::CPR, colc = cc % G::CPR;
-    const int64_t grow = (tile / P.grid_n) * kTileM + row;
-    const int64_t gcol = (tile % P.grid_n) * kTileN + colc * 16;
+    int64_t tr, tc;
+    pp.pos(j, tr, tc);
+    const int64_t grow = tr * kTileM + row;
+    const int64_t gcol = tc * kTileN + colc * 16;
     if (grow >= P.batch_rows) continue;
     uint16_t *g = reinterpret_cast<uint16_t *>(P.out + (grow * P.out_ld + gcol) * 2);
     const bool vec = P.out_v32 && gcol + 16 <= P.K;
