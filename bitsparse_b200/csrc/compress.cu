@@ -17,7 +17,10 @@
 // integer arithmetic on the raw bits (x > 0 <=> 0 < bits <= +inf /
 // max-finite).
 //
-// The fused compress (MODE 0) is two wait-free kernels:
+// The fused compress (MODE 0) is one persistent kernel, onepass_kernel
+// (described where it is defined), for inputs TMA can read: a 16-byte
+// aligned base and a row stride that is a multiple of 16 bytes.  Other
+// inputs (and fp32 ones) use two wait-free kernels:
 //  1. count_kernel, partitions in order: loads the dense tiles from DRAM,
 //     writes the bitmask bytes (and the dense e4m3 tensor when quantising),
 //     stores the partition's nonzero count and adds it to its segment total
@@ -29,19 +32,24 @@
 //     get the partition's base; the CTA reads its masks back from the bitmask,
 //     scans them, writes the tile prefixes and the values.  The last
 //     partition publishes the totals (arena offset, vals_offset, nnz).
-// No CTA ever waits for another one; ordering comes from the stream.  An
-// earlier single-kernel design with a decoupled look-back made every CTA
-// wait on the slowest of the hundreds of partitions between it and the
-// inclusive frontier and reached only ~20% of HBM bandwidth on B200.
+// No CTA of these two ever waits for another one; ordering comes from the
+// stream.  (BS_COMPRESS_TWO_KERNELS=1 in the environment selects them for
+// every input, for comparison.)
 //
-// Values.  Raw storage: staged in shared memory already shifted by the
-// destination's misalignment, then written with aligned 16-byte stores
+// Values of the two-kernel path.  Raw storage: staged in shared memory
+// already shifted by the destination's misalignment, then written with
+// aligned 16-byte stores
 // (element stores only for the two edge vectors shared with neighbouring
 // partitions).  Packed storage (15/7-bit): re-packed into 32-bit words of the
 // continuous bitstream; words shared with a neighbouring partition are merged
 // with atomicAnd / atomicOr on disjoint bit masks (order independent).
 #include "common.cuh"
 
+#include <cuda_bf16.h>
+
+#include <cuda.h>  // CUtensorMap (types only; the encoder comes through the runtime)
+
+#include <cstdlib>
 #include <mutex>
 
 namespace bs {
@@ -335,17 +343,14 @@ __device__ __forceinline__ uint32_t partition_scan(const uint32_t (&msk)[C::S],
   return total;
 }
 
-// Stage a partition's values (chunk order) in shared memory and write them
-// out.  `own_tail`: this partition owns (and zeroes) the packed stream after
-// its payload up to packed_storage_nbytes(nnz) (standalone, last partition).
-template <typename C, bool PACK>
-__device__ __forceinline__ void write_values(const CompressParams &P, uint8_t *stage,
-                                             const uint32_t (&msk)[C::S],
+// Stage a partition's values (chunk order) in shared memory, starting at
+// element `shift` of the stage.
+template <typename C>
+__device__ __forceinline__ void stage_values(uint8_t *stage, const uint32_t (&msk)[C::S],
                                              const uint32_t (&sv)[C::S][8],
                                              const uint32_t (&lex)[C::S], const uint32_t *s_wt,
-                                             long long gbase, long long n, bool own_tail) {
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int shift = PACK ? 0 : (int)(gbase % C::EPV);
+                                             int shift) {
+  const int warp = threadIdx.x >> 5;
 #pragma unroll
   for (int s = 0; s < C::S; ++s) {
     const uint32_t m = msk[s];
@@ -363,25 +368,53 @@ __device__ __forceinline__ void write_values(const CompressParams &P, uint8_t *s
     }
   }
   __syncthreads();
+}
 
+// Write n staged values to logical value index gbase.  Stage element i holds
+// value gbase + i - shift, where shift = gbase % (16 / SB) when PRESHIFTED
+// (16-byte destination vectors are then aligned 16-byte stage reads) and 0
+// otherwise (each vector is funnel-shifted out of five stage words; the
+// stage needs 16 bytes of slack past its values).  `own_tail`: this
+// partition owns (and zeroes) the packed stream after its payload up to
+// packed_storage_nbytes(nnz) (standalone, last partition).  NT threads
+// cooperate; this one is number `tid` of them.
+template <typename C, bool PACK, bool PRESHIFTED, int NT = kThreads>
+__device__ __forceinline__ void emit_values(const CompressParams &P, const uint8_t *stage,
+                                            long long gbase, long long n, bool own_tail,
+                                            int tid) {
   if constexpr (!PACK) {
     if (n == 0) return;
+    const int shift = PRESHIFTED ? (int)(gbase % C::EPV) : 0;
     const long long cap = P.cap;
     if (tid == 0 && gbase + n > cap) status_or(P.status, BS_STATUS_CAPACITY);
-    const long long v0 = (gbase - shift) / C::EPV;
+    const long long v0 = gbase / C::EPV;
     const long long v1 = (gbase + n - 1) / C::EPV;
-    for (long long v = v0 + tid; v <= v1; v += kThreads) {
+    for (long long v = v0 + tid; v <= v1; v += NT) {
       const long long e0 = v * C::EPV;
-      const uint8_t *src = stage + (v - v0) * 16;
+      const long long i0 = e0 - gbase + shift;  // stage index of value e0
       if (P.vals_v16 && e0 >= gbase && e0 + C::EPV <= gbase + n && e0 + C::EPV <= cap) {
-        st_v4(P.vals + e0 * C::SB, *reinterpret_cast<const uint4 *>(src));
+        uint4 o;
+        if constexpr (PRESHIFTED) {
+          o = *reinterpret_cast<const uint4 *>(stage + i0 * C::SB);
+        } else {
+          const uint32_t b = (uint32_t)i0 * C::SB;
+          const uint32_t *w = reinterpret_cast<const uint32_t *>(stage) + (b >> 2);
+          const uint32_t sh = (b & 3u) * 8u;
+          const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+          o.x = __funnelshift_r(w0, w1, sh);
+          o.y = __funnelshift_r(w1, w2, sh);
+          o.z = __funnelshift_r(w2, w3, sh);
+          o.w = __funnelshift_r(w3, w4, sh);
+        }
+        st_v4(P.vals + e0 * C::SB, o);
       } else {
         for (int e = 0; e < C::EPV; ++e) {
           const long long g = e0 + e;
           if (g >= gbase && g < gbase + n && g < cap) {
-            if constexpr (C::SB == 1) P.vals[g] = src[e];
+            const long long i = i0 + e;
+            if constexpr (C::SB == 1) P.vals[g] = stage[i];
             else reinterpret_cast<uint16_t *>(P.vals)[g] =
-                reinterpret_cast<const uint16_t *>(src)[e];
+                reinterpret_cast<const uint16_t *>(stage)[i];
           }
         }
       }
@@ -400,7 +433,7 @@ __device__ __forceinline__ void write_values(const CompressParams &P, uint8_t *s
     const long long w0 = bit0 >> 5, w1 = (own_end - 1) >> 5;
     if (tid == 0 && ((bit1 + 31) >> 5) > cap_words) status_or(P.status, BS_STATUS_CAPACITY);
     uint32_t *words = reinterpret_cast<uint32_t *>(P.vals);
-    for (long long w = w0 + tid; w <= w1; w += kThreads) {
+    for (long long w = w0 + tid; w <= w1; w += NT) {
       if (w >= cap_words) break;
       const long long wb = w * 32;
       unsigned long long acc = 0;
@@ -419,6 +452,16 @@ __device__ __forceinline__ void write_values(const CompressParams &P, uint8_t *s
       merge_word(words + w, (uint32_t)(acc >> 32), own);
     }
   }
+}
+
+template <typename C, bool PACK>
+__device__ __forceinline__ void write_values(const CompressParams &P, uint8_t *stage,
+                                             const uint32_t (&msk)[C::S],
+                                             const uint32_t (&sv)[C::S][8],
+                                             const uint32_t (&lex)[C::S], const uint32_t *s_wt,
+                                             long long gbase, long long n, bool own_tail) {
+  stage_values<C>(stage, msk, sv, lex, s_wt, PACK ? 0 : (int)(gbase % C::EPV));
+  emit_values<C, PACK, true>(P, stage, gbase, n, own_tail, threadIdx.x);
 }
 
 // ---------------------------------------------------------------------------
@@ -531,12 +574,529 @@ __global__ void __launch_bounds__(kThreads) compact_kernel(const CompressParams 
 }
 
 // ---------------------------------------------------------------------------
+// MODE 0, one pass: a persistent kernel, every CTA resident (a cooperative
+// launch).  CTA b owns partitions b, b+G, b+2G, ... (G = grid size; a
+// partition is 32 KB of input: 4 bf16 / 8 fp8 tiles).  Per round r
+// (partition p = rG + b) the CTA
+//   1. has TMA fetch the tiles of partition p + A*G into input stage
+//      (r + A) % NS (2-D tiled copies, zero-filled past the tensor's edge),
+//   2. prefetches the counts it needs to flush partition q = p - D*G,
+//   3. waits for stage r % NS and compacts p IN PLACE: each warp owns RW
+//      whole tile rows; in step s lane l takes 8 consecutive elements of row
+//      4s + l/8 (one 16-byte shared load), whose 8 mask bits (a bf16x2
+//      compare per word) are exactly one bitmask byte; a warp scan of the
+//      lanes' counts orders the values.  After a barrier (every row read,
+//      warp counts published) each value is stored, predicated, at its
+//      partition-wide position -- never past the element it came from --
+//      and p's count is published (count + 1, so 0 means "not yet"),
+//   4. flushes q: its base is the end of the CTA's own previous partition
+//      (q - G) plus the published counts of the G-1 partitions in between.
+//      No chain of prefixes runs through the CTAs: a slow CTA delays the
+//      others by its counting only, and D rounds of slack absorb that.  The
+//      CTA writes q's prefixes and its values (16-byte vectors funnel-shifted
+//      out of the stage; only the two edge vectors element by element).
+// An earlier single-pass design with a decoupled look-back (a chain of
+// inclusive prefixes through the CTAs) reached only ~20% of HBM bandwidth:
+// every CTA waited on the slowest of the hundreds of partitions ahead of it.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// 2-D tiled TMA load of one 64 x 64 tile (no multicast).
+__device__ __forceinline__ void tma_load_tile(void *dst, const CUtensorMap *map, int x, int y,
+                                              uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u32(uint32_t *p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Shared-memory plan of the one-pass kernel.
+template <int DT_IN, bool QUANT, int TPP_, int NW, int D, int A>
+struct Onepass {
+  static constexpr int EB = Elt<DT_IN>::bytes;
+  static constexpr int TPP = TPP_;
+  using C = Cfg<DT_IN, QUANT, TPP>;
+  static constexpr int SB = C::SB;
+  static constexpr int R = TPP * kTileM;          // tile rows per partition
+  static constexpr int RW = R / NW;               // rows per warp
+  static constexpr int WREG = RW * kTileN * EB;   // bytes of a warp's rows (= its value region)
+  static constexpr int IN_BYTES = TPP * kTileNumel * EB;
+  // A stage holds a partition from its fetch (A rounds ahead) through its
+  // flush (D rounds after it is compacted in place).
+  static constexpr int NS = D + 1 + A;
+  // per stage: warp counts [NW], tile inclusive counts [TPP], total
+  static constexpr int META = NW + TPP + 1;
+  static constexpr size_t OFF_META = (size_t)NS * IN_BYTES + 32;  // + emit read slack
+  static constexpr size_t OFF_BAR = (OFF_META + 4 * NS * META + 7) / 8 * 8;
+  static constexpr size_t SMEM = OFF_BAR + 8 * NS;
+  static_assert(kTileM % RW == 0 && RW % 4 == 0, "a warp's rows lie in one tile");
+  static_assert(SB <= EB, "values fit in place of their inputs");
+};
+
+// NT threads write n raw staged values (stage element 0 = value g0): the
+// whole 16-byte destination vectors thread-strided, each funnel-shifted out
+// of five stage words, then the head and tail elements (the vectors shared
+// with the neighbouring ranges) one element per thread.  The stage needs 16 bytes
+// of slack past its values; vals must be 16-byte aligned.
+template <typename C, int NT>
+__device__ __forceinline__ void emit_words(const CompressParams &P, const uint8_t *stage,
+                                           long long g0, long long n, int lane) {
+  constexpr int EPV = 16 / C::SB;
+  if (n <= 0) return;
+  const long long cap = P.cap;
+  if (g0 + n > cap) {
+    if (lane == 0) status_or(P.status, BS_STATUS_CAPACITY);
+    n = cap - g0;
+    if (n <= 0) return;
+  }
+  uint8_t *vals = P.vals;
+  const int nn = (int)n;                                // < 2^31 (one warp's rows)
+  const int head = (int)((EPV - g0 % EPV) % EPV);       // elements before the first vector
+  const int nfull = nn > head ? (nn - head) / EPV : 0;  // whole vectors
+  const int tail0 = nfull ? head + nfull * EPV : 0;     // first element after them
+  const uint32_t *s32 = reinterpret_cast<const uint32_t *>(stage);
+  uint4 *dst = reinterpret_cast<uint4 *>(vals + (g0 + head) * C::SB);
+  for (int v = lane; v < nfull; v += NT) {
+    const int rel = (head + v * EPV) * C::SB;  // stage byte of the vector
+    const int j = rel >> 2;
+    const uint32_t sh = (uint32_t)(rel & 3) * 8u;
+    const uint32_t w0 = s32[j], w1 = s32[j + 1], w2 = s32[j + 2], w3 = s32[j + 3],
+                   w4 = s32[j + 4];
+    dst[v] = make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh),
+                        __funnelshift_r(w2, w3, sh), __funnelshift_r(w3, w4, sh));
+  }
+  // edge elements: [0, head) and [tail0, nn) (all of them when nfull == 0)
+  const int nhead = nfull ? head : nn;
+  for (int e = lane; e < nhead + (nn - tail0 > 0 && nfull ? nn - tail0 : 0); e += NT) {
+    const int i = e < nhead ? e : tail0 + (e - nhead);
+    if constexpr (C::SB == 2)
+      reinterpret_cast<uint16_t *>(vals)[g0 + i] = reinterpret_cast<const uint16_t *>(stage)[i];
+    else
+      vals[g0 + i] = stage[i];
+  }
+}
+
+// Mask of 8 bf16 (4 words): bit i set iff element i > 0 (a bf16x2 compare
+// per word: NaN, -0 and +0 give 0).
+__device__ __forceinline__ uint32_t mask_bf16x8(const uint32_t (&w)[4]) {
+  const __nv_bfloat162 zero = __float2bfloat162_rn(0.f);
+  uint32_t q = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t h = __hgt2_mask(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]), zero);
+    q |= (h & 0x80008000u) >> (15 - 2 * i);
+  }
+  return (q & 0x5555u) | ((q >> 15) & 0xAAAAu);
+}
+
+// Inclusive warp scan: shfl.up's in-range predicate guards each add (no
+// branches).
+__device__ __forceinline__ uint32_t warp_scan_pred(uint32_t v) {
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1)
+    asm("{\n .reg .u32 t;\n .reg .pred p;\n shfl.sync.up.b32 t|p, %0, %1, 0, 0xffffffff;\n"
+        " @p add.u32 %0, %0, t;\n}"
+        : "+r"(v)
+        : "r"(d));
+  return v;
+}
+
+// Value placement: when (m & bit) != 0, store v at shared address a and
+// advance a by one element; a bit test, a predicated store and a predicated
+// add.
+__device__ __forceinline__ void place16(uint32_t &a, uint32_t m, uint32_t bit, uint32_t v) {
+  asm volatile(
+      "{\n .reg .pred p;\n .reg .b32 t;\n and.b32 t, %1, %2;\n setp.ne.u32 p, t, 0;\n"
+      " @p st.shared.u16 [%0], %3;\n @p add.u32 %0, %0, 2;\n}"
+      : "+r"(a)
+      : "r"(m), "r"(bit), "h"((unsigned short)v));
+}
+__device__ __forceinline__ void place8(uint32_t &a, uint32_t m, uint32_t bit, uint32_t v) {
+  asm volatile(
+      "{\n .reg .pred p;\n .reg .b32 t;\n and.b32 t, %1, %2;\n setp.ne.u32 p, t, 0;\n"
+      " @p st.shared.u8 [%0], %3;\n @p add.u32 %0, %0, 1;\n}"
+      : "+r"(a)
+      : "r"(m), "r"(bit), "h"((unsigned short)(v & 0xFFu)));
+}
+
+template <int DT_IN, bool QUANT, bool PACK, int TPP_, int NW, int D, int A>
+__global__ void __launch_bounds__(NW * 32, 2)
+    onepass_kernel(const __grid_constant__ CUtensorMap tmap, const CompressParams P) {
+  using O = Onepass<DT_IN, QUANT, TPP_, NW, D, A>;
+  using C = typename O::C;
+  constexpr int TPP = O::TPP, RW = O::RW, NS = O::NS;
+  extern __shared__ __align__(128) uint8_t smem_dyn[];
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem_dyn + O::OFF_BAR);
+  uint32_t *s_meta = reinterpret_cast<uint32_t *>(smem_dyn + O::OFF_META);
+  __shared__ uint32_t s_sum[2];  // per round parity: sum of the flush's counts
+  __shared__ long long s_off0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long G = gridDim.x, b = blockIdx.x, nparts = P.num_parts;
+
+  // Thread 0 fetches partition `part` into input stage `st`.
+  auto fetch = [&](long long part, int st) {
+    uint8_t *dst = smem_dyn + (size_t)st * O::IN_BYTES;
+    const uint32_t t0 = (uint32_t)(part * TPP), gn = (uint32_t)P.grid_n;  // num_tiles < 2^31
+    const int nt = (int)min((long long)TPP, P.num_tiles - (long long)t0);
+    mbar_expect_tx(&bars[st], (uint32_t)(nt * kTileNumel * O::EB));
+    uint32_t tm = t0 / gn, tn = t0 - tm * gn;
+    for (int j = 0; j < nt; ++j) {
+      tma_load_tile(dst + j * kTileNumel * O::EB, &tmap, (int)(tn * kTileN), (int)(tm * kTileM),
+                    &bars[st]);
+      if (++tn == gn) { tn = 0; ++tm; }
+    }
+  };
+
+  if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    long long off = 0;
+    if (P.arena_offset) {
+      off = *P.arena_offset;
+      if (PACK) off = (off + 7) / 8 * 8;  // functions.py:78-81
+    }
+    s_off0 = off;
+    s_sum[0] = 0;
+    s_sum[1] = 0;
+    __threadfence();  // the arena-offset read precedes every count this CTA publishes
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int i = 0; i < A; ++i)
+      if (i * G + b < nparts) fetch(i * G + b, i);
+
+  const float qs = QUANT ? *P.qscale : 1.f;
+  const float qr = QUANT ? __frcp_rn(qs) : 1.f;
+  long long known_end = 0, known = -1;  // end (count) through this CTA's last flushed partition
+  for (long long r = 0;; ++r) {
+    const long long p = r * G + b;
+    const long long q = p - (long long)D * G;
+    if (q >= nparts) break;
+    if (tid == 0) {
+      const long long pf = p + (long long)A * G;
+      // the stage's last reads were ordered by the round's closing barrier
+      if (pf < nparts) fetch(pf, (int)((r + A) % NS));
+    }
+    // 2. counts of the partitions between this CTA's last flushed one and q
+    //    (G - 1 of them; a thread reads at most kCv)
+    constexpr int kCv = 2;
+    uint32_t cv[kCv];
+#pragma unroll
+    for (int i = 0; i < kCv; ++i) {
+      const long long ci = known + 1 + tid + (long long)i * NW * 32;
+      cv[i] = (q >= 0 && ci < q) ? ld_relaxed_u32(P.counts_ws + ci) : 1u;
+    }
+    // 3. compact partition p in place
+    if (p < nparts) {
+      const int st = (int)(r % NS);
+      {
+        bool ok = false;
+        for (uint32_t n = 0; n < kMaxPolls && !(ok = mbar_try_wait(&bars[st], (uint32_t)((r / NS) & 1))); ++n) {
+        }
+        if (!ok && tid == 0) status_or(P.status, BS_STATUS_TIMEOUT);
+      }
+      uint8_t *stage = smem_dyn + (size_t)st * O::IN_BYTES;
+      uint32_t *meta = s_meta + st * O::META;
+      const int rho0 = warp * RW;  // first partition row of this warp
+      const int j = rho0 / kTileM;  // its tile
+      const long long tile = p * TPP + j;
+      // lane: 8 consecutive elements (16 B of bf16 / 8 B of fp8) of row
+      // rho0 + 4s + lane / 8 in step s; its 8 mask bits are exactly one
+      // bitmask byte.  All of a warp's rows are read before the barrier
+      // below, after which values are written in place at their
+      // partition-wide positions (never past the element they came from).
+      constexpr int S = RW / 4;
+      constexpr int VW = O::EB == 2 ? 4 : 2;  // input words per lane and step
+      uint32_t v[S][VW], m[S], ex[S];
+      uint32_t wtot = 0;
+      const int sub = lane >> 3, c8 = lane & 7;
+      const bool valid = tile < P.num_tiles;  // warp-uniform
+      if (valid) {
+        uint8_t *bm = P.bitmask + (p * TPP * kTileM + rho0 + sub) * 8 + c8;
+#pragma unroll
+        for (int s4 = 0; s4 < S; ++s4) {
+          const uint8_t *src = stage + ((rho0 + 4 * s4 + sub) * kTileN + 8 * c8) * O::EB;
+          if constexpr (VW == 4) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(src);
+            v[s4][0] = w.x; v[s4][1] = w.y; v[s4][2] = w.z; v[s4][3] = w.w;
+          } else {
+            const uint2 w = *reinterpret_cast<const uint2 *>(src);
+            v[s4][0] = w.x; v[s4][1] = w.y;
+          }
+        }
+#pragma unroll
+        for (int s4 = 0; s4 < S; ++s4) {
+          if constexpr (QUANT) {
+            uint32_t qw[2] = {0, 0};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t qq =
+                  e4m3x2_bits(div_round_bf16(bf16_bits_to_f32(v[s4][i] & 0xFFFFu), qs, qr),
+                              div_round_bf16(bf16_bits_to_f32(v[s4][i] >> 16), qs, qr));
+              qw[i >> 1] |= qq << (16 * (i & 1));
+            }
+            v[s4][0] = qw[0]; v[s4][1] = qw[1];
+            if (P.qout) {
+              const long long tm = tile / P.grid_n, tn = tile - tm * P.grid_n;
+              const long long gcol = tn * kTileN + 8 * c8;
+              const long long grow = tm * kTileM + (rho0 + 4 * s4 + sub - j * kTileM);
+              if (grow < P.M) {
+                uint8_t *qo = P.qout + grow * P.N + gcol;
+                if (P.qout_vec && gcol + 8 <= P.N) {
+                  *reinterpret_cast<uint2 *>(qo) = make_uint2(qw[0], qw[1]);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 8; ++i)
+                    if (gcol + i < P.N) qo[i] = (uint8_t)(qw[i >> 2] >> (8 * (i & 3)));
+                }
+              }
+            }
+          }
+          uint32_t mm;
+          if constexpr (C::SB == 2) {
+            mm = mask_bf16x8(v[s4]);
+          } else {
+            const uint32_t w2[2] = {v[s4][0], v[s4][1]};
+            mm = mask_of_words<C::SDT, 2>(w2);
+          }
+          m[s4] = mm;
+          const uint32_t c = __popc(mm);
+          const uint32_t incl = warp_scan_pred(c);
+          ex[s4] = wtot + incl - c;
+          wtot += __shfl_sync(0xFFFFFFFFu, incl, 31);
+          bm[s4 * 32] = (uint8_t)mm;
+        }
+      }
+      if (lane == 0) meta[warp] = wtot;
+      __syncthreads();  // all rows read; warp counts published
+      if (valid && P.vals != nullptr) {
+        const uint32_t t = lane < warp ? meta[lane] : 0u;
+        const uint32_t wex = __reduce_add_sync(0xFFFFFFFFu, t);
+        const uint32_t base_addr = smem_addr(stage);
+#pragma unroll
+        for (int s4 = 0; s4 < S; ++s4) {
+          uint32_t a = base_addr + (wex + ex[s4]) * C::SB;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if constexpr (C::SB == 2) place16(a, m[s4], 1u << i, v[s4][i >> 1] >> (16 * (i & 1)));
+            else place8(a, m[s4], 1u << i, v[s4][i >> 2] >> (8 * (i & 3)));
+          }
+        }
+      }
+      if (tid == 0) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int t = 0; t < TPP; ++t) {
+#pragma unroll
+          for (int w = t * (kTileM / RW); w < (t + 1) * (kTileM / RW); ++w) acc += meta[w];
+          meta[NW + t] = acc;  // inclusive count after tile t
+        }
+        meta[NW + TPP] = acc;
+        st_relaxed_u32(P.counts_ws + p, acc + 1);
+      }
+    }
+
+    // 4. flush partition q
+    if (q >= 0) {
+      const int slot = (int)((r - D) % NS);
+      const uint32_t *meta = s_meta + slot * O::META;  // written before an earlier barrier
+      bool late = false;
+      uint32_t sum = 0;
+#pragma unroll
+      for (int i = 0; i < kCv; ++i) {
+        const long long ci = known + 1 + tid + (long long)i * NW * 32;
+        for (uint32_t n = 0; cv[i] == 0; ++n) {  // published yet?  (0 only for ci < q)
+          if (n >= kMaxPolls) { late = true; cv[i] = 1; break; }
+          __nanosleep(64);
+          cv[i] = ld_relaxed_u32(P.counts_ws + ci);
+        }
+        sum += cv[i] - 1;
+      }
+      if (late) status_or(P.status, BS_STATUS_TIMEOUT);
+      sum = __reduce_add_sync(0xFFFFFFFFu, sum);
+      if (lane == 0 && sum) atomicAdd(&s_sum[r & 1], sum);
+      __syncthreads();
+      long long base = known_end + s_sum[r & 1];
+      const uint32_t total = meta[NW + TPP];
+      const long long off0 = s_off0;
+      if (tid < TPP && q * TPP + tid < P.num_tiles)
+        P.prefix[q * TPP + tid + 1] = (uint32_t)(base + meta[NW + tid]);
+      if (tid == 0) {
+        if (q == 0) P.prefix[0] = 0;
+        if (q == nparts - 1) {
+          __threadfence();
+          const long long nnz = base + total;
+          if (P.arena_offset) *P.arena_offset = off0 + nnz;
+          if (P.vals_offset_out) *P.vals_offset_out = off0;
+          if (P.nnz_out) *P.nnz_out = nnz;
+        }
+      }
+      if (P.vals != nullptr) {
+        const uint8_t *vs = smem_dyn + (size_t)slot * O::IN_BYTES;
+        if constexpr (PACK)
+          emit_values<C, true, false, NW * 32>(P, vs, off0 + base, total,
+                                               q == nparts - 1 && P.arena_offset == nullptr, tid);
+        else
+          emit_words<C, NW * 32>(P, vs, off0 + base, total, tid);
+      }
+      known_end = base + total;
+      known = q;
+    }
+    if (tid == 0) s_sum[(r + 1) & 1] = 0;  // next round's accumulator (read this round: the other)
+    __syncthreads();  // stage (r-D) % NS and s_sum are free again
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 // Tiles per partition (a partition is 32 KB of bf16 / fp8 input, 8 KB per
 // thread-slot row); MODE 1 / 2 use small partitions.
 constexpr int tpp_for(int eb, int mode) {
   return mode == 0 ? (eb == 1 ? 8 : 4) : (eb == 1 ? 2 : 1);
+}
+
+// Resident CTAs of `kernel` on this device: cached per kernel and device
+// (the first query also raises the kernel's dynamic shared-memory limit).
+static int resident_ctas(const void *kernel, size_t smem, int threads) {
+  constexpr int kMaxDev = 64, kMaxKernels = 64;
+  static std::mutex mu;
+  static const void *keys[kMaxKernels] = {};
+  static int cache[kMaxKernels][kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  int k = 0;
+  while (k < kMaxKernels && keys[k] && keys[k] != kernel) ++k;
+  if (k == kMaxKernels) return 0;
+  keys[k] = kernel;
+  if (!cache[k][dev]) {
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) !=
+        cudaSuccess)
+      return 0;
+    cache[k][dev] = sms * per_sm;
+  }
+  return cache[k][dev];
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver, through the runtime (no -lcuda).
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+constexpr int kNotApplicable = -1;
+
+
+// The one-pass kernel, or kNotApplicable when the input cannot be read by
+// TMA (base not 16-byte aligned, row stride not a multiple of 16 bytes,
+// sizes past the tensor map's limits) or raw values are not 16-byte aligned.
+// TPP2: tiles per partition for 2-byte inputs (1-byte inputs take twice as
+// many while a warp's rows stay within one tile); NW warps per CTA; flush
+// lag D; prefetch depth A.
+template <int DT_IN, int TPP2, int NW>
+constexpr int onepass_tpp() {
+  return Elt<DT_IN>::bytes == 1 && 2 * TPP2 * kTileM / NW <= kTileM ? 2 * TPP2 : TPP2;
+}
+
+template <int DT_IN, bool QUANT, bool PACK, int TPP2, int NW, int D, int A>
+static int launch_onepass(const CompressParams &P, cudaStream_t st) {
+  constexpr int TPP = onepass_tpp<DT_IN, TPP2, NW>();
+  using O = Onepass<DT_IN, QUANT, TPP, NW, D, A>;
+  if (getenv("BS_COMPRESS_TWO_KERNELS")) return kNotApplicable;
+  const uint64_t row_bytes = (uint64_t)P.ld * O::EB;
+  if ((reinterpret_cast<uintptr_t>(P.dense) & 15) || (row_bytes & 15) ||
+      (!PACK && (reinterpret_cast<uintptr_t>(P.vals) & 15)) || P.M >= ((int64_t)1 << 31) ||
+      P.N >= ((int64_t)1 << 31) || row_bytes >= ((uint64_t)1 << 40))
+    return kNotApplicable;
+  EncodeTiledFn encode = encode_tiled();
+  if (!encode) return kNotApplicable;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)P.N, (cuuint64_t)P.M};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {kTileN, kTileM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType ty =
+      O::EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  if (encode(&map, ty, 2, const_cast<uint8_t *>(P.dense), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return kNotApplicable;
+  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A>;
+  int resident = resident_ctas(reinterpret_cast<const void *>(kernel), O::SMEM, NW * 32);
+  if (resident <= 0) return BS_ERR_LAUNCH;
+  // a flush reads the counts of G - 1 partitions, at most 2 per thread
+  if (resident > 2 * NW * 32 + 1) resident = 2 * NW * 32 + 1;
+  CompressParams Q = P;
+  Q.num_parts = (P.num_tiles + O::TPP - 1) / O::TPP;
+  if (cudaMemsetAsync(Q.counts_ws, 0, (size_t)Q.num_parts * sizeof(uint32_t), st) !=
+      cudaSuccess)
+    return BS_ERR_LAUNCH;
+  // Every CTA waits on counts that others publish: all must be resident,
+  // which a cooperative launch guarantees (or refuses).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(Q.num_parts < resident ? Q.num_parts : resident));
+  cfg.blockDim = dim3(NW * 32);
+  cfg.dynamicSmemBytes = O::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, map, Q) != cudaSuccess) return BS_ERR_LAUNCH;
+  return BS_OK;
 }
 
 template <int DT_IN, bool QUANT, bool PACK, int MODE>
@@ -547,6 +1107,10 @@ static int launch_t(const CompressParams &P, cudaStream_t st) {
   static_assert(smem <= 48 * 1024, "stage fits the default dynamic shared memory");
   const unsigned grid = (unsigned)P.num_parts;
   if constexpr (MODE == 0) {
+    if constexpr (DT_IN != BS_F32) {
+      const int rc = launch_onepass<DT_IN, QUANT, PACK, 4, 8, 1, 1>(P, st);
+      if (rc != kNotApplicable) return rc;
+    }
     const size_t nseg = (size_t)((P.num_parts + kSeg - 1) / kSeg);
     if (cudaMemsetAsync(P.seg_ws, 0, nseg * sizeof(unsigned long long), st) != cudaSuccess)
       return BS_ERR_LAUNCH;
@@ -614,9 +1178,9 @@ using namespace bs;
 
 extern "C" size_t bs_compress_workspace_bytes(int64_t num_tiles) {
   if (num_tiles < 0) num_tiles = 0;
-  // Per partition a 4-byte count and per 256 partitions an 8-byte total; a
-  // partition holds at least four tiles.
-  return sizeof(WsHeader) + 8 * ((size_t)num_tiles / 1024 + 1) + (size_t)num_tiles + 4;
+  // Per 256 partitions an 8-byte total and per partition a 4-byte count; a
+  // partition holds at least two tiles.
+  return sizeof(WsHeader) + 8 * ((size_t)num_tiles / 512 + 1) + 2 * (size_t)num_tiles + 4;
 }
 
 extern "C" int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N, int64_t ld,
@@ -636,7 +1200,7 @@ extern "C" int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N
   if (vals_capacity < 0) return BS_ERR_CAPACITY;
   if (pack_sbit && vals && (reinterpret_cast<uintptr_t>(vals) & 3)) return BS_ERR_ALIGN;
   if (pack_sbit && (vals_capacity & 3)) return BS_ERR_ALIGN;
-  if (workspace_bytes < bs_compress_workspace_bytes(P.num_parts)) return BS_ERR_WORKSPACE;
+  if (workspace_bytes < bs_compress_workspace_bytes(P.num_tiles)) return BS_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 15) return BS_ERR_ALIGN;
   P.qscale = quant_scale;
   P.qout = quant_out;

@@ -341,7 +341,6 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
     const int c = s * kThreads + tid;
     const int j = c / G::CPT, cc = c % G::CPT;
     if (j >= nt) continue;
-    const int64_t tile = pid0 + j;
     const int row = cc / G::CPR, colc = cc % G::CPR;
     int64_t tr, tc;
     pp.pos(j, tr, tc);

@@ -50,7 +50,7 @@ enum {
 /* Device status bits (OR-ed into *status by kernels). */
 enum {
   BS_STATUS_CAPACITY = 1, /* vals storage too small: writes were clipped    */
-  BS_STATUS_TIMEOUT = 2   /* reserved: a bounded device-side wait gave up    */
+  BS_STATUS_TIMEOUT = 2   /* a bounded device-side wait gave up (results invalid) */
 };
 
 /* Element types.  Codes 1/2 equal the reference's pack codecs
@@ -72,16 +72,21 @@ enum {
 const char *bs_version(void);
 
 /* Bytes of workspace bs_compress needs for `num_tiles` tiles (per-partition
- * counts and running totals; no initial contents are required).  Launches
+ * counts and running totals, about 2 bytes per tile; no initial contents are
+ * required).  Launches
  * that may overlap on the GPU (different streams) must use different
  * workspaces. */
 size_t bs_compress_workspace_bytes(int64_t num_tiles);
 
 /* Fused compress: dense [M, N] (row stride `ld` elements) -> bitmask
- * uint8[T*512], prefix uint32[T+1] and the compacted values: a count kernel
- * (bitmask, per-partition counts) followed by a compact kernel (bases,
- * prefix, values) that re-reads the input in reverse order so its most
- * recently counted part comes from L2; no CTA waits on another.
+ * uint8[T*512], prefix uint32[T+1] and the compacted values in one pass
+ * over the input: a persistent kernel (TMA-fed, values compacted in shared
+ * memory, bases from per-partition counts published by the other CTAs,
+ * waits bounded) when the input base is 16-byte aligned, the row stride is a
+ * multiple of 16 bytes and raw `vals` is 16-byte aligned; otherwise (and for
+ * BS_F32 input) a count kernel followed by a compact kernel that re-reads
+ * the input in reverse order so its most recently counted part comes from
+ * L2.
  *
  * Replaces the whole of dense_to_tilesparse (lib_sparse/src/functions.py:55-99):
  * tile_pack (lib_sparse/src/triton_operators.py:21-33), the torch.cumsum

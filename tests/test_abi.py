@@ -31,7 +31,7 @@ def test_version_and_workspace_size():
     assert b"sm_100a" in lib.bs_version()
     assert lib.bs_compress_workspace_bytes(0) >= 16
     sizes = [lib.bs_compress_workspace_bytes(t) for t in (0, 1, 1000, 65536, 1 << 20)]
-    assert sizes == sorted(sizes) and sizes[-1] < 2 * (1 << 20) + 4096
+    assert sizes == sorted(sizes) and sizes[-1] < 3 * (1 << 20)  # ~2 bytes per tile
 
 
 @pytest.mark.parametrize("call, code", [

@@ -288,3 +288,61 @@ def test_transpose_b8(rows, cols):
     assert torch.equal(_transposed_b8(x), x.T.contiguous())
     xf = x.view(torch.float8_e4m3fn)
     assert torch.equal(_transposed_b8(xf).view(torch.uint8), x.T.contiguous())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float8_e4m3fn, torch.float8_e5m2])
+def test_every_bit_pattern(dtype):
+    """Every bf16 / fp8 bit pattern (shuffled, several copies) through
+    compress and reconstruct against the oracle: the positive test must hold
+    for subnormals, -0, NaNs and infinities alike."""
+    odt = {torch.bfloat16: O.DT_BF16, torch.float8_e4m3fn: O.DT_E4M3,
+           torch.float8_e5m2: O.DT_E5M2}[dtype]
+    rng = np.random.default_rng(5)
+    if dtype == torch.bfloat16:
+        pats = np.tile(np.arange(65536, dtype=np.uint32).astype(np.uint16), 2)
+        shape = (512, 256)
+    else:
+        pats = np.tile(np.arange(256, dtype=np.uint32).astype(np.uint8), 64)
+        shape = (128, 128)
+    pats = rng.permutation(pats).reshape(shape)
+    xd = to_dev(pats, odt, shape)
+    for pack in (False, True):
+        sp = dense_to_tilesparse(xd, None, None, pack)
+        osp = O.dense_to_tilesparse(pats, odt, None, pack)
+        np.testing.assert_array_equal(bits(sp.bitmask), osp.bitmask)
+        np.testing.assert_array_equal(bits(sp.prefix), osp.prefix)
+        np.testing.assert_array_equal(bits(sp.vals), osp.vals)
+        np.testing.assert_array_equal(bits(_reconstruct(sp)), O.reconstruct(osp))
+    B.check_status()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("pack", [False, True])
+def test_large_arena_odd_offsets(dtype, pack):
+    """Tensors of many partitions per CTA compressed one after another into a
+    TensorBuffer whose offset starts odd: bases across CTAs and rounds, and
+    value ranges that start and end inside 16-byte vectors."""
+    odt = {torch.bfloat16: O.DT_BF16, torch.float8_e4m3fn: O.DT_E4M3}[dtype]
+    g = torch.Generator().manual_seed(11)
+    shapes = ((2048, 4096), (1000, 3000), (64, 64 * 700))
+    xs = []
+    for i, (M, N) in enumerate(shapes):
+        x = (torch.randn(M, N, generator=g) + 0.6 * (i - 1)).relu().to(dtype)
+        xs.append(x)
+    elt = 1 if dtype != torch.bfloat16 else 2
+    total = sum(x.numel() for x in xs) + 64
+    size = (total * bits_per_value(dtype) + 7) // 8 + 64 if pack else total * elt
+    buf = TensorBuffer(size, device="cuda", dtype=dtype, pack_sbit=pack)
+    arena = O.Arena(size, odt, pack)
+    start = 3
+    buf.offset.fill_(start)
+    arena.offset = start
+    for x in xs:
+        sp = dense_to_tilesparse(x.cuda(), None, buf, pack)
+        osp = O.dense_to_tilesparse(bits(x), odt, arena, pack)
+        np.testing.assert_array_equal(bits(sp.bitmask), osp.bitmask)
+        np.testing.assert_array_equal(bits(sp.prefix), osp.prefix)
+        assert int(sp.vals_offset.reshape(-1)[0].item()) == osp.vals_offset
+    assert int(buf.offset.item()) == arena.offset
+    np.testing.assert_array_equal(bits(buf.vals), arena.vals)
+    B.check_status()
