@@ -890,15 +890,37 @@ __global__ void __launch_bounds__(NW * 32, 2)
             mm = mask_of_words<C::SDT, 2>(w2);
           }
           m[s4] = mm;
-          const uint32_t c = __popc(mm);
-          const uint32_t incl = warp_scan_pred(c);
-          ex[s4] = wtot + incl - c;
-          wtot += __shfl_sync(0xFFFFFFFFu, incl, 31);
           bm[s4 * 32] = (uint8_t)mm;
+        }
+        // Lane counts of three steps share one scan: 10-bit fields (a
+        // step's inclusive count is at most 256, so fields never carry).
+#pragma unroll
+        for (int g = 0; g < S; g += 3) {
+          uint32_t packed = 0;
+#pragma unroll
+          for (int k = 0; k < 3 && g + k < S; ++k) packed |= (uint32_t)__popc(m[g + k]) << (10 * k);
+          const uint32_t incl = warp_scan_pred(packed);
+          const uint32_t tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+#pragma unroll
+          for (int k = 0; k < 3 && g + k < S; ++k) {
+            ex[g + k] = wtot + ((incl - packed) >> (10 * k) & 0x3FFu);
+            wtot += (tot >> (10 * k)) & 0x3FFu;
+          }
         }
       }
       if (lane == 0) meta[warp] = wtot;
       __syncthreads();  // all rows read; warp counts published
+      if (tid == 0) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int t = 0; t < TPP; ++t) {
+#pragma unroll
+          for (int w = t * (kTileM / RW); w < (t + 1) * (kTileM / RW); ++w) acc += meta[w];
+          meta[NW + t] = acc;  // inclusive count after tile t
+        }
+        meta[NW + TPP] = acc;
+        st_relaxed_u32(P.counts_ws + p, acc + 1);
+      }
       if (valid && P.vals != nullptr) {
         const uint32_t t = lane < warp ? meta[lane] : 0u;
         const uint32_t wex = __reduce_add_sync(0xFFFFFFFFu, t);
@@ -912,17 +934,6 @@ __global__ void __launch_bounds__(NW * 32, 2)
             else place8(a, m[s4], 1u << i, v[s4][i >> 2] >> (8 * (i & 3)));
           }
         }
-      }
-      if (tid == 0) {
-        uint32_t acc = 0;
-#pragma unroll
-        for (int t = 0; t < TPP; ++t) {
-#pragma unroll
-          for (int w = t * (kTileM / RW); w < (t + 1) * (kTileM / RW); ++w) acc += meta[w];
-          meta[NW + t] = acc;  // inclusive count after tile t
-        }
-        meta[NW + TPP] = acc;
-        st_relaxed_u32(P.counts_ws + p, acc + 1);
       }
     }
 
