@@ -343,7 +343,7 @@ def run_ours(args):
     comp_alg = compress_bytes(M, N, statistics.mean(nnz))
     achieved = comp_alg / (comp_avg * 1e-3) / 1e9
     unp_avg = statistics.mean(unp_ms)
-    traffic = ncu_traffic("compress_kernel")
+    traffic = ncu_traffic("onepass_kernel")
 
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
