@@ -253,9 +253,24 @@ def mlp_bench(cfg, steps, warmup, device):
         y = h @ params[2].T + params[4]
         y.backward(gy)
 
+    def graphed(fn):
+        """fn captured once in a CUDA graph (launch overhead removed)."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g.replay
+
     out = {}
     for name, fn in (("sparse", sparse_step), ("sparse_arena", lambda: sparse_step(arena)),
-                     ("dense", dense_step)):
+                     ("dense", dense_step),
+                     ("sparse_arena_graph", graphed(lambda: sparse_step(arena))),
+                     ("dense_graph", graphed(dense_step))):
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
@@ -276,6 +291,8 @@ def mlp_bench(cfg, steps, warmup, device):
     out["speedup_vs_dense"] = out["sparse"]["tokens_per_s"] / out["dense"]["tokens_per_s"]
     out["speedup_arena_vs_dense"] = (out["sparse_arena"]["tokens_per_s"]
                                      / out["dense"]["tokens_per_s"])
+    out["speedup_graph_vs_dense_graph"] = (out["sparse_arena_graph"]["tokens_per_s"]
+                                           / out["dense_graph"]["tokens_per_s"])
     return out
 
 

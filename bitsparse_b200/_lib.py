@@ -39,6 +39,8 @@ _SIGS = {
                                    _i32, _vp, _vp, _vp, _vp, _vp]),
     "bs_compress_noalloc_max_tiles": (_sz, []),
     "bs_transpose_b8": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
+    "bs_gemm_bf16_mask": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
+                                 _vp]),
     "bs_tile_pack": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),
     "bs_compact_vals": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _i64, _i32, _vp, _vp,
                                _vp]),

@@ -1,0 +1,427 @@
+// K3 -- tcgen05 GEMM with the ReLU mask fused into its epilogue.
+//
+//   C[M, N] = (A[M, K] . B[K, N]) (.) mask        (bf16 in, fp32 accumulate, bf16 out)
+//
+// A is row-major (K contiguous: "K-major"), B is row-major (N contiguous:
+// "MN-major"), both read by TMA with the 128-byte swizzle into the layouts
+// tcgen05.mma reads directly.  mask (optional) is the bitmask of a
+// bitsparse [M, N] tensor (64 x 64 tiles, grid-row-major, LSB-first): an
+// output element whose bit is clear is written as +0.  This is the
+// backward of ReluLinear (lib_sparse/layers.py:38-51, gradient half of
+// mask_with_bitmask_ in lib_sparse/src/triton_kernels.py:249-276):
+// grad_z = (grad_y @ W) masked by h > 0, without the dense grad_h ever
+// reaching HBM.
+//
+// Persistent: one CTA per SM walks a static schedule of 128 x 256 tiles of
+// C (M tile = the 128 TMEM lanes, N tile = 256 fp32 TMEM columns), with two
+// accumulators in TMEM (all 512 columns) so that the epilogue of one tile
+// overlaps the main loop of the next:
+//   warp 0      TMA producer: for each 64-wide K block of each tile, A box
+//               [128 x 64] and four B boxes [64 x 64] into the next of 4
+//               stages (48 KB);
+//   warp 1      MMA issuer (one thread): four tcgen05.mma (K = 16 each) per
+//               stage, tcgen05.commit to the stage's "empty" barrier, and
+//               after a tile's last stage to that accumulator's "full"
+//               barrier; it also allocates and frees the TMEM columns;
+//   warps 2..5  epilogue: the row's bitmask words are fetched before the
+//               wait; tcgen05.ld of 32 columns at a time from the warp's
+//               TMEM lane quarter (warp % 4), bf16 rounding, masking, 16-byte
+//               stores; then the accumulator is handed back to the MMA warp.
+// All mbarrier waits are bounded (BS_STATUS_TIMEOUT); the producer waits
+// for its own copies before the CTA exits; TMEM is always freed.
+#include "common.cuh"
+
+#include <cuda.h>  // CUtensorMap (types only; the encoder comes through the runtime)
+
+#include <mutex>
+
+namespace bs {
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;  // 16 KB
+constexpr int kBBytes = kBK * kBN * 2;  // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kThreadsG = 192;  // 6 warps
+constexpr uint32_t kTmemCols = 256;
+constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kStages * kStageBytes + 256;
+
+struct GemmParams {
+  uint8_t *C;
+  int64_t M, N, K, ldc;
+  const uint8_t *mask;  // bitmask of a bitsparse [M, N] tensor, or null
+  int64_t mask_grid_n;  // its tile columns: ceil(N / 64)
+  int c_vec;            // C base and row stride allow 16-byte stores
+  int32_t *status;
+};
+
+__device__ __forceinline__ uint32_t saddr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the status word flagged) if the phase never came.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_t *status) {
+  for (uint32_t n = 0; n < kMaxPolls; ++n)
+    if (mbar_try_wait(bar, parity)) return true;
+  status_or(status, BS_STATUS_TIMEOUT);
+  return false;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(saddr(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05): start address, leading and
+// stride byte offsets (all >> 4), version 1, layout 2 = 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, A
+// K-major, B MN-major, N = kBN, M = kBM.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) |
+                            ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          saddr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Tile t of the static schedule -> (m block, n block): groups of kGroupM
+// row blocks sweep the column blocks together, so neighbouring CTAs share
+// B columns and A rows in L2.
+constexpr int kGroupM = 8;
+__device__ __forceinline__ void tile_coords(int64_t t, int64_t mt, int64_t nt, int64_t &mb,
+                                            int64_t &nb) {
+  const int64_t per_group = (int64_t)kGroupM * nt;
+  const int64_t g = t / per_group, first_m = g * kGroupM;
+  const int64_t gm = mt - first_m < kGroupM ? mt - first_m : kGroupM;
+  const int64_t r = t - g * per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+template <bool MASK>
+__global__ void __launch_bounds__(kThreadsG, 1)
+    gemm_mask_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, const GemmParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)kStages * kStageBytes);
+  uint64_t *empty = full + kStages;
+  uint64_t *acc_full = empty + kStages;  // [2]: MMA -> epilogue
+  uint64_t *acc_empty = acc_full + 2;    // [2]: epilogue -> MMA
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (int)((P.K + kBK - 1) / kBK);
+  const int64_t mt = (P.M + kBM - 1) / kBM, nt = (P.N + kBN - 1) / kBN;
+  const int64_t ntiles = mt * nt;
+
+  if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // the whole warp allocates (sync.aligned)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(tmem_slot)),
+                 "r"(2 * kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int64_t it = 0;  // global k-block counter: stage it % kStages, phase it / kStages
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int64_t mb, nb;
+        tile_coords(t, mt, nt, mb, nb);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % kStages);
+          if (it >= kStages &&
+              !mbar_wait(&empty[s], (uint32_t)((it / kStages - 1) & 1), P.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t *a = smem + (size_t)s * kStageBytes;
+          uint8_t *b = a + kABytes;
+          mbar_expect_tx(&full[s], kStageBytes);
+          tma_load_2d(a, &tmA, kb * kBK, (int)(mb * kBM), &full[s]);
+#pragma unroll
+          for (int j = 0; j < kBN / 64; ++j)
+            tma_load_2d(b + j * (kBK * 64 * 2), &tmB, (int)(nb * kBN) + 64 * j, kb * kBK,
+                        &full[s]);
+        }
+      }
+      // every copy this CTA issued has landed before it may exit
+      for (int64_t i = it - kStages < 0 ? 0 : it - kStages; i < it; ++i)
+        mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1), P.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int64_t it = 0;
+      int j = 0;  // local tile counter: accumulator buffer j & 1, use j >> 1
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++j) {
+        const int buf = j & 1;
+        if (j >= 2 && !mbar_wait(&acc_empty[buf], (uint32_t)(((j >> 1) - 1) & 1), P.status))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * kTmemCols);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % kStages);
+          if (!mbar_wait(&full[s], (uint32_t)((it / kStages) & 1), P.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = saddr(smem + (size_t)s * kStageBytes);
+          const uint32_t b = a + kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // A: K-major, 128-byte rows, 8-row atoms 1024 B apart; +32 B per K=16.
+            // B: MN-major, 64-column atoms 8 KB apart (LBO), 8-row K groups
+            //    1024 B apart (SBO); +2048 B per K=16.
+            const uint64_t ad = smem_desc(a + 32 * k, 16, 1024);
+            const uint64_t bd = smem_desc(b + 2048 * k, kBK * 64 * 2, 1024);
+            mma_bf16(d, ad, bd, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);  // stage free once these MMAs have read it
+        }
+        mma_commit(&acc_full[buf]);  // accumulator j complete
+      }
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (rows of the tile)
+    const int q = warp & 3;
+    int j = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
+      int64_t mb, nb;
+      tile_coords(t, mt, nt, mb, nb);
+      const int64_t m = mb * kBM + 32 * q + lane, n0 = nb * kBN;
+      // this row's mask words for the tile's 256 columns, fetched before the wait
+      uint64_t keep[kBN / 64];
+#pragma unroll
+      for (int i = 0; i < kBN / 64; ++i) {
+        keep[i] = ~0ull;
+        if constexpr (MASK) {
+          if (m < P.M && n0 + 64 * i < P.N)
+            keep[i] = *reinterpret_cast<const uint64_t *>(
+                P.mask + ((m >> 6) * P.mask_grid_n + (n0 >> 6) + i) * kTileBytes + (m & 63) * 8);
+        }
+      }
+      const int buf = j & 1;
+      const bool ok = mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), P.status);
+      tc_fence_after();
+      const uint32_t zero_guard = ok ? 0xFFFFu : 0u;  // a failed wait writes zeros
+      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTmemCols);
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + (uint32_t)(32 * c), r);
+        const int64_t n = n0 + 32 * c;
+        if (m >= P.M || n >= P.N) continue;
+        const uint32_t kw = (uint32_t)(keep[c >> 1] >> (32 * (c & 1)));
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          uint32_t lo = f32_to_bf16_bits(__uint_as_float(r[2 * i])) & zero_guard;
+          uint32_t hi = f32_to_bf16_bits(__uint_as_float(r[2 * i + 1])) & zero_guard;
+          lo &= 0u - ((kw >> (2 * i)) & 1u);
+          hi &= 0u - ((kw >> (2 * i + 1)) & 1u);
+          w[i] = lo | (hi << 16);
+        }
+        uint8_t *dst = P.C + (m * P.ldc + n) * 2;
+        if (P.c_vec && n + 32 <= P.N) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4 *>(dst)[i] =
+                make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        } else {
+          for (int i = 0; i < 32 && n + i < P.N; ++i)
+            reinterpret_cast<uint16_t *>(dst)[i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+        }
+      }
+      // this warp is done with accumulator buf
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * kTmemCols)
+                 : "memory");
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D bf16 tensor map: rows x cols (cols contiguous), box box_cols x box_rows,
+// 128-byte swizzle.
+bool make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld,
+              uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn encode = encode_tiled();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+                strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool MASK>
+int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &P,
+                cudaStream_t st) {
+  auto kernel = gemm_mask_kernel<MASK>;
+  static std::once_flag once[2];
+  static cudaError_t attr_err[2];
+  std::call_once(once[MASK], [&] {
+    attr_err[MASK] =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+  });
+  if (attr_err[MASK] != cudaSuccess) return BS_ERR_LAUNCH;
+  static int sms = [] {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 1;
+  }();
+  const int64_t tiles = ((P.M + kBM - 1) / kBM) * ((P.N + kBN - 1) / kBN);
+  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
+  kernel<<<grid, kThreadsG, kSmem, st>>>(ta, tb, P);
+  return cudaGetLastError() == cudaSuccess ? BS_OK : BS_ERR_LAUNCH;
+}
+
+}  // namespace
+}  // namespace bs
+
+using namespace bs;
+
+extern "C" int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int64_t ldb,
+                                 void *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                 const uint8_t *mask, int32_t *status, void *stream) {
+  if (M < 0 || N < 0 || K < 0) return BS_ERR_SHAPE;
+  if (M == 0 || N == 0) return BS_OK;
+  if (!A || !B || !C) return BS_ERR_ARG;
+  if (lda < K || ldb < N || ldc < N) return BS_ERR_SHAPE;
+  if (M >= ((int64_t)1 << 31) || N >= ((int64_t)1 << 31) || K >= ((int64_t)1 << 31))
+    return BS_ERR_TOO_LARGE;
+  // TMA: 16-byte aligned bases and row strides
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+      ((lda * 2) & 15) || ((ldb * 2) & 15))
+    return BS_ERR_ALIGN;
+  if (mask && (reinterpret_cast<uintptr_t>(mask) & 3)) return BS_ERR_ALIGN;
+  GemmParams P{};
+  P.C = static_cast<uint8_t *>(C);
+  P.M = M; P.N = N; P.K = K; P.ldc = ldc;
+  P.mask = mask;
+  P.mask_grid_n = (N + kTileN - 1) / kTileN;
+  P.c_vec = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((ldc * 2) % 16 == 0);
+  P.status = status;
+  CUtensorMap ta, tb;
+  if (K == 0) {  // empty reduction: C = 0
+    for (int64_t r = 0; r < M; ++r)
+      if (cudaMemsetAsync(static_cast<uint8_t *>(C) + r * ldc * 2, 0, (size_t)N * 2,
+                          static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return BS_ERR_LAUNCH;
+    return BS_OK;
+  }
+  if (!make_map(&ta, A, M, K, lda, kBK, kBM) || !make_map(&tb, B, K, N, ldb, 64, kBK))
+    return BS_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return mask ? launch_gemm<true>(ta, tb, P, st) : launch_gemm<false>(ta, tb, P, st);
+}

@@ -15,8 +15,34 @@ from .bitsparse import BitsparseTensor, TensorBuffer
 from .config import RELU2_SCALE
 from .fp8 import is_fp8, matmul, to_fp8
 from .src.functions import dense_to_tilesparse, relu_to_tilesparse_fp8
-from .src.operators import mask_with_bitmask_, relu2_grad_sparse_
+from .src.operators import mask_with_bitmask_, matmul_relu_mask, relu2_grad_sparse_
 from .src.sparse_matmul import AspB, AspRelu2B
+
+
+FUSED_MASK_MIN_K = 4096
+
+
+def _tma_ok(t: Tensor) -> bool:
+    """A bf16 matrix the tcgen05 GEMM can read with TMA: unit column stride,
+    16-byte aligned base and row stride."""
+    return (t.dtype == torch.bfloat16 and t.dim() == 2 and t.stride(1) == 1
+            and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0)
+
+
+def _relu_grad(grad_output: Tensor, W: Tensor, h: BitsparseTensor) -> Tensor:
+    """grad_z = (grad_output @ W) masked by h > 0 (lib_sparse/layers.py:47-51).
+
+    The tcgen05 GEMM with the mask in its epilogue (the dense grad_h never
+    reaches memory) when both operands can be read by TMA and the reduction
+    is long (K >= FUSED_MASK_MIN_K: measured on B200, it matches cuBLAS at
+    K = 8192 and trails it at K = 768, where cuBLAS's two-SM tiles read half
+    the operand bytes); else the cuBLAS GEMM followed by mask_with_bitmask_.
+    """
+    if not grad_output.is_contiguous():
+        grad_output = grad_output.contiguous()
+    if grad_output.shape[1] >= FUSED_MASK_MIN_K and _tma_ok(grad_output) and _tma_ok(W):
+        return matmul_relu_mask(grad_output, W, h)
+    return mask_with_bitmask_(matmul(grad_output, W, False), h)
 
 
 class ReluLinear(Function):
@@ -50,7 +76,9 @@ class ReluLinear(Function):
         else:
             scale = None
         grad_W2 = AspB(grad_output.T, h, A_scale=scale)
-        if needs_z:
+        if needs_z and not fp8:
+            grad_z = _relu_grad(grad_output, W, h)
+        elif needs_z:
             grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
             grad_z = mask_with_bitmask_(grad_h, h)
         else:

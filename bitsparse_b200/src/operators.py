@@ -245,3 +245,36 @@ def relu2_grad_sparse_(grad: Tensor, sparse_z: BitsparseTensor) -> Tensor:
               R.dtype_code(sparse_z.dtype), int(sparse_z.pack_sbit), R.ptr(scale),
               _stream(grad))
     return grad
+
+
+# ---------------------------------------------------------------------------
+# Tensor-core GEMM with the ReLU mask in its epilogue
+# ---------------------------------------------------------------------------
+def matmul_relu_mask(a: Tensor, b: Tensor, sparse: BitsparseTensor | None = None) -> Tensor:
+    """bf16 ``a [M, K] @ b [K, N]`` on the tcgen05 tensor cores (fp32
+    accumulation, bf16 result); with ``sparse`` (a bitsparse [M, N] tensor)
+    the elements whose bitmask bit is clear are written as 0.
+
+    ``matmul_relu_mask(grad_y, W2, h)`` equals ``mask_with_bitmask_(grad_y @
+    W2, h)`` (lib_sparse/layers.py:38-51) up to the accumulation order of the
+    GEMM, without the dense ``grad_y @ W2`` reaching memory.
+    """
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("matmul_relu_mask takes bfloat16 operands")
+    a, lda = _row_major(a, "a")
+    b, ldb = _row_major(b, "b")
+    M, K = a.shape
+    K2, N = b.shape
+    if K != K2:
+        raise ValueError(f"inner dimensions differ: {K} vs {K2}")
+    mask = 0
+    if sparse is not None:
+        if tuple(sparse.shape) != (M, N):
+            raise ValueError(f"mask shape {tuple(sparse.shape)} != output shape {(M, N)}")
+        _check_tiles(sparse.BLOCK_M, sparse.BLOCK_N)
+        mask = sparse.bitmask.data_ptr()
+    out = torch.empty((M, N), device=a.device, dtype=torch.bfloat16)
+    status = R.status_word(a.device)
+    _lib.call("bs_gemm_bf16_mask", a.data_ptr(), lda, b.data_ptr(), ldb, out.data_ptr(), N,
+              M, N, K, mask or None, status.data_ptr(), _stream(a))
+    return out

@@ -186,6 +186,20 @@ int bs_relu2_grad(void *grad, int grad_dtype, int64_t M, int64_t N, int64_t ld,
                   int store_dtype, int pack_sbit, const float *scale,
                   void *stream);
 
+/* C[M, N] = A[M, K] @ B[K, N] on the tcgen05 tensor cores (bf16 operands,
+ * fp32 accumulation, bf16 result rounded to nearest even), with the ReLU
+ * mask fused into the epilogue when `mask` != NULL: `mask` is the bitmask of
+ * a bitsparse [M, N] tensor and every element whose bit is clear is written
+ * as +0.  With the bitmask of the saved activation h this is the backward of
+ * ReluLinear, grad_z = (grad_y @ W2) masked by h > 0 (lib_sparse/layers.py:38-51
+ * followed by mask_with_bitmask_, lib_sparse/src/triton_kernels.py:249-276),
+ * without the dense grad_h reaching memory.  A, B, C row-major with row
+ * strides lda >= K, ldb >= N, ldc >= N elements; A and B 16-byte aligned
+ * with strides that are multiples of 8 elements (BS_ERR_ALIGN otherwise). */
+int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int64_t ldb,
+                      void *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                      const uint8_t *mask, int32_t *status, void *stream);
+
 /* Per-tensor fp8 scale of to_fp8 (lib_sparse/fp8.py:123-129):
  * *scale_out = max(amax(|x|) / 448, 1e-9), with the amax / 448 rounded to
  * bf16 for bf16 input (eager PyTorch semantics).  `amax_ws` is a device

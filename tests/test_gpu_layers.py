@@ -129,6 +129,13 @@ class _DenseTwin(torch.autograd.Function):
                              torch.zeros((), dtype=torch.bfloat16, device=gh.device))
             if scale is not None:
                 gz.mul_(scale)
+        elif not fp8:
+            # the layer's own grad_z path (fused masked GEMM), with the mask
+            # taken from the dense activation kept here
+            from bitsparse_b200.layers import _relu_grad
+            from bitsparse_b200.src.functions import dense_to_tilesparse
+            gW = matmul(go.T, h, fp8, a_scale=gscale, b_scale=scale)
+            gz = _relu_grad(go, W, dense_to_tilesparse(h.contiguous(), None))
         else:
             gW = matmul(go.T, h, fp8, a_scale=gscale, b_scale=scale)
             gh = matmul(go, W, fp8=fp8, a_scale=gscale)
@@ -176,3 +183,20 @@ def test_ffn_fp8(relu2):
     assert rel(y, yr) < 0.2
     for n, a, b in zip(("x", "W1", "W2", "b1", "b2"), grads, gr):
         assert rel(a, b) < 0.2, n
+
+
+def test_ffn_fused_masked_gemm_path_bit_exact(monkeypatch):
+    """The bf16 FFN with grad_z from the fused masked tcgen05 GEMM (forced
+    for this small K) equals its dense-activation twin bit for bit."""
+    import bitsparse_b200.layers as L
+    monkeypatch.setattr(L, "FUSED_MASK_MIN_K", 0)
+    T, d, H, do = 512, 256, 1024, 256
+    x, W1, W2, b1, b2, gy = make(T, d, H, do, seed=5, bias_shift=-0.01)
+    y, grads = run(FFNRelu, (x, W1, W2, b1, b2), gy)
+    ps = [t.detach().clone().requires_grad_() for t in (x, W1, W2, b1, b2)]
+    yt = _twin_ffn(*ps, False, False)
+    yt.backward(gy)
+    assert torch.equal(y, yt.detach())
+    for n, a, p in zip(("x", "W1", "W2", "b1", "b2"), grads, ps):
+        assert torch.equal(a, p.grad), n
+    B.check_status()
