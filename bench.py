@@ -470,6 +470,35 @@ def mlp_suite(dev):
     }
 
 
+def gemm_case():
+    """Small case for ncu captures of K3 (the tcgen05 GEMM with the ReLU mask
+    in its epilogue): the config-2 backward shape (grad_z = grad_y @ W2
+    masked by h, [8192 x 768] @ [768 x 3072]) and a square 8192^3 product,
+    each with and without the mask, checked against torch."""
+    import torch
+    from bitsparse_b200.src.functions import dense_to_tilesparse
+    from bitsparse_b200.src.operators import mask_with_bitmask_, matmul_relu_mask
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    for M, N, K in ((8192, 3072, 768), (8192, 8192, 8192)):
+        a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        b = torch.randn(K, N, generator=g, device=dev).to(torch.bfloat16)
+        h = torch.randn(M, N, generator=g, device=dev).relu().to(torch.bfloat16)
+        sp = dense_to_tilesparse(h, None)
+        for _ in range(2):
+            out = matmul_relu_mask(a, b, sp)
+            plain = matmul_relu_mask(a, b)
+        ref = mask_with_bitmask_((a.float() @ b.float()).to(torch.bfloat16), sp).float()
+        err = (out.float() - ref).abs().max().item()
+        if err > 1e-2 * ref.abs().max().item() or not bool(torch.all(out[h == 0] == 0)):
+            raise RuntimeError(f"gemm case mismatch at {(M, N, K)}: {err}")
+        del plain
+    import bitsparse_b200 as B
+    B.check_status(dev)
+    print("gemm case ok")
+
+
 def profile_case():
     """Small case for ncu captures: compress + reconstruct of one [8192, 8192]
     bf16 relu(N(0,1)) tensor (134 MB, above L2) into a TensorBuffer, 3 times."""
@@ -502,9 +531,14 @@ def main():
                     help="skip the sweep, MLP and CPU-baseline extras")
     ap.add_argument("--mlp-only", action="store_true",
                     help="run only the sparse-MLP fwd+bwd comparison (configs 2 and 4)")
+    ap.add_argument("--gemm-case", action="store_true",
+                    help="run only the small ncu capture case of the masked tcgen05 GEMM")
     ap.add_argument("--profile-case", action="store_true",
                     help="run only the small ncu capture case and exit")
     args = ap.parse_args()
+    if args.gemm_case:
+        gemm_case()
+        return
     if args.profile_case:
         profile_case()
         return

@@ -41,12 +41,25 @@ def require_cuda(t: torch.Tensor, name: str = "tensor") -> None:
         raise RuntimeError(f"{name} must be a CUDA tensor (bitsparse_b200 has no CPU path)")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
 def stream_handle(device: torch.device) -> int:
+    """cudaStream_t of the current stream of `device` (as an int)."""
+    if _raw_stream is not None:  # the fast accessor (no Stream object built)
+        return _raw_stream(_index(device))
     return torch.cuda.current_stream(device).cuda_stream
 
 
 def status_word(device: torch.device) -> torch.Tensor:
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+    idx = _index(device)
+    s = _status.get(idx)
+    if s is not None:
+        return s
     with _lock:
         s = _status.get(idx)
         if s is None:
@@ -55,11 +68,16 @@ def status_word(device: torch.device) -> torch.Tensor:
     return s
 
 
-def workspace(device: torch.device, num_tiles: int) -> torch.Tensor:
-    """Scan workspace for bs_compress on the current stream (zeroed once)."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    key = (idx, stream_handle(device))
-    need = int(_lib.load().bs_compress_workspace_bytes(int(num_tiles)))
+_ws_bytes: dict[int, int] = {}
+
+
+def workspace(device: torch.device, num_tiles: int, stream: int | None = None) -> torch.Tensor:
+    """Scan workspace for bs_compress on `stream` (default: the current one)."""
+    idx = _index(device)
+    key = (idx, stream if stream is not None else stream_handle(device))
+    need = _ws_bytes.get(num_tiles)
+    if need is None:
+        need = _ws_bytes[num_tiles] = int(_lib.load().bs_compress_workspace_bytes(int(num_tiles)))
     with _lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < need:

@@ -24,9 +24,11 @@
 //               after a tile's last stage to that accumulator's "full"
 //               barrier; it also allocates and frees the TMEM columns;
 //   warps 2..5  epilogue: the row's bitmask words are fetched before the
-//               wait; tcgen05.ld of 32 columns at a time from the warp's
-//               TMEM lane quarter (warp % 4), bf16 rounding, masking, 16-byte
-//               stores; then the accumulator is handed back to the MMA warp.
+//               wait; tcgen05.ld of 64 columns at a time from the warp's
+//               TMEM lane quarter (warp % 4), bf16 rounding, masking, a
+//               swizzled 32 x 64 staging box in shared memory (two per warp,
+//               alternating) and a TMA store of the box (clipped at the
+//               edges); then the accumulator is handed back to the MMA warp.
 // All mbarrier waits are bounded (BS_STATUS_TIMEOUT); the producer waits
 // for its own copies before the CTA exits; TMEM is always freed.
 #include "common.cuh"
@@ -45,14 +47,19 @@ constexpr int kBBytes = kBK * kBN * 2;  // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreadsG = 192;  // 6 warps
 constexpr uint32_t kTmemCols = 256;
-constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kStages * kStageBytes + 256;
+// Epilogue staging: per epilogue warp two 32-row x 64-column bf16 boxes
+// (128-byte rows, 128-byte swizzle) for the TMA stores of C.
+constexpr int kEpiBox = 32 * 64 * 2;  // 4 KB
+constexpr int kEpiBytes = 4 * 2 * kEpiBox;
+constexpr size_t kSmem =
+    1024 /* alignment slack */ + (size_t)kStages * kStageBytes + kEpiBytes + 256;
 
 struct GemmParams {
   uint8_t *C;
   int64_t M, N, K, ldc;
   const uint8_t *mask;  // bitmask of a bitsparse [M, N] tensor, or null
   int64_t mask_grid_n;  // its tile columns: ceil(N / 64)
-  int c_vec;            // C base and row stride allow 16-byte stores
+  int c_tma;            // C is written by TMA stores (aligned base and row stride)
   int32_t *status;
 };
 
@@ -158,12 +165,14 @@ __device__ __forceinline__ void tile_coords(int64_t t, int64_t mt, int64_t nt, i
 template <bool MASK>
 __global__ void __launch_bounds__(kThreadsG, 1)
     gemm_mask_kernel(const __grid_constant__ CUtensorMap tmA,
-                     const __grid_constant__ CUtensorMap tmB, const GemmParams P) {
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)kStages * kStageBytes);
+  uint8_t *epi = smem + (size_t)kStages * kStageBytes;  // staging boxes
+  uint64_t *full = reinterpret_cast<uint64_t *>(epi + kEpiBytes);
   uint64_t *empty = full + kStages;
   uint64_t *acc_full = empty + kStages;  // [2]: MMA -> epilogue
   uint64_t *acc_empty = acc_full + 2;    // [2]: epilogue -> MMA
@@ -286,30 +295,47 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       const uint32_t zero_guard = ok ? 0xFFFFu : 0u;  // a failed wait writes zeros
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTmemCols);
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + (uint32_t)(32 * c), r);
-        const int64_t n = n0 + 32 * c;
-        if (m >= P.M || n >= P.N) continue;
-        const uint32_t kw = (uint32_t)(keep[c >> 1] >> (32 * (c & 1)));
-        uint32_t w[16];
+      for (int c = 0; c < kBN / 64; ++c) {
+        uint32_t r[64];
+        tmem_ld32(tbase + (uint32_t)(64 * c), *reinterpret_cast<uint32_t(*)[32]>(r));
+        tmem_ld32(tbase + (uint32_t)(64 * c + 32), *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+        const uint64_t kw = keep[c];
+        uint32_t w[32];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 32; ++i) {
           uint32_t lo = f32_to_bf16_bits(__uint_as_float(r[2 * i])) & zero_guard;
           uint32_t hi = f32_to_bf16_bits(__uint_as_float(r[2 * i + 1])) & zero_guard;
-          lo &= 0u - ((kw >> (2 * i)) & 1u);
-          hi &= 0u - ((kw >> (2 * i + 1)) & 1u);
+          lo &= 0u - (uint32_t)((kw >> (2 * i)) & 1u);
+          hi &= 0u - (uint32_t)((kw >> (2 * i + 1)) & 1u);
           w[i] = lo | (hi << 16);
         }
-        uint8_t *dst = P.C + (m * P.ldc + n) * 2;
-        if (P.c_vec && n + 32 <= P.N) {
+        const int64_t n = n0 + 64 * c;
+        if (P.c_tma) {
+          // stage row `lane` of this warp's 32 x 64 box: 16-byte chunk i at
+          // chunk i ^ (row & 7) (the 128-byte swizzle of the store's tensor
+          // map; conflict-free), then one lane stores the box with TMA
+          uint8_t *box = epi + (size_t)(q * 2 + (c & 1)) * kEpiBox;
+          if (lane == 0)  // the store that last read this box is done reading
+            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            reinterpret_cast<uint4 *>(dst)[i] =
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint4 *>(box + lane * 128 + ((i ^ (lane & 7)) * 16)) =
                 make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-        } else {
-          for (int i = 0; i < 32 && n + i < P.N; ++i)
-            reinterpret_cast<uint16_t *>(dst)[i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0 && n < P.N && mb * kBM + 32 * q < P.M) {
+            asm volatile(
+                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                    reinterpret_cast<uint64_t>(&tmC)),
+                "r"((int)n), "r"((int)(mb * kBM + 32 * q)), "r"(saddr(box))
+                : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        } else if (m < P.M) {
+          for (int i = 0; i < 64 && n + i < P.N; ++i)
+            reinterpret_cast<uint16_t *>(P.C + (m * P.ldc + n) * 2)[i] =
+                (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
         }
       }
       // this warp is done with accumulator buf
@@ -318,6 +344,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
+  if (warp >= 2 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -364,8 +391,8 @@ bool make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, in
 }
 
 template <bool MASK>
-int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &P,
-                cudaStream_t st) {
+int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
+                const GemmParams &P, cudaStream_t st) {
   auto kernel = gemm_mask_kernel<MASK>;
   static std::once_flag once[2];
   static cudaError_t attr_err[2];
@@ -382,7 +409,7 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &
   }();
   const int64_t tiles = ((P.M + kBM - 1) / kBM) * ((P.N + kBN - 1) / kBN);
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
-  kernel<<<grid, kThreadsG, kSmem, st>>>(ta, tb, P);
+  kernel<<<grid, kThreadsG, kSmem, st>>>(ta, tb, tc, P);
   return cudaGetLastError() == cudaSuccess ? BS_OK : BS_ERR_LAUNCH;
 }
 
@@ -410,9 +437,9 @@ extern "C" int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int6
   P.M = M; P.N = N; P.K = K; P.ldc = ldc;
   P.mask = mask;
   P.mask_grid_n = (N + kTileN - 1) / kTileN;
-  P.c_vec = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((ldc * 2) % 16 == 0);
+  P.c_tma = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((ldc * 2) % 16 == 0);
   P.status = status;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   if (K == 0) {  // empty reduction: C = 0
     for (int64_t r = 0; r < M; ++r)
       if (cudaMemsetAsync(static_cast<uint8_t *>(C) + r * ldc * 2, 0, (size_t)N * 2,
@@ -422,6 +449,8 @@ extern "C" int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int6
   }
   if (!make_map(&ta, A, M, K, lda, kBK, kBM) || !make_map(&tb, B, K, N, ldb, 64, kBK))
     return BS_ERR_ALIGN;
+  if (P.c_tma && !make_map(&tc, C, M, N, ldc, 64, 32)) P.c_tma = 0;
+  if (!P.c_tma) tc = ta;  // unused
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return mask ? launch_gemm<true>(ta, tb, P, st) : launch_gemm<false>(ta, tb, P, st);
+  return mask ? launch_gemm<true>(ta, tb, tc, P, st) : launch_gemm<false>(ta, tb, tc, P, st);
 }

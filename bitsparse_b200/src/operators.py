@@ -112,7 +112,8 @@ def compress(dense: Tensor, scale: Tensor | None = None, sparse_data=None,
     bits = bits_per_value(stored)
     bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
     prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
-    ws = R.workspace(dev, T)
+    st = _stream(dense)
+    ws = R.workspace(dev, T, st)
     status = R.status_word(dev)
     qs = R.ptr(quant_scale)
     qo = R.ptr(quant_out)
@@ -120,7 +121,6 @@ def compress(dense: Tensor, scale: Tensor | None = None, sparse_data=None,
                                   or not quant_out.is_contiguous()
                                   or tuple(quant_out.shape) != (M, N)):
         raise ValueError("quant_out must be a contiguous float8_e4m3fn [M, N] tensor")
-    st = _stream(dense)
     if sparse_data is None:
         if T == 0:
             prefix.zero_()
