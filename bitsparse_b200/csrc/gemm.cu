@@ -35,24 +35,20 @@
 
 #include <cuda.h>  // CUtensorMap (types only; the encoder comes through the runtime)
 
+#include <cstdlib>
 #include <mutex>
 
 namespace bs {
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
-constexpr int kBBytes = kBK * kBN * 2;  // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreadsG = 192;  // 6 warps
 constexpr uint32_t kTmemCols = 256;
 // Epilogue staging: per epilogue warp two 32-row x 64-column bf16 boxes
 // (128-byte rows, 128-byte swizzle) for the TMA stores of C.
 constexpr int kEpiBox = 32 * 64 * 2;  // 4 KB
 constexpr int kEpiBytes = 4 * 2 * kEpiBox;
-constexpr size_t kSmem =
-    1024 /* alignment slack */ + (size_t)kStages * kStageBytes + kEpiBytes + 256;
 
 struct GemmParams {
   uint8_t *C;
@@ -91,9 +87,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_
   status_or(status, BS_STATUS_TIMEOUT);
   return false;
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
-}
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
   asm volatile(
@@ -109,23 +102,44 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, A
-// K-major, B MN-major, N = kBN, M = kBM.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) |
-                            ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
-
+template <int CG>
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+                                         uint32_t idesc, uint32_t accumulate) {
+  if constexpr (CG == 2)
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  else
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+// Arrive on the barrier at shared::cluster address `bar` once every MMA
+// issued so far by this thread has completed.
+template <int CG>
+__device__ __forceinline__ void mma_commit_to(uint32_t bar) {
+  if constexpr (CG == 2)
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+  else
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+// TMA tile load of one CTA of a pair, completing on the barrier at
+// shared::cluster address `bar` (the leader's).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int x, int y,
+                                                 uint32_t bar) {
   asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          saddr(bar))
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -134,8 +148,16 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// Two fp32 -> bf16 conversions, round to nearest even (the hardware
+// conversion; it matches torch's bf16 rounding for every non-NaN value).
+__device__ __forceinline__ uint32_t bf16x2_rn(uint32_t lo, uint32_t hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(__uint_as_float(hi)), "f"(__uint_as_float(lo)));
+  return r;
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (no wait).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t *r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
       "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -145,8 +167,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
 
 // Tile t of the static schedule -> (m block, n block): groups of kGroupM
 // row blocks sweep the column blocks together, so neighbouring CTAs share
@@ -162,99 +187,160 @@ __device__ __forceinline__ void tile_coords(int64_t t, int64_t mt, int64_t nt, i
   nb = r / gm;
 }
 
-template <bool MASK>
+// Per cluster size CG (1: one CTA per tile; 2: a CTA pair shares a
+// 256 x 256 tile through tcgen05's cta_group::2, each CTA loading its 128
+// rows of A and 128 of the 256 columns of B, so a stage is 32 KB instead
+// of 48 KB and the operand bytes per flop drop by a third).
+template <int CG>
+struct GemmCfg {
+  static constexpr int BM = kBM * CG;           // rows of C per tile
+  static constexpr int BNL = kBN / CG;          // columns of B this CTA loads
+  static constexpr int BBYTES = kBK * BNL * 2;  // B bytes per stage and CTA
+  static constexpr int STAGE = kABytes + BBYTES;
+  static constexpr int NST = CG == 2 ? 6 : 4;   // stages
+  static constexpr size_t SMEM = 1024 + (size_t)NST * STAGE + kEpiBytes + 256;
+  // instruction descriptor: M = BM, N = kBN
+  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) |
+                                    (1u << 16) | ((uint32_t)(kBN >> 3) << 17) |
+                                    ((uint32_t)(BM >> 4) << 24);
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+template <bool MASK, int CG>
 __global__ void __launch_bounds__(kThreadsG, 1)
     gemm_mask_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmParams P) {
+  using G = GemmCfg<CG>;
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte alignment for the 128-byte swizzle atoms
+  // 1024-byte alignment for the 128-byte swizzle atoms (same offsets in both
+  // CTAs of a pair, which the cta_group::2 descriptors rely on)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t *epi = smem + (size_t)kStages * kStageBytes;  // staging boxes
+  uint8_t *epi = smem + (size_t)G::NST * G::STAGE;  // staging boxes
   uint64_t *full = reinterpret_cast<uint64_t *>(epi + kEpiBytes);
-  uint64_t *empty = full + kStages;
-  uint64_t *acc_full = empty + kStages;  // [2]: MMA -> epilogue
-  uint64_t *acc_empty = acc_full + 2;    // [2]: epilogue -> MMA
+  uint64_t *empty = full + G::NST;
+  uint64_t *acc_full = empty + G::NST;  // [2]: MMA -> epilogue
+  uint64_t *acc_empty = acc_full + 2;   // [2]: epilogue -> MMA
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = CG == 2 ? cluster_rank() : 0;
+  const bool leader = rank == 0;
+  const int64_t cid = (int64_t)blockIdx.x / CG, ncl = (int64_t)gridDim.x / CG;
   const int nk = (int)((P.K + kBK - 1) / kBK);
-  const int64_t mt = (P.M + kBM - 1) / kBM, nt = (P.N + kBN - 1) / kBN;
+  const int64_t mt = (P.M + G::BM - 1) / G::BM, nt = (P.N + kBN - 1) / kBN;
   const int64_t ntiles = mt * nt;
 
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < G::NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[i], 4 * CG);  // one arrival per epilogue warp of the pair
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // the whole warp allocates (sync.aligned)
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     saddr(tmem_slot)),
-                 "r"(2 * kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  if (warp == 1) {  // the whole warp allocates (sync.aligned); both CTAs of a pair
+    if constexpr (CG == 2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       saddr(tmem_slot)),
+                   "r"(2 * kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       saddr(tmem_slot)),
+                   "r"(2 * kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // both CTAs' barriers initialised
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
-      int64_t it = 0;  // global k-block counter: stage it % kStages, phase it / kStages
+      int64_t it = 0;  // global k-block counter: stage it % NST, phase it / NST
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      // the stage's "full" barrier is the leader's; it expects both CTAs' bytes
+      for (int64_t t = cid; t < ntiles && ok; t += ncl) {
         int64_t mb, nb;
         tile_coords(t, mt, nt, mb, nb);
         for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int s = (int)(it % kStages);
-          if (it >= kStages &&
-              !mbar_wait(&empty[s], (uint32_t)((it / kStages - 1) & 1), P.status)) {
+          const int s = (int)(it % G::NST);
+          if (it >= G::NST &&
+              !mbar_wait(&empty[s], (uint32_t)((it / G::NST - 1) & 1), P.status)) {
             ok = false;
             break;
           }
-          uint8_t *a = smem + (size_t)s * kStageBytes;
+          uint8_t *a = smem + (size_t)s * G::STAGE;
           uint8_t *b = a + kABytes;
-          mbar_expect_tx(&full[s], kStageBytes);
-          tma_load_2d(a, &tmA, kb * kBK, (int)(mb * kBM), &full[s]);
+          const int ay = (int)(mb * G::BM + rank * kBM);
+          const int bx = (int)(nb * kBN + rank * G::BNL);
+          if constexpr (CG == 2) {
+            if (leader) mbar_expect_tx(&full[s], 2 * G::STAGE);
+            const uint32_t bar = map_rank(saddr(&full[s]), 0);
+            tma_load_2d_pair(a, &tmA, kb * kBK, ay, bar);
 #pragma unroll
-          for (int j = 0; j < kBN / 64; ++j)
-            tma_load_2d(b + j * (kBK * 64 * 2), &tmB, (int)(nb * kBN) + 64 * j, kb * kBK,
-                        &full[s]);
+            for (int j = 0; j < G::BNL / 64; ++j)
+              tma_load_2d_pair(b + j * (kBK * 64 * 2), &tmB, bx + 64 * j, kb * kBK, bar);
+          } else {
+            mbar_expect_tx(&full[s], G::STAGE);
+            tma_load_2d(a, &tmA, kb * kBK, ay, &full[s]);
+#pragma unroll
+            for (int j = 0; j < G::BNL / 64; ++j)
+              tma_load_2d(b + j * (kBK * 64 * 2), &tmB, bx + 64 * j, kb * kBK, &full[s]);
+          }
         }
       }
-      // every copy this CTA issued has landed before it may exit
-      for (int64_t i = it - kStages < 0 ? 0 : it - kStages; i < it; ++i)
-        mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1), P.status);
+      // every copy landed before the CTA may exit (the leader's barriers
+      // count the peer's copies too)
+      if (leader)
+        for (int64_t i = it - G::NST < 0 ? 0 : it - G::NST; i < it; ++i)
+          mbar_wait(&full[i % G::NST], (uint32_t)((i / G::NST) & 1), P.status);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int64_t it = 0;
       int j = 0;  // local tile counter: accumulator buffer j & 1, use j >> 1
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++j) {
+      for (int64_t t = cid; t < ntiles && ok; t += ncl, ++j) {
         const int buf = j & 1;
         if (j >= 2 && !mbar_wait(&acc_empty[buf], (uint32_t)(((j >> 1) - 1) & 1), P.status))
           break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * kTmemCols);
         for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int s = (int)(it % kStages);
-          if (!mbar_wait(&full[s], (uint32_t)((it / kStages) & 1), P.status)) {
+          const int s = (int)(it % G::NST);
+          if (!mbar_wait(&full[s], (uint32_t)((it / G::NST) & 1), P.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a = saddr(smem + (size_t)s * kStageBytes);
+          const uint32_t a = saddr(smem + (size_t)s * G::STAGE);
           const uint32_t b = a + kABytes;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
@@ -263,21 +349,26 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             //    1024 B apart (SBO); +2048 B per K=16.
             const uint64_t ad = smem_desc(a + 32 * k, 16, 1024);
             const uint64_t bd = smem_desc(b + 2048 * k, kBK * 64 * 2, 1024);
-            mma_bf16(d, ad, bd, (kb > 0 || k > 0) ? 1u : 0u);
+            mma_bf16<CG>(d, ad, bd, G::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
           }
-          mma_commit(&empty[s]);  // stage free once these MMAs have read it
+          // the stage is free (in both CTAs) once these MMAs have read it
+          mma_commit_to<CG>(saddr(&empty[s]));
+          if constexpr (CG == 2) mma_commit_to<CG>(map_rank(saddr(&empty[s]), 1));
         }
-        mma_commit(&acc_full[buf]);  // accumulator j complete
+        mma_commit_to<CG>(saddr(&acc_full[buf]));  // accumulator j complete
+        if constexpr (CG == 2) mma_commit_to<CG>(map_rank(saddr(&acc_full[buf]), 1));
       }
     }
   } else {
-    // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (rows of the tile)
+    // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (this CTA's rows)
     const int q = warp & 3;
+    const uint32_t acc_empty_leader = map_rank(saddr(acc_empty), 0);
     int j = 0;
-    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
+    for (int64_t t = cid; t < ntiles; t += ncl, ++j) {
       int64_t mb, nb;
       tile_coords(t, mt, nt, mb, nb);
-      const int64_t m = mb * kBM + 32 * q + lane, n0 = nb * kBN;
+      const int64_t row0 = mb * G::BM + rank * kBM + 32 * q;  // first row of this warp
+      const int64_t m = row0 + lane, n0 = nb * kBN;
       // this row's mask words for the tile's 256 columns, fetched before the wait
       uint64_t keep[kBN / 64];
 #pragma unroll
@@ -292,22 +383,22 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       const int buf = j & 1;
       const bool ok = mbar_wait(&acc_full[buf], (uint32_t)((j >> 1) & 1), P.status);
       tc_fence_after();
-      const uint32_t zero_guard = ok ? 0xFFFFu : 0u;  // a failed wait writes zeros
+      const uint32_t zero_guard = ok ? 0xFFFFFFFFu : 0u;  // a failed wait writes zeros
       const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTmemCols);
 #pragma unroll
       for (int c = 0; c < kBN / 64; ++c) {
         uint32_t r[64];
-        tmem_ld32(tbase + (uint32_t)(64 * c), *reinterpret_cast<uint32_t(*)[32]>(r));
-        tmem_ld32(tbase + (uint32_t)(64 * c + 32), *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+        tmem_ld32_nowait(tbase + (uint32_t)(64 * c), r);
+        tmem_ld32_nowait(tbase + (uint32_t)(64 * c + 32), r + 32);
+        tmem_wait_ld();
         const uint64_t kw = keep[c];
         uint32_t w[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          uint32_t lo = f32_to_bf16_bits(__uint_as_float(r[2 * i])) & zero_guard;
-          uint32_t hi = f32_to_bf16_bits(__uint_as_float(r[2 * i + 1])) & zero_guard;
-          lo &= 0u - (uint32_t)((kw >> (2 * i)) & 1u);
-          hi &= 0u - (uint32_t)((kw >> (2 * i + 1)) & 1u);
-          w[i] = lo | (hi << 16);
+          // mask bits 2i, 2i+1 -> 0x0000FFFF / 0xFFFF0000 halves
+          const uint32_t two = (uint32_t)(kw >> (2 * i)) & 3u;
+          const uint32_t keep_w = ((two & 1u) ? 0x0000FFFFu : 0u) | ((two & 2u) ? 0xFFFF0000u : 0u);
+          w[i] = bf16x2_rn(r[2 * i], r[2 * i + 1]) & keep_w & zero_guard;
         }
         const int64_t n = n0 + 64 * c;
         if (P.c_tma) {
@@ -324,11 +415,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
                 make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
-          if (lane == 0 && n < P.N && mb * kBM + 32 * q < P.M) {
+          if (lane == 0 && n < P.N && row0 < P.M) {
             asm volatile(
                 "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                     reinterpret_cast<uint64_t>(&tmC)),
-                "r"((int)n), "r"((int)(mb * kBM + 32 * q)), "r"(saddr(box))
+                "r"((int)n), "r"((int)row0), "r"(saddr(box))
                 : "memory");
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
@@ -338,20 +429,27 @@ __global__ void __launch_bounds__(kThreadsG, 1)
                 (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
         }
       }
-      // this warp is done with accumulator buf
+      // this warp is done with accumulator buf (the leader's barrier counts
+      // the epilogue warps of both CTAs)
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader + (uint32_t)(8 * buf));
     }
   }
   if (warp >= 2 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // no CTA leaves while its peer may signal it
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(2 * kTmemCols)
-                 : "memory");
+    if constexpr (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"(2 * kTmemCols)
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"(2 * kTmemCols)
+                   : "memory");
   }
 }
 
@@ -390,27 +488,40 @@ bool make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, in
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool MASK>
+template <bool MASK, int CG>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
                 const GemmParams &P, cudaStream_t st) {
-  auto kernel = gemm_mask_kernel<MASK>;
-  static std::once_flag once[2];
-  static cudaError_t attr_err[2];
-  std::call_once(once[MASK], [&] {
-    attr_err[MASK] =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+  using G = GemmCfg<CG>;
+  auto kernel = gemm_mask_kernel<MASK, CG>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
   });
-  if (attr_err[MASK] != cudaSuccess) return BS_ERR_LAUNCH;
+  if (attr_err != cudaSuccess) return BS_ERR_LAUNCH;
   static int sms = [] {
     int dev = 0, n = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     return n > 0 ? n : 1;
   }();
-  const int64_t tiles = ((P.M + kBM - 1) / kBM) * ((P.N + kBN - 1) / kBN);
-  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
-  kernel<<<grid, kThreadsG, kSmem, st>>>(ta, tb, tc, P);
-  return cudaGetLastError() == cudaSuccess ? BS_OK : BS_ERR_LAUNCH;
+  const int64_t tiles = ((P.M + G::BM - 1) / G::BM) * ((P.N + kBN - 1) / kBN);
+  const int64_t slots = sms / CG;  // persistent: one CTA (pair) per SM (pair)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(CG * (tiles < slots ? tiles : slots)));
+  cfg.blockDim = dim3(kThreadsG);
+  cfg.dynamicSmemBytes = G::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, P) != cudaSuccess) return BS_ERR_LAUNCH;
+  return BS_OK;
 }
 
 }  // namespace
@@ -449,8 +560,12 @@ extern "C" int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int6
   }
   if (!make_map(&ta, A, M, K, lda, kBK, kBM) || !make_map(&tb, B, K, N, ldb, 64, kBK))
     return BS_ERR_ALIGN;
+  // CTA pairs (cta_group::2) once there are two 128-row blocks to share
+  const bool pair = M >= 2 * kBM && !getenv("BS_GEMM_ONE_CTA");
   if (P.c_tma && !make_map(&tc, C, M, N, ldc, 64, 32)) P.c_tma = 0;
   if (!P.c_tma) tc = ta;  // unused
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return mask ? launch_gemm<true>(ta, tb, tc, P, st) : launch_gemm<false>(ta, tb, tc, P, st);
+  if (pair)
+    return mask ? launch_gemm<true, 2>(ta, tb, tc, P, st) : launch_gemm<false, 2>(ta, tb, tc, P, st);
+  return mask ? launch_gemm<true, 1>(ta, tb, tc, P, st) : launch_gemm<false, 1>(ta, tb, tc, P, st);
 }
