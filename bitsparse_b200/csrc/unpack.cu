@@ -72,8 +72,19 @@ __device__ __forceinline__ uint32_t stage_values(const UnpackParams &P, int64_t 
     const int64_t v0 = base / EPV;
     const int64_t nvec = cnt ? (base + cnt - 1) / EPV - v0 + 1 : 0;
     if (P.vals_v16) {
-      for (int64_t i = tid; i < nvec; i += kThreads)
-        *reinterpret_cast<uint4 *>(stage + 16 * i) = ld_nc_v4(P.vals + (v0 + i) * 16);
+      // all of this thread's vectors are loaded before any is stored
+      constexpr int kPer = (kStageBytes / 16 + kThreads - 1) / kThreads;
+      uint4 v[kPer];
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int64_t i = tid + (int64_t)k * kThreads;
+        if (i < nvec) v[k] = ld_nc_v4(P.vals + (v0 + i) * 16);
+      }
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int64_t i = tid + (int64_t)k * kThreads;
+        if (i < nvec) *reinterpret_cast<uint4 *>(stage + 16 * i) = v[k];
+      }
     } else {
       for (int64_t i = tid; i < nvec * 16; i += kThreads) {
         const int64_t byte = v0 * 16 + i;
@@ -89,7 +100,18 @@ __device__ __forceinline__ uint32_t stage_values(const UnpackParams &P, int64_t 
     const int64_t nw = cnt ? (((base + cnt) * B + 31) >> 5) - w0 : 0;
     const uint32_t *words = reinterpret_cast<const uint32_t *>(P.vals);
     uint32_t *sw = reinterpret_cast<uint32_t *>(stage);
-    for (int64_t i = tid; i < nw; i += kThreads) sw[i] = __ldg(words + w0 + i);
+    constexpr int kPer = (kStageBytes / 4 + kThreads - 1) / kThreads;
+    uint32_t v[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int64_t i = tid + (int64_t)k * kThreads;
+      if (i < nw) v[k] = __ldg(words + w0 + i);
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int64_t i = tid + (int64_t)k * kThreads;
+      if (i < nw) sw[i] = v[k];
+    }
     if (tid == 0) sw[nw] = 0;  // guard for the two-word read of the last value
     return (uint32_t)(bit0 - (w0 << 5));
   }
@@ -184,19 +206,19 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
   const int nt = tiles_here(P, pid0);
   const PidPos pp(pid0, P.grid_n);
   const int tid = threadIdx.x;
-  const uint32_t first = stage_values<SDT, PACK>(P, P.first_tile + pid0, nt, stage);
-
   uint32_t m[G::S], cnt[G::S], ex[G::S];
 #pragma unroll
-  for (int s = 0; s < G::S; ++s) {
+  for (int s = 0; s < G::S; ++s) {  // masks first: independent of the values
     const int c = s * kThreads + tid;
     const int j = c / G::CPT, cc = c % G::CPT;
     m[s] = 0;
     if (j < nt)
       m[s] = load_mask<G::VEC>(P.bitmask + (P.first_tile + pid0 + j) * kTileBytes +
                                cc * (G::VEC / 8));
-    cnt[s] = __popc(m[s]);
   }
+  const uint32_t first = stage_values<SDT, PACK>(P, P.first_tile + pid0, nt, stage);
+#pragma unroll
+  for (int s = 0; s < G::S; ++s) cnt[s] = __popc(m[s]);
   block_excl_scan<G::S>(cnt, ex, s_wt);  // its barriers also publish the stage
 
   float s2 = 0.f;
@@ -322,16 +344,17 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
   const int nt = tiles_here(P, pid0);
   const PidPos pp(pid0, P.grid_n);
   const int tid = threadIdx.x;
-  const uint32_t first = stage_values<SDT, PACK>(P, pid0, nt, stage);
   uint32_t m[G::S], cnt[G::S], ex[G::S];
 #pragma unroll
-  for (int s = 0; s < G::S; ++s) {
+  for (int s = 0; s < G::S; ++s) {  // masks first: independent of the values
     const int c = s * kThreads + tid;
     const int j = c / G::CPT, cc = c % G::CPT;
     m[s] = 0;
     if (j < nt) m[s] = load_mask<16>(P.bitmask + (pid0 + j) * kTileBytes + cc * 2);
-    cnt[s] = __popc(m[s]);
   }
+  const uint32_t first = stage_values<SDT, PACK>(P, pid0, nt, stage);
+#pragma unroll
+  for (int s = 0; s < G::S; ++s) cnt[s] = __popc(m[s]);
   block_excl_scan<G::S>(cnt, ex, s_wt);
   float sb = 0.f;
   if constexpr (SCALE) sb = bf16_bits_to_f32(f32_to_bf16_bits(*P.scale));
