@@ -748,8 +748,8 @@ __device__ __forceinline__ void place8(uint32_t &a, uint32_t m, uint32_t bit, ui
       : "r"(m), "r"(bit), "h"((unsigned short)(v & 0xFFu)));
 }
 
-template <int DT_IN, bool QUANT, bool PACK, int TPP_, int NW, int D, int A>
-__global__ void __launch_bounds__(NW * 32, 2)
+template <int DT_IN, bool QUANT, bool PACK, int TPP_, int NW, int D, int A, int MINB>
+__global__ void __launch_bounds__(NW * 32, MINB)
     onepass_kernel(const __grid_constant__ CUtensorMap tmap, const CompressParams P) {
   using O = Onepass<DT_IN, QUANT, TPP_, NW, D, A>;
   using C = typename O::C;
@@ -1060,7 +1060,7 @@ constexpr int onepass_tpp() {
   return Elt<DT_IN>::bytes == 1 && 2 * TPP2 * kTileM / NW <= kTileM ? 2 * TPP2 : TPP2;
 }
 
-template <int DT_IN, bool QUANT, bool PACK, int TPP2, int NW, int D, int A>
+template <int DT_IN, bool QUANT, bool PACK, int TPP2, int NW, int D, int A, int MINB = 2>
 static int launch_onepass(const CompressParams &P, cudaStream_t st) {
   constexpr int TPP = onepass_tpp<DT_IN, TPP2, NW>();
   using O = Onepass<DT_IN, QUANT, TPP, NW, D, A>;
@@ -1084,7 +1084,7 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return kNotApplicable;
-  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A>;
+  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB>;
   int resident = resident_ctas(reinterpret_cast<const void *>(kernel), O::SMEM, NW * 32);
   if (resident <= 0) return BS_ERR_LAUNCH;
   // a flush reads the counts of G - 1 partitions, at most 2 per thread

@@ -1,0 +1,122 @@
+"""Token-row sharding of compressed activations across ranks.
+
+Compression and reconstruction are independent per tile row (64 token rows),
+so on N GPUs each rank compresses only its own rows and no communication is
+needed on the data path (the reference runs one process per GPU the same
+way).  Where a global view is wanted -- one compressed tensor for a
+checkpoint, or an activation all-gather -- the shards are merged without
+decompressing:
+
+* the bitmasks of whole tile rows are contiguous in the global tile order,
+  so they concatenate;
+* the global prefix is each shard's prefix offset by the value counts of
+  the shards before it (mod 2^32, like the reference's int32 cumsum viewed
+  as uint32, lib_sparse/src/functions.py:33-40);
+* the raw value streams concatenate.
+
+These are host-side helpers on torch tensors (any device, any
+torch.distributed backend); they launch no kernels of their own.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .bitsparse import BitsparseTensor, tile_grid
+from .config import BLOCK_M
+
+
+def row_range(M: int, rank: int, world: int, block: int = BLOCK_M) -> tuple[int, int]:
+    """Rows [start, stop) of an [M, N] tensor owned by `rank` of `world`:
+    contiguous runs of whole tile rows (the last shard takes the ragged end;
+    trailing ranks may get no rows)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} not in a world of {world}")
+    tiles_m = (M + block - 1) // block
+    per = (tiles_m + world - 1) // world
+    start = min(rank * per * block, M)
+    stop = min((rank + 1) * per * block, M)
+    return start, stop
+
+
+def _values(sp: BitsparseTensor) -> torch.Tensor:
+    """The shard's own nnz raw values (a slice of an arena when shared)."""
+    nnz = int(sp.prefix[-1].item())
+    off = int(sp.vals_offset.reshape(-1)[0].item())
+    return sp.vals[off: off + nnz]
+
+
+def concat_row_shards(shards: list[BitsparseTensor]) -> BitsparseTensor:
+    """Merge compressed row shards (in row order) into one compressed tensor
+    equal to compressing the concatenated rows.  Raw (not pack_sbit) storage;
+    every shard but the last must hold whole tile rows; fp8 shards must share
+    one scale."""
+    if not shards:
+        raise ValueError("no shards")
+    s0 = shards[0]
+    N = s0.shape[1]
+    for i, s in enumerate(shards):
+        if s.pack_sbit:
+            raise ValueError("concat_row_shards takes raw storage (pack_sbit=False)")
+        if s.shape[1] != N or s.dtype != s0.dtype:
+            raise ValueError("shards differ in columns or dtype")
+        if (s.BLOCK_M, s.BLOCK_N) != (s0.BLOCK_M, s0.BLOCK_N):
+            raise ValueError("shards differ in tile size")
+        if i < len(shards) - 1 and s.shape[0] % s.BLOCK_M:
+            raise ValueError("every shard but the last must hold whole tile rows")
+    scales = [s.scale for s in shards]
+    if any(sc is not None for sc in scales):
+        if any(sc is None for sc in scales) or any(
+                not torch.equal(sc.reshape(()), scales[0].reshape(())) for sc in scales):
+            raise ValueError("fp8 shards must share one scale")
+    M = sum(s.shape[0] for s in shards)
+    grid_m, grid_n, _, _, _ = tile_grid(M, N, s0.BLOCK_M, s0.BLOCK_N)
+    bitmask = torch.cat([s.bitmask for s in shards])
+    pieces, base = [], 0
+    for s in shards:
+        p = s.prefix.to(torch.int64)
+        pieces.append(p[:-1] + base)
+        base += int(p[-1].item())
+    pieces.append(torch.tensor([base], dtype=torch.int64, device=bitmask.device))
+    prefix = (torch.cat(pieces) & 0xFFFFFFFF).to(torch.uint32)
+    vals = torch.cat([_values(s) for s in shards])
+    return BitsparseTensor(vals, bitmask, prefix, (M, N), s0.dtype, grid_m, grid_n,
+                           s0.BLOCK_M, s0.BLOCK_N, scale=s0.scale, pack_sbit=False)
+
+
+def _all_gather_var(t: torch.Tensor, sizes: list[int], group) -> list[torch.Tensor]:
+    """all_gather of 1-D tensors of different lengths (padded to the longest)."""
+    n = max(sizes) if sizes else 0
+    pad = torch.zeros(n, dtype=t.dtype, device=t.device)
+    pad[: t.numel()] = t
+    out = [torch.empty_like(pad) for _ in sizes]
+    dist.all_gather(out, pad, group=group)
+    return [o[:k] for o, k in zip(out, sizes)]
+
+
+def gather_bitsparse(local: BitsparseTensor, group=None) -> BitsparseTensor:
+    """All-gather the row shards of every rank (rank order = row order) into
+    the global compressed tensor, on every rank."""
+    world = dist.get_world_size(group)
+    vals = _values(local)
+    dev = local.bitmask.device
+    meta = torch.tensor([local.shape[0], local.bitmask.numel(), local.prefix.numel(),
+                         vals.numel()], dtype=torch.int64, device=dev)
+    metas = [torch.empty_like(meta) for _ in range(world)]
+    dist.all_gather(metas, meta, group=group)
+    rows, bm_n, pf_n, v_n = ([int(m[i].item()) for m in metas] for i in range(4))
+    bms = _all_gather_var(local.bitmask, bm_n, group)
+    pfs = _all_gather_var(local.prefix.to(torch.int64), pf_n, group)
+    # bf16 / fp8 values travel as raw bytes (not every backend takes fp8)
+    vbytes = _all_gather_var(vals.view(torch.uint8), [k * vals.element_size() for k in v_n],
+                             group)
+    shards = []
+    for r in range(world):
+        if rows[r] == 0:
+            continue
+        gm, gn, _, _, _ = tile_grid(rows[r], local.shape[1], local.BLOCK_M, local.BLOCK_N)
+        shards.append(BitsparseTensor(vbytes[r].view(local.vals.dtype), bms[r],
+                                      pfs[r].to(torch.uint32), (rows[r], local.shape[1]),
+                                      local.dtype, gm, gn, local.BLOCK_M, local.BLOCK_N,
+                                      scale=local.scale, pack_sbit=False))
+    return concat_row_shards(shards)
