@@ -83,6 +83,11 @@ struct CompressParams {
   int vec_ok;    // dense base / row stride allow 32-byte vector loads
   int vals_v16;  // vals base 16-byte aligned (raw storage)
   int qout_vec;  // quant_out allows chunk-wide stores
+  // one-pass bias + ReLU mode: the input is z, the compressed tensor is
+  // relu(bf16(z + bias)), which is also written densely to relu_out
+  const uint8_t *bias;  // bf16 [N]
+  uint8_t *relu_out;    // bf16 [M, N], row stride relu_ld
+  int64_t relu_ld;
 };
 
 template <int DT_IN, bool QUANT, int TPP>
@@ -705,6 +710,23 @@ __device__ __forceinline__ void emit_words(const CompressParams &P, const uint8_
   }
 }
 
+// Two fp32 -> bf16 conversions, round to nearest even (the hardware
+// conversion; equal to torch's bf16 rounding for every non-NaN value).
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;
+// -0 and NaN unchanged.
+__device__ __forceinline__ uint32_t relu_bf16x2(uint32_t w) {
+  const uint32_t v = w & 0x7FFF7FFFu;
+  const uint32_t nz = v + 0x7FFF7FFFu;   // bit 15 of a half set iff v != 0
+  const uint32_t nan = v + 0x007F007Fu;  // bit 15 set iff v >= 0x7F81 (NaN)
+  const uint32_t kill = w & nz & ~nan & 0x80008000u;
+  return w & ~((kill >> 15) * 0xFFFFu);
+}
+
 // Mask of 8 bf16 (4 words): bit i set iff element i > 0 (a bf16x2 compare
 // per word: NaN, -0 and +0 give 0).
 __device__ __forceinline__ uint32_t mask_bf16x8(const uint32_t (&w)[4]) {
@@ -748,7 +770,8 @@ __device__ __forceinline__ void place8(uint32_t &a, uint32_t m, uint32_t bit, ui
       : "r"(m), "r"(bit), "h"((unsigned short)(v & 0xFFu)));
 }
 
-template <int DT_IN, bool QUANT, bool PACK, int TPP_, int NW, int D, int A, int MINB>
+template <int DT_IN, bool QUANT, bool PACK, int TPP_, int NW, int D, int A, int MINB,
+          bool BIAS = false>
 __global__ void __launch_bounds__(NW * 32, MINB)
     onepass_kernel(const __grid_constant__ CUtensorMap tmap, const CompressParams P) {
   using O = Onepass<DT_IN, QUANT, TPP_, NW, D, A>;
@@ -843,6 +866,23 @@ __global__ void __launch_bounds__(NW * 32, MINB)
       const bool valid = tile < P.num_tiles;  // warp-uniform
       if (valid) {
         uint8_t *bm = P.bitmask + (p * TPP * kTileM + rho0 + sub) * 8 + c8;
+        // bias + ReLU mode: this lane's 8 columns are the same in every step
+        uint32_t bw[4] = {0, 0, 0, 0};
+        int64_t brow0 = 0, bcol = 0;
+        if constexpr (BIAS) {
+          const int64_t tm = tile / P.grid_n, tn = tile - tm * P.grid_n;
+          brow0 = tm * kTileM + (rho0 - j * kTileM) + sub;
+          bcol = tn * kTileN + 8 * c8;
+          if (bcol + 8 <= P.N) {
+            const uint4 b4 = *reinterpret_cast<const uint4 *>(P.bias + bcol * 2);
+            bw[0] = b4.x; bw[1] = b4.y; bw[2] = b4.z; bw[3] = b4.w;
+          } else {
+            for (int i = 0; i < 8; ++i)
+              if (bcol + i < P.N)
+                bw[i >> 1] |= (uint32_t)reinterpret_cast<const uint16_t *>(P.bias)[bcol + i]
+                              << (16 * (i & 1));
+          }
+        }
 #pragma unroll
         for (int s4 = 0; s4 < S; ++s4) {
           const uint8_t *src = stage + ((rho0 + 4 * s4 + sub) * kTileN + 8 * c8) * O::EB;
@@ -856,6 +896,29 @@ __global__ void __launch_bounds__(NW * 32, MINB)
         }
 #pragma unroll
         for (int s4 = 0; s4 < S; ++s4) {
+          if constexpr (BIAS) {
+            // y = relu(bf16(z + bias)): fp32 add rounded once to bf16 (torch's
+            // bf16 add), then strictly negative values -> +0 (-0 and NaN kept)
+            const int64_t grow = brow0 + 4 * s4;
+            // rows past M (TMA zero fill) stay 0: the bias must not reach them
+            const uint32_t live = grow < P.M ? 0xFFFFFFFFu : 0u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float lo = bf16_bits_to_f32(v[s4][i] & 0xFFFFu) + bf16_bits_to_f32(bw[i] & 0xFFFFu);
+              const float hi = bf16_bits_to_f32(v[s4][i] >> 16) + bf16_bits_to_f32(bw[i] >> 16);
+              v[s4][i] = relu_bf16x2(bf16x2_rn(lo, hi)) & live;
+            }
+            if (grow < P.M) {
+              uint8_t *dst = P.relu_out + (grow * P.relu_ld + bcol) * 2;
+              if (bcol + 8 <= P.N) {
+                *reinterpret_cast<uint4 *>(dst) = make_uint4(v[s4][0], v[s4][1], v[s4][2], v[s4][3]);
+              } else {
+                for (int i = 0; i < 8; ++i)
+                  if (bcol + i < P.N)
+                    reinterpret_cast<uint16_t *>(dst)[i] = (uint16_t)(v[s4][i >> 1] >> (16 * (i & 1)));
+              }
+            }
+          }
           if constexpr (QUANT) {
             uint32_t qw[2] = {0, 0};
 #pragma unroll
@@ -1060,7 +1123,8 @@ constexpr int onepass_tpp() {
   return Elt<DT_IN>::bytes == 1 && 2 * TPP2 * kTileM / NW <= kTileM ? 2 * TPP2 : TPP2;
 }
 
-template <int DT_IN, bool QUANT, bool PACK, int TPP2, int NW, int D, int A, int MINB = 2>
+template <int DT_IN, bool QUANT, bool PACK, int TPP2, int NW, int D, int A, int MINB = 2,
+          bool BIAS = false>
 static int launch_onepass(const CompressParams &P, cudaStream_t st) {
   constexpr int TPP = onepass_tpp<DT_IN, TPP2, NW>();
   using O = Onepass<DT_IN, QUANT, TPP, NW, D, A>;
@@ -1084,7 +1148,7 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return kNotApplicable;
-  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB>;
+  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS>;
   int resident = resident_ctas(reinterpret_cast<const void *>(kernel), O::SMEM, NW * 32);
   if (resident <= 0) return BS_ERR_LAUNCH;
   // a flush reads the counts of G - 1 partitions, at most 2 per thread
@@ -1194,13 +1258,15 @@ extern "C" size_t bs_compress_workspace_bytes(int64_t num_tiles) {
   return sizeof(WsHeader) + 8 * ((size_t)num_tiles / 512 + 1) + 2 * (size_t)num_tiles + 4;
 }
 
-extern "C" int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N, int64_t ld,
-                           const float *quant_scale, uint8_t *quant_out, uint8_t *bitmask,
-                           uint32_t *prefix, void *vals, int64_t vals_capacity, int pack_sbit,
-                           int64_t *arena_offset, int64_t *vals_offset_out, int64_t *nnz_out,
-                           void *workspace, size_t workspace_bytes, int32_t *status,
-                           void *stream) {
-  CompressParams P{};
+namespace bs {
+// Argument checks and parameter block shared by bs_compress and
+// bs_compress_bias_relu.
+static int setup_compress(CompressParams &P, const void *dense, int in_dtype, int64_t M,
+                          int64_t N, int64_t ld, const float *quant_scale, uint8_t *quant_out,
+                          uint8_t *bitmask, uint32_t *prefix, void *vals,
+                          int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
+                          int64_t *vals_offset_out, int64_t *nnz_out, void *workspace,
+                          size_t workspace_bytes, int32_t *status) {
   int rc = fill_common(P, dense, in_dtype, M, N, ld, 0);
   if (rc) return rc;
   const bool quant = quant_scale != nullptr;
@@ -1230,13 +1296,61 @@ extern "C" int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N
                                                      sizeof(WsHeader));
   P.counts_ws = reinterpret_cast<uint32_t *>(P.seg_ws + (P.num_parts + kSeg - 1) / kSeg);
   P.status = status;
+  return BS_OK;
+}
+}  // namespace bs
+
+extern "C" int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N, int64_t ld,
+                           const float *quant_scale, uint8_t *quant_out, uint8_t *bitmask,
+                           uint32_t *prefix, void *vals, int64_t vals_capacity, int pack_sbit,
+                           int64_t *arena_offset, int64_t *vals_offset_out, int64_t *nnz_out,
+                           void *workspace, size_t workspace_bytes, int32_t *status,
+                           void *stream) {
+  CompressParams P{};
+  const int rc = setup_compress(P, dense, in_dtype, M, N, ld, quant_scale, quant_out, bitmask,
+                                prefix, vals, vals_capacity, pack_sbit, arena_offset,
+                                vals_offset_out, nnz_out, workspace, workspace_bytes, status);
+  if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (P.num_tiles == 0) {
     // Empty tensor: prefix = [0]; arena offset, vals_offset_out, nnz_out untouched.
     if (cudaMemsetAsync(prefix, 0, sizeof(uint32_t), st) != cudaSuccess) return BS_ERR_LAUNCH;
     return BS_OK;
   }
-  return dispatch<0>(P, in_dtype, quant, pack_sbit, st);
+  return dispatch<0>(P, in_dtype, quant_scale != nullptr, pack_sbit, st);
+}
+
+extern "C" int bs_compress_bias_relu(const void *z, int64_t M, int64_t N, int64_t ld,
+                                     const void *bias, void *relu_out, int64_t relu_ld,
+                                     uint8_t *bitmask, uint32_t *prefix, void *vals,
+                                     int64_t vals_capacity, int pack_sbit,
+                                     int64_t *arena_offset, int64_t *vals_offset_out,
+                                     int64_t *nnz_out, void *workspace, size_t workspace_bytes,
+                                     int32_t *status, void *stream) {
+  CompressParams P{};
+  int rc = setup_compress(P, z, BS_BF16, M, N, ld, nullptr, nullptr, bitmask, prefix, vals,
+                          vals_capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out,
+                          workspace, workspace_bytes, status);
+  if (rc) return rc;
+  if (!bias || !relu_out) return BS_ERR_ARG;
+  if (relu_ld < N) return BS_ERR_SHAPE;
+  // 16-byte bias loads and dense stores
+  if ((reinterpret_cast<uintptr_t>(bias) & 15) || (reinterpret_cast<uintptr_t>(relu_out) & 15) ||
+      ((relu_ld * 2) & 15))
+    return BS_ERR_ALIGN;
+  P.bias = static_cast<const uint8_t *>(bias);
+  P.relu_out = static_cast<uint8_t *>(relu_out);
+  P.relu_ld = relu_ld;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (P.num_tiles == 0) {
+    if (cudaMemsetAsync(prefix, 0, sizeof(uint32_t), st) != cudaSuccess) return BS_ERR_LAUNCH;
+    return BS_OK;
+  }
+  // one pass only; BS_ERR_ALIGN when TMA cannot read z (the caller then
+  // applies bias and ReLU itself and calls bs_compress)
+  rc = pack_sbit ? launch_onepass<BS_BF16, false, true, 4, 8, 1, 1, 2, true>(P, st)
+                 : launch_onepass<BS_BF16, false, false, 4, 8, 1, 1, 2, true>(P, st);
+  return rc == kNotApplicable ? BS_ERR_ALIGN : rc;
 }
 
 // Reference compact_vals (lib_sparse/src/triton_operators.py:36-115): values

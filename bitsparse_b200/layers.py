@@ -15,7 +15,8 @@ from .bitsparse import BitsparseTensor, TensorBuffer
 from .config import RELU2_SCALE
 from .fp8 import is_fp8, matmul, to_fp8
 from .src.functions import dense_to_tilesparse, relu_to_tilesparse_fp8
-from .src.operators import mask_with_bitmask_, matmul_relu_mask, relu2_grad_sparse_
+from .src.operators import (compress_bias_relu, mask_with_bitmask_, matmul_relu_mask,
+                            relu2_grad_sparse_)
 from .src.sparse_matmul import AspB, AspRelu2B
 
 
@@ -50,16 +51,29 @@ class ReluLinear(Function):
 
     @staticmethod
     def forward(ctx, z, W, sparse_data: TensorBuffer | None = None, pack_sbit: bool = False,
-                dtype: torch.dtype = torch.bfloat16):
+                dtype: torch.dtype = torch.bfloat16, bias: Tensor | None = None):
+        """``bias`` (optional, not in the reference's signature): y =
+        relu(z + bias) @ W^T, with the bias add and the ReLU fused into the
+        compression pass for bf16 storage (one read of z)."""
         ctx.dtype = dtype
+        ctx.has_bias = bias is not None
         ctx.save_for_backward(W)
-        h = z.relu_()
-        if is_fp8(dtype):
-            h, h_sparse = relu_to_tilesparse_fp8(h, sparse_data, pack_sbit)
-            scale = h_sparse.scale
-        else:
+        fused = None
+        if bias is not None and not is_fp8(dtype):
+            fused = compress_bias_relu(z, bias, sparse_data, pack_sbit)
+        if fused is not None:
+            h, h_sparse = fused
             scale = None
-            h_sparse = dense_to_tilesparse(h, scale, sparse_data, pack_sbit)
+        else:
+            if bias is not None:
+                z = z + bias
+            h = z.relu_()
+            if is_fp8(dtype):
+                h, h_sparse = relu_to_tilesparse_fp8(h, sparse_data, pack_sbit)
+                scale = h_sparse.scale
+            else:
+                scale = None
+                h_sparse = dense_to_tilesparse(h, scale, sparse_data, pack_sbit)
         ctx.h_sparse = h_sparse
         return matmul(h, W.T, is_fp8(dtype), a_scale=scale)
 
@@ -83,7 +97,10 @@ class ReluLinear(Function):
             grad_z = mask_with_bitmask_(grad_h, h)
         else:
             grad_z = None
-        return grad_z, grad_W2, None, None, None
+        grad_bias = None
+        if ctx.has_bias and ctx.needs_input_grad[5]:
+            grad_bias = grad_z.sum(0) if grad_z is not None else None
+        return grad_z, grad_W2, None, None, None, grad_bias
 
 
 class FFNRelu:
@@ -98,9 +115,13 @@ class FFNRelu:
         bs_dims = x.shape[:-1]
         x = x.reshape(-1, x.shape[-1])
         z = matmul(x, W1.T, is_fp8(dtype))
-        if b1 is not None:
-            z = z + b1
-        y = ReluLinear.apply(z, W2, sparse_data, pack_sbit, dtype)
+        if b1 is not None and not is_fp8(dtype):
+            # bias add and ReLU fused into the compression pass
+            y = ReluLinear.apply(z, W2, sparse_data, pack_sbit, dtype, b1)
+        else:
+            if b1 is not None:
+                z = z + b1
+            y = ReluLinear.apply(z, W2, sparse_data, pack_sbit, dtype)
         y = y.reshape(*bs_dims, y.shape[-1])
         if b2 is not None:
             y = y + b2

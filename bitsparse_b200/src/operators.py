@@ -278,3 +278,68 @@ def matmul_relu_mask(a: Tensor, b: Tensor, sparse: BitsparseTensor | None = None
     _lib.call("bs_gemm_bf16_mask", a.data_ptr(), lda, b.data_ptr(), ldb, out.data_ptr(), N,
               M, N, K, mask or None, status.data_ptr(), _stream(a))
     return out
+
+
+def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: bool = False):
+    """Fused ``h = relu(z + bias)`` + compress of h in one pass over z (bf16).
+
+    Returns ``(h, BitsparseTensor)`` -- h dense (the FFN's second GEMM needs
+    it), the compressed form equal to ``compress(h, ...)`` -- or ``None``
+    when the one-pass kernel cannot read these tensors (alignment), in which
+    case the caller runs the steps separately.  Same storage modes as
+    ``compress`` (standalone, or a TensorBuffer arena).
+    """
+    if z.dtype != torch.bfloat16 or bias.dtype != torch.bfloat16:
+        return None
+    z, ld = _row_major(z, "z")
+    M, N = z.shape
+    bias = bias.contiguous()
+    if bias.numel() != N:
+        raise ValueError(f"bias has {bias.numel()} elements, z has {N} columns")
+    grid_m, grid_n, T, _, TB = tile_grid(M, N, _BM, _BN)
+    dev = z.device
+    if T == 0:
+        return None
+    bits = bits_per_value(torch.bfloat16)
+    h = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+    bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
+    prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
+    st = _stream(z)
+    ws = R.workspace(dev, T, st)
+    status = R.status_word(dev)
+    lib = _lib.load()
+    if sparse_data is None:
+        if pack_sbit:
+            tmp = torch.empty(packed_storage_nbytes(M * N, bits), device=dev, dtype=torch.uint8)
+        else:
+            tmp = torch.empty(M * N, device=dev, dtype=torch.bfloat16)
+        nnz_t = torch.empty((), device=dev, dtype=torch.int64)
+        rc = lib.bs_compress_bias_relu(z.data_ptr(), M, N, ld, bias.data_ptr(), h.data_ptr(), N,
+                                       bitmask.data_ptr(), prefix.data_ptr(), tmp.data_ptr(),
+                                       tmp.numel(), int(pack_sbit), None, None,
+                                       nnz_t.data_ptr(), ws.data_ptr(), ws.numel(),
+                                       status.data_ptr(), st)
+        if rc == _lib.BS_ERR_ALIGN:
+            return None
+        _lib.check(rc, "bs_compress_bias_relu")
+        nnz = int(nnz_t.item())  # host sync (triton_operators.py:50)
+        size = packed_storage_nbytes(nnz, bits) if pack_sbit else nnz
+        vals = tmp[:size].clone()
+        vals_offset = torch.zeros((), device=dev, dtype=torch.int64)
+    else:
+        vals = sparse_data.vals
+        if pack_sbit != bool(sparse_data.pack_sbit):
+            raise ValueError("pack_sbit must match the TensorBuffer's pack_sbit")
+        if not pack_sbit and vals.dtype != torch.bfloat16:
+            raise TypeError(f"TensorBuffer holds {vals.dtype}, values are bfloat16")
+        vals_offset = torch.empty(1, device=dev, dtype=torch.int64)
+        rc = lib.bs_compress_bias_relu(z.data_ptr(), M, N, ld, bias.data_ptr(), h.data_ptr(), N,
+                                       bitmask.data_ptr(), prefix.data_ptr(), vals.data_ptr(),
+                                       vals.numel(), int(pack_sbit),
+                                       sparse_data.offset.data_ptr(), vals_offset.data_ptr(),
+                                       None, ws.data_ptr(), ws.numel(), status.data_ptr(), st)
+        if rc == _lib.BS_ERR_ALIGN:
+            return None
+        _lib.check(rc, "bs_compress_bias_relu")
+    return h, BitsparseTensor(vals, bitmask, prefix, (M, N), torch.bfloat16, grid_m, grid_n,
+                              _BM, _BN, vals_offset=vals_offset, pack_sbit=pack_sbit)

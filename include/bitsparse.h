@@ -121,6 +121,23 @@ int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N,
                 int64_t *vals_offset_out, int64_t *nnz_out, void *workspace,
                 size_t workspace_bytes, int32_t *status, void *stream);
 
+/* Fused bias + ReLU + compress for bf16 input z [M, N]: h = relu(bf16(z +
+ * bias)) (the fp32 sum rounded once to bf16, as torch adds bf16 tensors;
+ * strictly negative values become +0, -0 and NaN pass through, as
+ * torch.relu), h written densely to relu_out [M, N] (row stride relu_ld)
+ * and compressed exactly as bs_compress compresses it -- one read of z.
+ * The forward of FFNRelu (lib_sparse/layers.py:84-94: z = x W1^T + b1,
+ * relu, compress) in one pass.  Needs the one-pass path (z, bias, relu_out
+ * and raw vals 16-byte aligned, row strides multiples of 16 bytes);
+ * returns BS_ERR_ALIGN otherwise, and the caller falls back to separate
+ * steps.  Other arguments as bs_compress. */
+int bs_compress_bias_relu(const void *z, int64_t M, int64_t N, int64_t ld,
+                          const void *bias, void *relu_out, int64_t relu_ld,
+                          uint8_t *bitmask, uint32_t *prefix, void *vals,
+                          int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
+                          int64_t *vals_offset_out, int64_t *nnz_out, void *workspace,
+                          size_t workspace_bytes, int32_t *status, void *stream);
+
 /* bs_compress without any device allocation, for callers that cannot call
  * cudaMalloc (code running inside an allocator or a hook where allocating is
  * forbidden, hosts without a device allocator).  No counterpart in the

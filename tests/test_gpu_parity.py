@@ -346,3 +346,32 @@ def test_large_arena_odd_offsets(dtype, pack):
     assert int(buf.offset.item()) == arena.offset
     np.testing.assert_array_equal(bits(buf.vals), arena.vals)
     B.check_status()
+
+
+@pytest.mark.parametrize("M, N", [(512, 1024), (200, 3000), (8192, 3072), (64, 64)])
+@pytest.mark.parametrize("pack", [False, True])
+def test_compress_bias_relu_equals_separate_steps(M, N, pack):
+    """Fused bias + ReLU + compress == torch's z + b, relu, then compress:
+    the dense h bit for bit and the compressed form bit for bit."""
+    from bitsparse_b200.src.operators import compress_bias_relu
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    z = torch.randn(M, N, generator=g, device="cuda").to(torch.bfloat16)
+    z[0, :5] = torch.tensor([0.0, -0.0, float("inf"), float("-inf"), 1e-30])
+    b = (0.5 * torch.randn(N, generator=g, device="cuda")).to(torch.bfloat16)
+    ref_h = torch.relu(z + b)
+    ref = dense_to_tilesparse(ref_h.clone(), None, None, pack)
+    out = compress_bias_relu(z, b, None, pack)
+    assert out is not None
+    h, sp = out
+    assert torch.equal(h.view(torch.int16), ref_h.view(torch.int16))
+    assert torch.equal(sp.bitmask, ref.bitmask)
+    assert torch.equal(sp.prefix.view(torch.int32), ref.prefix.view(torch.int32))
+    assert torch.equal(sp.vals.view(torch.uint8) if pack else sp.vals.view(torch.int16),
+                       ref.vals.view(torch.uint8) if pack else ref.vals.view(torch.int16))
+    # arena mode
+    buf = TensorBuffer(M * N * 2 + 64, device="cuda", dtype=torch.bfloat16, pack_sbit=pack)
+    buf.offset.fill_(5)
+    h2, sp2 = compress_bias_relu(z, b, buf, pack)
+    assert torch.equal(h2, h)
+    np.testing.assert_array_equal(bits(_reconstruct(sp2)), bits(ref_h))
+    B.check_status()
