@@ -38,6 +38,9 @@ _SIGS = {
     "bs_compress_noalloc": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i64,
                                    _i32, _vp, _vp, _vp, _vp, _vp]),
     "bs_compress_noalloc_max_tiles": (_sz, []),
+    "bs_compress_bias_relu_fp8": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+                                         _vp, _i64, _i32, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
+    "bs_fp8_scales_bias_relu": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "bs_compress_bias_relu": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i64,
                                      _i32, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     "bs_transpose_b8": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),

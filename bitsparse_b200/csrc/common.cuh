@@ -122,6 +122,23 @@ __device__ __forceinline__ uint32_t e4m3x2_bits(float a, float b) {
   return r;
 }
 
+// Two fp32 -> bf16 conversions, round to nearest even (the hardware
+// conversion; equal to torch's bf16 rounding for every non-NaN value).
+__device__ __forceinline__ uint32_t bf16x2_from_f32(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;
+// -0 and NaN unchanged.
+__device__ __forceinline__ uint32_t relu_bf16x2(uint32_t w) {
+  const uint32_t v = w & 0x7FFF7FFFu;
+  const uint32_t nz = v + 0x7FFF7FFFu;   // bit 15 of a half set iff v != 0
+  const uint32_t nan = v + 0x007F007Fu;  // bit 15 set iff v >= 0x7F81 (NaN)
+  const uint32_t kill = w & nz & ~nan & 0x80008000u;
+  return w & ~((kill >> 15) * 0xFFFFu);
+}
+
 // Positive test on raw bits (x > 0.0 as a float; NaN and -0 are not).
 template <int DT>
 __device__ __forceinline__ bool is_pos(uint32_t b) {

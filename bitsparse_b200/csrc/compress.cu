@@ -86,8 +86,11 @@ struct CompressParams {
   // one-pass bias + ReLU mode: the input is z, the compressed tensor is
   // relu(bf16(z + bias)), which is also written densely to relu_out
   const uint8_t *bias;  // bf16 [N]
-  uint8_t *relu_out;    // bf16 [M, N], row stride relu_ld
+  uint8_t *relu_out;    // bf16 [M, N], row stride relu_ld (optional with quant)
   int64_t relu_ld;
+  // with quant_out in bias + ReLU mode: quant_out receives e4m3(bf16(h * h)
+  // / *qscale2) (the FFN's squared activation) instead of e4m3(h / scale)
+  const float *qscale2;
 };
 
 template <int DT_IN, bool QUANT, int TPP>
@@ -710,23 +713,6 @@ __device__ __forceinline__ void emit_words(const CompressParams &P, const uint8_
   }
 }
 
-// Two fp32 -> bf16 conversions, round to nearest even (the hardware
-// conversion; equal to torch's bf16 rounding for every non-NaN value).
-__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-// torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;
-// -0 and NaN unchanged.
-__device__ __forceinline__ uint32_t relu_bf16x2(uint32_t w) {
-  const uint32_t v = w & 0x7FFF7FFFu;
-  const uint32_t nz = v + 0x7FFF7FFFu;   // bit 15 of a half set iff v != 0
-  const uint32_t nan = v + 0x007F007Fu;  // bit 15 set iff v >= 0x7F81 (NaN)
-  const uint32_t kill = w & nz & ~nan & 0x80008000u;
-  return w & ~((kill >> 15) * 0xFFFFu);
-}
-
 // Mask of 8 bf16 (4 words): bit i set iff element i > 0 (a bf16x2 compare
 // per word: NaN, -0 and +0 give 0).
 __device__ __forceinline__ uint32_t mask_bf16x8(const uint32_t (&w)[4]) {
@@ -820,6 +806,8 @@ __global__ void __launch_bounds__(NW * 32, MINB)
 
   const float qs = QUANT ? *P.qscale : 1.f;
   const float qr = QUANT ? __frcp_rn(qs) : 1.f;
+  const float qs2 = (QUANT && BIAS && P.qscale2 != nullptr) ? *P.qscale2 : 1.f;
+  const float qr2 = __frcp_rn(qs2);
   long long known_end = 0, known = -1;  // end (count) through this CTA's last flushed partition
   for (long long r = 0;; ++r) {
     const long long p = r * G + b;
@@ -906,9 +894,9 @@ __global__ void __launch_bounds__(NW * 32, MINB)
             for (int i = 0; i < 4; ++i) {
               const float lo = bf16_bits_to_f32(v[s4][i] & 0xFFFFu) + bf16_bits_to_f32(bw[i] & 0xFFFFu);
               const float hi = bf16_bits_to_f32(v[s4][i] >> 16) + bf16_bits_to_f32(bw[i] >> 16);
-              v[s4][i] = relu_bf16x2(bf16x2_rn(lo, hi)) & live;
+              v[s4][i] = relu_bf16x2(bf16x2_from_f32(lo, hi)) & live;
             }
-            if (grow < P.M) {
+            if (P.relu_out != nullptr && grow < P.M) {
               uint8_t *dst = P.relu_out + (grow * P.relu_ld + bcol) * 2;
               if (bcol + 8 <= P.N) {
                 *reinterpret_cast<uint4 *>(dst) = make_uint4(v[s4][0], v[s4][1], v[s4][2], v[s4][3]);
@@ -920,13 +908,31 @@ __global__ void __launch_bounds__(NW * 32, MINB)
             }
           }
           if constexpr (QUANT) {
-            uint32_t qw[2] = {0, 0};
+            uint32_t qw[2] = {0, 0}, side[2];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint32_t qq =
                   e4m3x2_bits(div_round_bf16(bf16_bits_to_f32(v[s4][i] & 0xFFFFu), qs, qr),
                               div_round_bf16(bf16_bits_to_f32(v[s4][i] >> 16), qs, qr));
               qw[i >> 1] |= qq << (16 * (i & 1));
+            }
+            side[0] = qw[0];
+            side[1] = qw[1];
+            if constexpr (BIAS) {
+              if (P.qscale2 != nullptr) {
+                // side output: e4m3(bf16(h * h) / scale2) (h.square_() then to_fp8)
+                side[0] = side[1] = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float h0 = bf16_bits_to_f32(v[s4][i] & 0xFFFFu);
+                  const float h1 = bf16_bits_to_f32(v[s4][i] >> 16);
+                  const float q0 = bf16_bits_to_f32(f32_to_bf16_bits(h0 * h0));
+                  const float q1 = bf16_bits_to_f32(f32_to_bf16_bits(h1 * h1));
+                  side[i >> 1] |= e4m3x2_bits(div_round_bf16(q0, qs2, qr2),
+                                              div_round_bf16(q1, qs2, qr2))
+                                  << (16 * (i & 1));
+                }
+              }
             }
             v[s4][0] = qw[0]; v[s4][1] = qw[1];
             if (P.qout) {
@@ -936,11 +942,11 @@ __global__ void __launch_bounds__(NW * 32, MINB)
               if (grow < P.M) {
                 uint8_t *qo = P.qout + grow * P.N + gcol;
                 if (P.qout_vec && gcol + 8 <= P.N) {
-                  *reinterpret_cast<uint2 *>(qo) = make_uint2(qw[0], qw[1]);
+                  *reinterpret_cast<uint2 *>(qo) = make_uint2(side[0], side[1]);
                 } else {
 #pragma unroll
                   for (int i = 0; i < 8; ++i)
-                    if (gcol + i < P.N) qo[i] = (uint8_t)(qw[i >> 2] >> (8 * (i & 3)));
+                    if (gcol + i < P.N) qo[i] = (uint8_t)(side[i >> 2] >> (8 * (i & 3)));
                 }
               }
             }
@@ -1350,6 +1356,35 @@ extern "C" int bs_compress_bias_relu(const void *z, int64_t M, int64_t N, int64_
   // applies bias and ReLU itself and calls bs_compress)
   rc = pack_sbit ? launch_onepass<BS_BF16, false, true, 4, 8, 1, 1, 2, true>(P, st)
                  : launch_onepass<BS_BF16, false, false, 4, 8, 1, 1, 2, true>(P, st);
+  return rc == kNotApplicable ? BS_ERR_ALIGN : rc;
+}
+
+extern "C" int bs_compress_bias_relu_fp8(const void *z, int64_t M, int64_t N, int64_t ld,
+                                         const void *bias, const float *scale_h,
+                                         const float *scale_side, uint8_t *side_out,
+                                         uint8_t *bitmask, uint32_t *prefix, void *vals,
+                                         int64_t vals_capacity, int pack_sbit,
+                                         int64_t *arena_offset, int64_t *vals_offset_out,
+                                         int64_t *nnz_out, void *workspace,
+                                         size_t workspace_bytes, int32_t *status,
+                                         void *stream) {
+  CompressParams P{};
+  if (!scale_h) return BS_ERR_ARG;
+  int rc = setup_compress(P, z, BS_BF16, M, N, ld, scale_h, side_out, bitmask, prefix, vals,
+                          vals_capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out,
+                          workspace, workspace_bytes, status);
+  if (rc) return rc;
+  if (!bias) return BS_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(bias) & 15) return BS_ERR_ALIGN;
+  P.bias = static_cast<const uint8_t *>(bias);
+  P.qscale2 = scale_side;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (P.num_tiles == 0) {
+    if (cudaMemsetAsync(prefix, 0, sizeof(uint32_t), st) != cudaSuccess) return BS_ERR_LAUNCH;
+    return BS_OK;
+  }
+  rc = pack_sbit ? launch_onepass<BS_BF16, true, true, 4, 8, 1, 1, 2, true>(P, st)
+                 : launch_onepass<BS_BF16, true, false, 4, 8, 1, 1, 2, true>(P, st);
   return rc == kNotApplicable ? BS_ERR_ALIGN : rc;
 }
 

@@ -60,6 +60,68 @@ __global__ void scale_kernel(uint32_t *amax_ws, float *scale_out) {
   *amax_ws = 0u;
 }
 
+// amax of h = relu(bf16(z + bias)) over a bf16 [M, N] tensor (row stride
+// ld), the input of to_fp8 in the fused FFN forward: bias add and ReLU as
+// torch computes them, no h materialised.
+__global__ void __launch_bounds__(kThreads)
+amax_bias_relu_kernel(const uint8_t *z, int64_t M, int64_t N, int64_t ld, const uint8_t *bias,
+                      uint32_t *amax_ws) {
+  const int64_t cpr = (N + 7) / 8;  // 8-column chunks per row
+  const int64_t nch = M * cpr;
+  const bool vec = (N % 8 == 0) && (ld % 8 == 0);
+  float m = 0.f;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nch; i += stride) {
+    const int64_t r = i / cpr, c0 = (i - r * cpr) * 8;
+    uint32_t zw[4] = {0, 0, 0, 0}, bw[4] = {0, 0, 0, 0};
+    if (vec) {
+      const uint4 v = ld_nc_v4(z + (r * ld + c0) * 2);
+      const uint4 b = *reinterpret_cast<const uint4 *>(bias + c0 * 2);
+      zw[0] = v.x; zw[1] = v.y; zw[2] = v.z; zw[3] = v.w;
+      bw[0] = b.x; bw[1] = b.y; bw[2] = b.z; bw[3] = b.w;
+    } else {
+      for (int e = 0; e < 8 && c0 + e < N; ++e) {
+        zw[e >> 1] |= (uint32_t)reinterpret_cast<const uint16_t *>(z)[r * ld + c0 + e] << (16 * (e & 1));
+        bw[e >> 1] |= (uint32_t)reinterpret_cast<const uint16_t *>(bias)[c0 + e] << (16 * (e & 1));
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float lo = bf16_bits_to_f32(zw[q] & 0xFFFFu) + bf16_bits_to_f32(bw[q] & 0xFFFFu);
+      const float hi = bf16_bits_to_f32(zw[q] >> 16) + bf16_bits_to_f32(bw[q] >> 16);
+      const uint32_t h = relu_bf16x2(bf16x2_from_f32(lo, hi));
+      m = fmaxf(m, fabsf(bf16_bits_to_f32(h & 0xFFFFu)));
+      m = fmaxf(m, fabsf(bf16_bits_to_f32(h >> 16)));
+    }
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, d));
+  __shared__ float s_m[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) s_m[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.f;
+    for (int i = 0; i < kThreads / 32; ++i) b = fmaxf(b, s_m[i]);
+    atomicMax(amax_ws, __float_as_uint(b));  // non-negative floats order as uints
+  }
+}
+
+// The to_fp8 scales of h (bf16) and of h2 = bf16(h * h) from amax(h): h2 is
+// a non-decreasing function of h >= 0 and rounding is monotonic, so
+// amax(h2) = bf16(amax(h)^2) exactly; both scales follow scale_kernel's
+// bf16 rule.  Resets the scratch word.
+__global__ void scales_relu2_kernel(uint32_t *amax_ws, float *scale_h, float *scale_h2) {
+  const float amax = __uint_as_float(*amax_ws);
+  float s = bf16_bits_to_f32(f32_to_bf16_bits(__fdiv_rn(amax, 448.0f)));
+  *scale_h = fmaxf(s, 1e-9f);
+  if (scale_h2) {
+    const float a2 = bf16_bits_to_f32(f32_to_bf16_bits(amax * amax));
+    s = bf16_bits_to_f32(f32_to_bf16_bits(__fdiv_rn(a2, 448.0f)));
+    *scale_h2 = fmaxf(s, 1e-9f);
+  }
+  *amax_ws = 0u;
+}
+
 // q = e4m3(x / scale) over a flat tensor (the quantise half of to_fp8).
 template <int DT>
 __global__ void __launch_bounds__(kThreads)
@@ -187,6 +249,22 @@ extern "C" int bs_fp8_scale(const void *x, int dtype, int64_t numel, uint32_t *a
     amax_kernel<BS_F32><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, amax_ws);
     scale_kernel<BS_F32><<<1, 1, 0, st>>>(amax_ws, scale_out);
   }
+  return launch_err();
+}
+
+extern "C" int bs_fp8_scales_bias_relu(const void *z, int64_t M, int64_t N, int64_t ld,
+                                       const void *bias, uint32_t *amax_ws, float *scale_h,
+                                       float *scale_h2, void *stream) {
+  if (M < 0 || N < 0 || ld < N) return BS_ERR_SHAPE;
+  if (!amax_ws || !scale_h || !bias || (M > 0 && N > 0 && !z)) return BS_ERR_ARG;
+  if (!aligned16(z) || !aligned16(bias)) return BS_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t blocks = (M * ((N + 7) / 8) + kThreads - 1) / kThreads;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  amax_bias_relu_kernel<<<(unsigned)blocks, kThreads, 0, st>>>(
+      static_cast<const uint8_t *>(z), M, N, ld, static_cast<const uint8_t *>(bias), amax_ws);
+  scales_relu2_kernel<<<1, 1, 0, st>>>(amax_ws, scale_h, scale_h2);
   return launch_err();
 }
 

@@ -15,8 +15,8 @@ from .bitsparse import BitsparseTensor, TensorBuffer
 from .config import RELU2_SCALE
 from .fp8 import is_fp8, matmul, to_fp8
 from .src.functions import dense_to_tilesparse, relu_to_tilesparse_fp8
-from .src.operators import (compress_bias_relu, mask_with_bitmask_, matmul_relu_mask,
-                            relu2_grad_sparse_)
+from .src.operators import (compress_bias_relu, compress_bias_relu_fp8, mask_with_bitmask_,
+                            matmul_relu_mask, relu2_grad_sparse_)
 from .src.sparse_matmul import AspB, AspRelu2B
 
 
@@ -59,12 +59,16 @@ class ReluLinear(Function):
         ctx.has_bias = bias is not None
         ctx.save_for_backward(W)
         fused = None
-        if bias is not None and not is_fp8(dtype):
+        if bias is not None and is_fp8(dtype):
+            fused = compress_bias_relu_fp8(z, bias, sparse_data, pack_sbit)
+            if fused is not None:
+                h, scale, h_sparse = fused
+        elif bias is not None:
             fused = compress_bias_relu(z, bias, sparse_data, pack_sbit)
-        if fused is not None:
-            h, h_sparse = fused
-            scale = None
-        else:
+            if fused is not None:
+                h, h_sparse = fused
+                scale = None
+        if fused is None:
             if bias is not None:
                 z = z + bias
             h = z.relu_()
@@ -115,7 +119,7 @@ class FFNRelu:
         bs_dims = x.shape[:-1]
         x = x.reshape(-1, x.shape[-1])
         z = matmul(x, W1.T, is_fp8(dtype))
-        if b1 is not None and not is_fp8(dtype):
+        if b1 is not None:
             # bias add and ReLU fused into the compression pass
             y = ReluLinear.apply(z, W2, sparse_data, pack_sbit, dtype, b1)
         else:
@@ -134,18 +138,37 @@ class Relu2Linear(Function):
 
     @staticmethod
     def forward(ctx, z, W, sparse_data: TensorBuffer | None, pack_sbit: bool = False,
-                storage_dtype: torch.dtype = torch.bfloat16):
+                storage_dtype: torch.dtype = torch.bfloat16, bias: Tensor | None = None):
+        """``bias`` (optional, not in the reference's signature): relu(z +
+        bias), with the bias add, the ReLU, the fp8 quantisations and the
+        square fused into the compression passes."""
         ctx.dtype = storage_dtype
+        ctx.has_bias = bias is not None
         ctx.save_for_backward(W)
+        fp8 = is_fp8(storage_dtype)
+        if bias is not None and fp8:
+            fused = compress_bias_relu_fp8(z, bias, sparse_data, pack_sbit, square=True)
+            if fused is not None:  # the GEMM operand to_fp8(relu(z + b)^2), stored relu
+                h2_fp8, h2_scale, ctx.h_sparse = fused
+                return matmul(h2_fp8, W.T, True, a_scale=h2_scale)
+        elif bias is not None:
+            fused = compress_bias_relu(z, bias, sparse_data, pack_sbit)
+            if fused is not None:
+                h, ctx.h_sparse = fused
+                h.square_()
+                h.mul_(RELU2_SCALE)
+                return matmul(h, W.T, False)
+        if bias is not None:
+            z = z + bias
         h = z.relu_()
-        if is_fp8(storage_dtype):
+        if fp8:
             _, h_sparse = relu_to_tilesparse_fp8(h, sparse_data, pack_sbit)
         else:
             h_sparse = dense_to_tilesparse(h, None, sparse_data, pack_sbit)
         ctx.h_sparse = h_sparse
         h.square_()
         h.mul_(RELU2_SCALE)
-        return matmul(h, W.T, is_fp8(storage_dtype))
+        return matmul(h, W.T, fp8)
 
     @staticmethod
     @torch.compiler.disable
@@ -165,7 +188,10 @@ class Relu2Linear(Function):
             grad_z = relu2_grad_sparse_(grad_h, h)
         else:
             grad_z = None
-        return grad_z, grad_W2, None, None, None
+        grad_bias = None
+        if ctx.has_bias and ctx.needs_input_grad[5] and grad_z is not None:
+            grad_bias = grad_z.sum(0)
+        return grad_z, grad_W2, None, None, None, grad_bias
 
 
 class FFNRelu2:
@@ -180,9 +206,10 @@ class FFNRelu2:
         bs_dims = x.shape[:-1]
         x = x.reshape(-1, x.shape[-1])
         z = matmul(x, W1.T, is_fp8(storage_dtype))
-        if b1 is not None:
-            z = z + b1
-        y = Relu2Linear.apply(z, W2, sparse_data, pack_sbit, storage_dtype)
+        if b1 is not None:  # bias add fused into the compression passes
+            y = Relu2Linear.apply(z, W2, sparse_data, pack_sbit, storage_dtype, b1)
+        else:
+            y = Relu2Linear.apply(z, W2, sparse_data, pack_sbit, storage_dtype)
         y = y.reshape(*bs_dims, y.shape[-1])
         if b2 is not None:
             y = y + b2

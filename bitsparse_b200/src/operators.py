@@ -280,6 +280,48 @@ def matmul_relu_mask(a: Tensor, b: Tensor, sparse: BitsparseTensor | None = None
     return out
 
 
+def _fused_compress(fn, head: tuple, tail: tuple, dev, stored, M: int, N: int, T: int,
+                    bitmask: Tensor, prefix: Tensor, sparse_data, pack_sbit: bool):
+    """Run a fused compress entry point ``fn(*head, bitmask, prefix, vals,
+    capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out, workspace,
+    workspace_bytes, status, stream)`` in either storage mode.  Returns
+    (vals, vals_offset), or None when the entry point reports BS_ERR_ALIGN
+    (the one-pass kernel cannot read the tensors)."""
+    bits = bits_per_value(stored)
+    st = _stream(head[0]) if isinstance(head[0], Tensor) else R.stream_handle(dev)
+    ws = R.workspace(dev, T, st)
+    status = R.status_word(dev)
+    head = tuple(h.data_ptr() if isinstance(h, Tensor) else h for h in head)
+    if sparse_data is None:
+        if pack_sbit:
+            tmp = torch.empty(packed_storage_nbytes(M * N, bits), device=dev, dtype=torch.uint8)
+        else:
+            tmp = torch.empty(M * N, device=dev, dtype=stored)
+        nnz_t = torch.empty((), device=dev, dtype=torch.int64)
+        rc = fn(*head, bitmask.data_ptr(), prefix.data_ptr(), tmp.data_ptr(), tmp.numel(),
+                int(pack_sbit), None, None, nnz_t.data_ptr(), ws.data_ptr(), ws.numel(),
+                status.data_ptr(), st)
+        if rc == _lib.BS_ERR_ALIGN:
+            return None
+        _lib.check(rc, fn.__name__)
+        nnz = int(nnz_t.item())  # host sync (triton_operators.py:50)
+        size = packed_storage_nbytes(nnz, bits) if pack_sbit else nnz
+        return tmp[:size].clone(), torch.zeros((), device=dev, dtype=torch.int64)
+    vals = sparse_data.vals
+    if pack_sbit != bool(sparse_data.pack_sbit):
+        raise ValueError("pack_sbit must match the TensorBuffer's pack_sbit")
+    if not pack_sbit and vals.dtype != stored:
+        raise TypeError(f"TensorBuffer holds {vals.dtype}, values are {stored}")
+    vals_offset = torch.empty(1, device=dev, dtype=torch.int64)
+    rc = fn(*head, bitmask.data_ptr(), prefix.data_ptr(), vals.data_ptr(), vals.numel(),
+            int(pack_sbit), sparse_data.offset.data_ptr(), vals_offset.data_ptr(), None,
+            ws.data_ptr(), ws.numel(), status.data_ptr(), st)
+    if rc == _lib.BS_ERR_ALIGN:
+        return None
+    _lib.check(rc, fn.__name__)
+    return vals, vals_offset
+
+
 def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: bool = False):
     """Fused ``h = relu(z + bias)`` + compress of h in one pass over z (bf16).
 
@@ -297,49 +339,62 @@ def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: boo
     if bias.numel() != N:
         raise ValueError(f"bias has {bias.numel()} elements, z has {N} columns")
     grid_m, grid_n, T, _, TB = tile_grid(M, N, _BM, _BN)
-    dev = z.device
     if T == 0:
         return None
-    bits = bits_per_value(torch.bfloat16)
+    dev = z.device
     h = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
     bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
     prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
-    st = _stream(z)
-    ws = R.workspace(dev, T, st)
-    status = R.status_word(dev)
-    lib = _lib.load()
-    if sparse_data is None:
-        if pack_sbit:
-            tmp = torch.empty(packed_storage_nbytes(M * N, bits), device=dev, dtype=torch.uint8)
-        else:
-            tmp = torch.empty(M * N, device=dev, dtype=torch.bfloat16)
-        nnz_t = torch.empty((), device=dev, dtype=torch.int64)
-        rc = lib.bs_compress_bias_relu(z.data_ptr(), M, N, ld, bias.data_ptr(), h.data_ptr(), N,
-                                       bitmask.data_ptr(), prefix.data_ptr(), tmp.data_ptr(),
-                                       tmp.numel(), int(pack_sbit), None, None,
-                                       nnz_t.data_ptr(), ws.data_ptr(), ws.numel(),
-                                       status.data_ptr(), st)
-        if rc == _lib.BS_ERR_ALIGN:
-            return None
-        _lib.check(rc, "bs_compress_bias_relu")
-        nnz = int(nnz_t.item())  # host sync (triton_operators.py:50)
-        size = packed_storage_nbytes(nnz, bits) if pack_sbit else nnz
-        vals = tmp[:size].clone()
-        vals_offset = torch.zeros((), device=dev, dtype=torch.int64)
-    else:
-        vals = sparse_data.vals
-        if pack_sbit != bool(sparse_data.pack_sbit):
-            raise ValueError("pack_sbit must match the TensorBuffer's pack_sbit")
-        if not pack_sbit and vals.dtype != torch.bfloat16:
-            raise TypeError(f"TensorBuffer holds {vals.dtype}, values are bfloat16")
-        vals_offset = torch.empty(1, device=dev, dtype=torch.int64)
-        rc = lib.bs_compress_bias_relu(z.data_ptr(), M, N, ld, bias.data_ptr(), h.data_ptr(), N,
-                                       bitmask.data_ptr(), prefix.data_ptr(), vals.data_ptr(),
-                                       vals.numel(), int(pack_sbit),
-                                       sparse_data.offset.data_ptr(), vals_offset.data_ptr(),
-                                       None, ws.data_ptr(), ws.numel(), status.data_ptr(), st)
-        if rc == _lib.BS_ERR_ALIGN:
-            return None
-        _lib.check(rc, "bs_compress_bias_relu")
+    out = _fused_compress(_lib.load().bs_compress_bias_relu, (z, M, N, ld, bias, h, N), (),
+                          dev, torch.bfloat16, M, N, T, bitmask, prefix, sparse_data, pack_sbit)
+    if out is None:
+        return None
+    vals, vals_offset = out
     return h, BitsparseTensor(vals, bitmask, prefix, (M, N), torch.bfloat16, grid_m, grid_n,
                               _BM, _BN, vals_offset=vals_offset, pack_sbit=pack_sbit)
+
+
+def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: bool = False,
+                           square: bool = False):
+    """FP8 form of ``compress_bias_relu``: h = relu(z + bias) is stored as
+    ``to_fp8(h)`` (lib_sparse/layers.py:32-37, 112-117) and compressed, in two
+    passes over z (the amax of h, then quantise + compress).
+
+    Returns ``(side, side_scale, BitsparseTensor)``: ``side`` is the dense
+    e4m3 operand of the FFN's second GEMM -- ``to_fp8(h)`` or, with
+    ``square``, ``to_fp8(h * h)`` (Relu2Linear, RELU2_SCALE = 1) -- or
+    ``None`` when the one-pass kernel cannot read the tensors.
+    """
+    from ..config import RELU2_SCALE
+    if z.dtype != torch.bfloat16 or bias.dtype != torch.bfloat16:
+        return None
+    if square and RELU2_SCALE != 1:
+        return None  # the fused square assumes k = 1 (config.py)
+    z, ld = _row_major(z, "z")
+    M, N = z.shape
+    bias = bias.contiguous()
+    if bias.numel() != N:
+        raise ValueError(f"bias has {bias.numel()} elements, z has {N} columns")
+    grid_m, grid_n, T, _, TB = tile_grid(M, N, _BM, _BN)
+    if T == 0 or z.data_ptr() % 16 or bias.data_ptr() % 16:
+        return None
+    dev = z.device
+    lib = _lib.load()
+    st = _stream(z)
+    scale_h = torch.empty((), device=dev, dtype=torch.float32)
+    scale_s = torch.empty((), device=dev, dtype=torch.float32) if square else None
+    _lib.check(lib.bs_fp8_scales_bias_relu(z.data_ptr(), M, N, ld, bias.data_ptr(),
+                                           R.amax_scratch(dev).data_ptr(), scale_h.data_ptr(),
+                                           R.ptr(scale_s), st), "bs_fp8_scales_bias_relu")
+    side = torch.empty((M, N), device=dev, dtype=torch.float8_e4m3fn)
+    bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
+    prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
+    out = _fused_compress(lib.bs_compress_bias_relu_fp8,
+                          (z, M, N, ld, bias, scale_h, scale_s, side), (), dev,
+                          torch.float8_e4m3fn, M, N, T, bitmask, prefix, sparse_data, pack_sbit)
+    if out is None:
+        return None
+    vals, vals_offset = out
+    sp = BitsparseTensor(vals, bitmask, prefix, (M, N), torch.float8_e4m3fn, grid_m, grid_n,
+                         _BM, _BN, scale=scale_h, vals_offset=vals_offset, pack_sbit=pack_sbit)
+    return side, (scale_s if square else scale_h), sp

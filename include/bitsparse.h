@@ -138,6 +138,31 @@ int bs_compress_bias_relu(const void *z, int64_t M, int64_t N, int64_t ld,
                           int64_t *vals_offset_out, int64_t *nnz_out, void *workspace,
                           size_t workspace_bytes, int32_t *status, void *stream);
 
+/* FP8 form of bs_compress_bias_relu: h = relu(bf16(z + bias)) quantised to
+ * e4m3 with *scale_h (to_fp8's quantiser, lib_sparse/fp8.py:127) and
+ * compressed; side_out (optional, e4m3 [M, N], row stride N) receives the
+ * quantised h, or with scale_side != NULL the quantised squared activation
+ * e4m3(bf16(h * h) / *scale_side) (Relu2Linear's GEMM input,
+ * lib_sparse/layers.py:118-123).  The scales come from
+ * bs_fp8_scales_bias_relu.  BS_ERR_ALIGN when the one-pass kernel cannot
+ * read z. */
+int bs_compress_bias_relu_fp8(const void *z, int64_t M, int64_t N, int64_t ld,
+                              const void *bias, const float *scale_h,
+                              const float *scale_side, uint8_t *side_out,
+                              uint8_t *bitmask, uint32_t *prefix, void *vals,
+                              int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
+                              int64_t *vals_offset_out, int64_t *nnz_out, void *workspace,
+                              size_t workspace_bytes, int32_t *status, void *stream);
+
+/* to_fp8 scales for the fused FFN forward without materialising h =
+ * relu(bf16(z + bias)): *scale_h = max(bf16(amax(h) / 448), 1e-9) and,
+ * with scale_h2 != NULL, the same rule for h2 = bf16(h * h), whose amax is
+ * bf16(amax(h)^2) (rounding is monotonic and h >= 0).  One pass over z;
+ * amax_ws as in bs_fp8_scale. */
+int bs_fp8_scales_bias_relu(const void *z, int64_t M, int64_t N, int64_t ld,
+                            const void *bias, uint32_t *amax_ws, float *scale_h,
+                            float *scale_h2, void *stream);
+
 /* bs_compress without any device allocation, for callers that cannot call
  * cudaMalloc (code running inside an allocator or a hook where allocating is
  * forbidden, hosts without a device allocator).  No counterpart in the
