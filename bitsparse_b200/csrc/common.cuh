@@ -97,20 +97,12 @@ __device__ __forceinline__ uint32_t f32_to_e4m3_bits(float f) {
   return s | q;
 }
 
-// bf16(x / s) as fp32 with the quotient rounded exactly as IEEE division then
-// round-to-nearest-even bf16 would: y1 = x*r corrected by one FMA residual
-// step is within 1 fp32 ulp of the true quotient, so rounding it to bf16 can
-// only differ from rounding the exact quotient when it lies within an ulp or
-// two of a bf16 rounding midpoint (low 16 bits near 0x8000); those rare
-// quotients are recomputed with the exact division.  r = 1/s rounded.
-__device__ __forceinline__ float div_round_bf16(float x, float s, float r) {
-  const float y0 = x * r;
-  const float e = fmaf(-y0, s, x);  // exact residual
-  const float y1 = fmaf(e, r, y0);
-  const uint32_t lo = __float_as_uint(y1) & 0xFFFFu;
-  // s > 0: the quotient has x's sign (keeps -0, which the residual loses)
-  const float y = (lo - 0x7FFCu <= 8u) ? __fdiv_rn(x, s) : copysignf(y1, x);
-  return bf16_bits_to_f32(f32_to_bf16_bits(y));
+// Two fp32 -> bf16 conversions, round to nearest even (the hardware
+// conversion, which torch's bf16 conversion on CUDA also uses).
+__device__ __forceinline__ uint32_t bf16x2_from_f32(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // Two fp32 values that are already representable-range e4m3 inputs (|v| <=
@@ -122,13 +114,27 @@ __device__ __forceinline__ uint32_t e4m3x2_bits(float a, float b) {
   return r;
 }
 
-// Two fp32 -> bf16 conversions, round to nearest even (the hardware
-// conversion; equal to torch's bf16 rounding for every non-NaN value).
-__device__ __forceinline__ uint32_t bf16x2_from_f32(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
+// x / s in fp32, close enough that rounding it to bf16 gives bf16(x / s) of
+// the exact IEEE quotient: y1 = x*r corrected by one FMA residual step is
+// within 1 fp32 ulp of the true quotient, so its bf16 rounding can only
+// differ from the exact one when it lies within an ulp or two of a bf16
+// rounding midpoint (low 16 bits near 0x8000); those rare quotients are
+// recomputed with the exact division.  r = 1/s rounded, s > 0.
+__device__ __forceinline__ float quotient_fp32(float x, float s, float r) {
+  const float y0 = x * r;
+  const float e = fmaf(-y0, s, x);  // exact residual
+  const float y1 = fmaf(e, r, y0);
+  const uint32_t lo = __float_as_uint(y1) & 0xFFFFu;
+  // the quotient has x's sign (keeps -0, which the residual loses)
+  return (lo - 0x7FFCu <= 8u) ? __fdiv_rn(x, s) : copysignf(y1, x);
 }
+
+// to_fp8's quantiser on two bf16 values (as fp32): e4m3(bf16(x / s)).
+__device__ __forceinline__ uint32_t div_e4m3x2(float x0, float x1, float s, float r) {
+  const uint32_t b = bf16x2_from_f32(quotient_fp32(x0, s, r), quotient_fp32(x1, s, r));
+  return e4m3x2_bits(bf16_bits_to_f32(b & 0xFFFFu), bf16_bits_to_f32(b >> 16));
+}
+
 // torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;
 // -0 and NaN unchanged.
 __device__ __forceinline__ uint32_t relu_bf16x2(uint32_t w) {

@@ -197,9 +197,9 @@ __device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64
       const float r = __frcp_rn(qs);
 #pragma unroll
       for (int e = 0; e < C::VEC; e += 2) {
-        const float y0 = div_round_bf16(bf16_bits_to_f32((raw[e >> 1] & 0xFFFFu)), qs, r);
-        const float y1 = div_round_bf16(bf16_bits_to_f32(raw[e >> 1] >> 16), qs, r);
-        sv[e >> 2] |= e4m3x2_bits(y0, y1) << (8 * (e & 3));
+        sv[e >> 2] |= div_e4m3x2(bf16_bits_to_f32(raw[e >> 1] & 0xFFFFu),
+                                 bf16_bits_to_f32(raw[e >> 1] >> 16), qs, r)
+                      << (8 * (e & 3));
       }
     } else {
 #pragma unroll
@@ -911,9 +911,8 @@ __global__ void __launch_bounds__(NW * 32, MINB)
             uint32_t qw[2] = {0, 0}, side[2];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const uint32_t qq =
-                  e4m3x2_bits(div_round_bf16(bf16_bits_to_f32(v[s4][i] & 0xFFFFu), qs, qr),
-                              div_round_bf16(bf16_bits_to_f32(v[s4][i] >> 16), qs, qr));
+              const uint32_t qq = div_e4m3x2(bf16_bits_to_f32(v[s4][i] & 0xFFFFu),
+                                             bf16_bits_to_f32(v[s4][i] >> 16), qs, qr);
               qw[i >> 1] |= qq << (16 * (i & 1));
             }
             side[0] = qw[0];
@@ -926,10 +925,9 @@ __global__ void __launch_bounds__(NW * 32, MINB)
                 for (int i = 0; i < 4; ++i) {
                   const float h0 = bf16_bits_to_f32(v[s4][i] & 0xFFFFu);
                   const float h1 = bf16_bits_to_f32(v[s4][i] >> 16);
-                  const float q0 = bf16_bits_to_f32(f32_to_bf16_bits(h0 * h0));
-                  const float q1 = bf16_bits_to_f32(f32_to_bf16_bits(h1 * h1));
-                  side[i >> 1] |= e4m3x2_bits(div_round_bf16(q0, qs2, qr2),
-                                              div_round_bf16(q1, qs2, qr2))
+                  const uint32_t sq = bf16x2_from_f32(h0 * h0, h1 * h1);  // h.square_()
+                  side[i >> 1] |= div_e4m3x2(bf16_bits_to_f32(sq & 0xFFFFu),
+                                             bf16_bits_to_f32(sq >> 16), qs2, qr2)
                                   << (16 * (i & 1));
                 }
               }

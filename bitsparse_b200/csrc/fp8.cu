@@ -159,9 +159,8 @@ quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q) {
       // fast e4m3 conversion applies (NaN stays NaN).
 #pragma unroll
       for (int e = 0; e < 8; e += 2) {
-        const float y0 = div_round_bf16(bf16_bits_to_f32(b[e]), s, r);
-        const float y1 = div_round_bf16(bf16_bits_to_f32(b[e + 1]), s, r);
-        o[e >> 2] |= e4m3x2_bits(y0, y1) << (8 * (e & 3));
+        o[e >> 2] |= div_e4m3x2(bf16_bits_to_f32(b[e]), bf16_bits_to_f32(b[e + 1]), s, r)
+                     << (8 * (e & 3));
       }
     } else {
 #pragma unroll
