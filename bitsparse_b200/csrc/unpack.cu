@@ -39,6 +39,7 @@ struct UnpackParams {
   int64_t grid_n, K, batch_rows;
   const float *scale;
   float k;       // RELU2_SCALE
+  const float *qscale;  // OUT 2: to_fp8 scale of the ReLU^2 reconstruction
   int vals_v16;  // vals base 16-byte aligned
   int out_v32;   // out base + row stride allow 32-byte accesses
 };
@@ -194,13 +195,18 @@ struct PidPos {
   }
 };
 
-// OUT: 0 = elements of SDT (plain reconstruct), 1 = bf16 k*r^2 (ReLU^2).
+// OUT: 0 = elements of SDT (plain reconstruct), 1 = bf16 k*r^2 (ReLU^2),
+// 2 = the ReLU^2 reconstruction quantised to e4m3 with *qscale (to_fp8's
+// quantiser) and written transposed (out is [K, batch_rows]) -- the B
+// operand of the fp8 dW GEMM in the column-major order cuBLASLt wants.
 template <int SDT, bool PACK, int OUT, bool SCALE>
 __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) {
-  constexpr int OB = OUT ? 2 : Elt<SDT>::bytes;  // output element bytes
+  constexpr int OB = OUT == 1 ? 2 : (OUT == 2 ? 1 : Elt<SDT>::bytes);  // output element bytes
   using G = Chunk<OB>;
+  constexpr int kTP = 80;  // OUT 2: pitch of a transposed tile column in smem
   __shared__ __align__(16) uint8_t stage[kStageBytes];
   __shared__ uint32_t s_wt[G::S * 8];
+  __shared__ __align__(16) uint8_t tstage[OUT == 2 ? kUT * kTileN * kTP : 16];
 
   const int64_t pid0 = (int64_t)blockIdx.x * kUT;
   const int nt = tiles_here(P, pid0);
@@ -225,6 +231,11 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
   if constexpr (SCALE) {
     const float sc = *P.scale;
     s2 = bf16_bits_to_f32(f32_to_bf16_bits(sc * sc));  // scale.square(), cast to bf16
+  }
+  float qs = 1.f, qr = 1.f;
+  if constexpr (OUT == 2) {
+    qs = *P.qscale;
+    qr = __frcp_rn(qs);
   }
 #pragma unroll
   for (int s = 0; s < G::S; ++s) {
@@ -258,7 +269,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
       if constexpr (OUT == 0 && !PACK) break;
       if (!((mm >> e) & 1u)) continue;
       uint32_t v = staged_value<SDT, PACK>(stage, first, r++);
-      if constexpr (OUT == 1) {
+      if constexpr (OUT >= 1) {
         if constexpr (SDT == BS_BF16) {
           // bf16 * bf16 in bf16 (triton_kernels.py:238): k*v rounded, then *v
           const float x = bf16_bits_to_f32(v);
@@ -269,9 +280,17 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
           v = f32_to_bf16_bits(P.k * x * x);
         }
         if constexpr (SCALE) v = f32_to_bf16_bits(bf16_bits_to_f32(v) * s2);
+        if constexpr (OUT == 2)  // e4m3(bf16(v / qscale)), as to_fp8 on the bf16 tensor
+          v = div_e4m3x2(bf16_bits_to_f32(v), 0.f, qs, qr) & 0xFFu;
       }
       if constexpr (OB == 1) w[e >> 2] |= v << (8 * (e & 3));
       else w[e >> 1] |= v << (16 * (e & 1));
+    }
+    if constexpr (OUT == 2) {  // into the transposed staging tile: column (colc*32+e), row
+#pragma unroll
+      for (int e = 0; e < G::VEC; ++e)
+        tstage[(j * kTileN + colc * G::VEC + e) * kTP + row] = (uint8_t)(w[e >> 2] >> (8 * (e & 3)));
+      continue;
     }
     uint8_t *dst = P.out + (grow * P.out_ld + gcol) * OB;
     if (P.out_v32 && gcol + G::VEC <= P.K) {
@@ -281,6 +300,28 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
         if (gcol + e >= P.K) break;
         if constexpr (OB == 1) dst[e] = (w[e >> 2] >> (8 * (e & 3))) & 0xFFu;
         else reinterpret_cast<uint16_t *>(dst)[e] = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+      }
+    }
+  }
+  if constexpr (OUT == 2) {
+    // each tile leaves as 64 rows (its columns) of 64 bytes (its rows):
+    // thread -> column tid / 4, rows 16 * (tid % 4) .. + 15, one 16-byte store
+    __syncthreads();
+    const int c = tid >> 2, r0 = (tid & 3) * 16;
+    for (int j = 0; j < nt; ++j) {
+      int64_t tr, tc;
+      pp.pos(j, tr, tc);
+      const int64_t ocol = tc * kTileN + c;    // output row  (a column of the tensor)
+      const int64_t orow = tr * kTileM + r0;   // output column (a row of the tensor)
+      if (ocol >= P.K || orow >= P.batch_rows) continue;
+      const uint4 v = *reinterpret_cast<const uint4 *>(tstage + (j * kTileN + c) * kTP + r0);
+      uint8_t *dst = P.out + ocol * P.out_ld + orow;
+      if (P.out_v32 && orow + 16 <= P.batch_rows) {
+        *reinterpret_cast<uint4 *>(dst) = v;
+      } else {
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+        for (int e = 0; e < 16 && orow + e < P.batch_rows; ++e)
+          dst[e] = (uint8_t)(w4[e >> 2] >> (8 * (e & 3)));
       }
     }
   }
@@ -537,4 +578,90 @@ extern "C" int bs_relu2_grad(void *grad, int grad_dtype, int64_t M, int64_t N, i
     case BS_E4M3: return relu2g_disp<BS_E4M3>(P, pack_sbit, sc, st);
     default: return relu2g_disp<BS_E5M2>(P, pack_sbit, sc, st);
   }
+}
+
+namespace bs {
+namespace {
+
+// Largest stored code of one tensor's raw fp8 values [off, off + nnz): the
+// stored values are positive, so the largest code is the largest value.
+__global__ void __launch_bounds__(kThreads)
+code_max_kernel(const uint8_t *vals, const int64_t *vals_offset, const uint32_t *prefix_last,
+                uint32_t *out) {
+  const int64_t off = vals_offset ? *vals_offset : 0;
+  const int64_t n = *prefix_last;
+  uint32_t m = 0;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride)
+    m = max(m, (uint32_t)vals[off + i] & 0x7Fu);
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, d));
+  if ((threadIdx.x & 31) == 0 && m) atomicMax(out, m);
+}
+
+// to_fp8 scale of the ReLU^2 reconstruction k x^2 (x fp8 as fp32, rounded
+// to bf16, then times bf16(scale^2) rounded to bf16): it is non-decreasing
+// in x >= 0, so its amax is its value at the largest stored code.  Resets
+// the scratch word.
+template <int SDT>
+__global__ void relu2_qscale_kernel(uint32_t *code_ws, const float *scale, float k,
+                                    float *qscale) {
+  const float x = store_bits_to_f32<SDT>(*code_ws);
+  float v = bf16_bits_to_f32(f32_to_bf16_bits(k * x * x));
+  if (scale) {
+    const float sc = *scale;
+    v = bf16_bits_to_f32(f32_to_bf16_bits(v * bf16_bits_to_f32(f32_to_bf16_bits(sc * sc))));
+  }
+  const float s = bf16_bits_to_f32(f32_to_bf16_bits(__fdiv_rn(v, 448.0f)));
+  *qscale = fmaxf(s, 1e-9f);
+  *code_ws = 0u;
+}
+
+}  // namespace
+}  // namespace bs
+
+extern "C" int bs_unpack_relu2_fp8t(const void *vals, const uint8_t *bitmask,
+                                    const uint32_t *prefix, const int64_t *vals_offset,
+                                    int store_dtype, int64_t M, int64_t N, const float *scale,
+                                    float k, uint32_t *code_ws, float *qscale_out, void *outT,
+                                    int64_t out_ld, void *stream) {
+  if (store_dtype != BS_E4M3 && store_dtype != BS_E5M2) return BS_ERR_DTYPE;
+  if (M < 0 || N < 0 || out_ld < M) return BS_ERR_SHAPE;
+  const int64_t gm = (M + kTileM - 1) / kTileM, gn = (N + kTileN - 1) / kTileN;
+  if (!bitmask || !prefix || !code_ws || !qscale_out || (gm * gn && !outT)) return BS_ERR_ARG;
+  if (gm * gn > ((int64_t)1 << 31)) return BS_ERR_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t *v8 = static_cast<const uint8_t *>(vals);
+  code_max_kernel<<<148 * 4, kThreads, 0, st>>>(v8, vals_offset, prefix + gm * gn, code_ws);
+  if (store_dtype == BS_E4M3)
+    relu2_qscale_kernel<BS_E4M3><<<1, 1, 0, st>>>(code_ws, scale, k, qscale_out);
+  else
+    relu2_qscale_kernel<BS_E5M2><<<1, 1, 0, st>>>(code_ws, scale, k, qscale_out);
+  if (gm * gn == 0) return launch_err();
+  UnpackParams P{};
+  P.vals = v8;
+  P.bitmask = bitmask;
+  P.prefix = prefix;
+  P.vals_offset = vals_offset;
+  P.out = static_cast<uint8_t *>(outT);
+  P.out_ld = out_ld;
+  P.first_tile = 0;
+  P.ntiles = gm * gn;
+  P.grid_n = gn;
+  P.K = N;
+  P.batch_rows = M;
+  P.scale = scale;
+  P.k = k;
+  P.qscale = qscale_out;
+  P.vals_v16 = aligned(vals, 16);
+  P.out_v32 = aligned(outT, 16) && (out_ld % 16 == 0);
+  const dim3 g(ctas(P.ntiles));
+  if (store_dtype == BS_E4M3) {
+    if (scale) unpack_kernel<BS_E4M3, false, 2, true><<<g, kThreads, 0, st>>>(P);
+    else unpack_kernel<BS_E4M3, false, 2, false><<<g, kThreads, 0, st>>>(P);
+  } else {
+    if (scale) unpack_kernel<BS_E5M2, false, 2, true><<<g, kThreads, 0, st>>>(P);
+    else unpack_kernel<BS_E5M2, false, 2, false><<<g, kThreads, 0, st>>>(P);
+  }
+  return launch_err();
 }

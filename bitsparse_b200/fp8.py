@@ -140,7 +140,7 @@ class MatmulFp8(Function):
             b_fp8 = b
         if CACHE_FP8_MATMUl:
             ctx.save_for_backward(a_fp8, b_fp8, a_scale, b_scale)
-        return _scaled_mm(a_fp8.contiguous(), b_fp8, a_scale, b_scale,
+        return _scaled_mm(_row_major_fp8(a_fp8), b_fp8, a_scale, b_scale,
                           output_dtype=torch.bfloat16)
 
     @staticmethod

@@ -62,6 +62,23 @@ def spAB(A_sparse: BitsparseTensor, B: Tensor, out: Tensor | None = None,
     return out
 
 
+def _relu2_fp8_colmajor(sp: BitsparseTensor) -> tuple[Tensor, Tensor]:
+    """to_fp8(unpack_relu2(sp)) transposed ([N, M] row-major) and its scale,
+    in one pass over the compressed tensor (bs_unpack_relu2_fp8t)."""
+    from .. import _lib, _runtime as R
+    from ..config import RELU2_SCALE
+    M, N = sp.shape
+    dev = sp.bitmask.device
+    bT = torch.empty(N, M, device=dev, dtype=torch.float8_e4m3fn)
+    qs = torch.empty((), device=dev, dtype=torch.float32)
+    scale = None if sp.scale is None else sp.scale.to(device=dev, dtype=torch.float32)
+    _lib.call("bs_unpack_relu2_fp8t", sp.vals.data_ptr(), sp.bitmask.data_ptr(),
+              sp.prefix.data_ptr(), sp.vals_offset.data_ptr(), R.dtype_code(sp.dtype), M, N,
+              R.ptr(scale), float(RELU2_SCALE), R.amax_scratch(dev).data_ptr(), qs.data_ptr(),
+              bT.data_ptr(), M, R.stream_handle(dev))
+    return bT, qs
+
+
 def AspRelu2B(A: Tensor, B_sparse: BitsparseTensor, A_scale: Tensor | None = None,
               row_batch: int = 0) -> Tensor:
     """A @ (k * B^2) with sparse B = relu(preact) (lib_sparse/src/sparse_matmul.py:91-132).
@@ -73,6 +90,14 @@ def AspRelu2B(A: Tensor, B_sparse: BitsparseTensor, A_scale: Tensor | None = Non
     N, K = B_sparse.shape
     M = A.shape[0]
     if row_batch <= 0:
+        if (B_sparse.fp8 and not B_sparse.pack_sbit and A_scale is not None
+                and A.dtype == B_sparse.dtype == torch.float8_e4m3fn):
+            # the fp8 operand straight from the compressed form: reconstruct,
+            # to_fp8 and the column-major copy in one kernel
+            from ..fp8 import _row_major_fp8, _scaled_mm
+            bT, b_scale = _relu2_fp8_colmajor(B_sparse)
+            return _scaled_mm(_row_major_fp8(A), bT.T, A_scale, b_scale,
+                              output_dtype=torch.bfloat16)
         dense = torch.empty(N, K, device=A.device, dtype=torch.bfloat16)
         unpack_relu2_batch_(B_sparse, dense, 0, grid_n, K, N, grid_m * grid_n)
         return matmul(A, dense, B_sparse.fp8, a_scale=A_scale)

@@ -218,6 +218,20 @@ int bs_unpack(const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
 int bs_mask_with_bitmask(void *grad, int grad_dtype, int64_t M, int64_t N,
                          int64_t ld, const uint8_t *bitmask, void *stream);
 
+/* The B operand of the fp8 dW GEMM of Relu2Linear (AspRelu2B,
+ * lib_sparse/src/sparse_matmul.py:91-132 with the FP8 matmul of
+ * lib_sparse/fp8.py:52-115) straight from the compressed fp8 tensor [M, N]:
+ * the ReLU^2 reconstruction of bs_unpack (relu2 = 1) quantised by to_fp8 --
+ * its scale, written to *qscale_out, is derived from the largest stored code
+ * (the reconstruction is non-decreasing in the stored value) -- and written
+ * transposed into outT [N, M] (row stride out_ld >= M), i.e. the [M, N]
+ * operand in column-major order.  Raw storage only (not pack_sbit).
+ * code_ws: one device uint32 of scratch, zero before the call (left zero). */
+int bs_unpack_relu2_fp8t(const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
+                         const int64_t *vals_offset, int store_dtype, int64_t M, int64_t N,
+                         const float *scale, float k, uint32_t *code_ws, float *qscale_out,
+                         void *outT, int64_t out_ld, void *stream);
+
 /* In place grad <- bit ? grad * (2 * k * r) : 0, r gathered from the stored
  * values, then (scale != NULL) grad *= scale.  Replaces relu2_grad_sparse_
  * (lib_sparse/src/triton_operators.py:178-202,

@@ -375,3 +375,26 @@ def test_compress_bias_relu_equals_separate_steps(M, N, pack):
     assert torch.equal(h2, h)
     np.testing.assert_array_equal(bits(_reconstruct(sp2)), bits(ref_h))
     B.check_status()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M, N", [(64, 64), (300, 200), (1000, 3072), (129, 4097), (1, 17)])
+@pytest.mark.parametrize("zero", [False, True])
+def test_relu2_fp8_colmajor_equals_to_fp8_of_reconstruction(M, N, zero):
+    """bs_unpack_relu2_fp8t == to_fp8(ReLU^2 reconstruction) transposed, bit
+    for bit (the dW operand of the fp8 Relu2Linear backward)."""
+    from bitsparse_b200.src.sparse_matmul import _relu2_fp8_colmajor
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    x = (torch.randn(M, N, generator=g, device="cuda") * 2 - 0.5).relu()
+    if zero:
+        x.zero_()
+    q, s = to_fp8(x)
+    sp = dense_to_tilesparse(q, s)
+    bT, qs = _relu2_fp8_colmajor(sp)
+    rq, rs = to_fp8(_reconstruct(sp, relu2=True))
+    torch.cuda.synchronize()
+    assert torch.equal(qs, rs.reshape(()).to(qs.dtype))
+    assert torch.equal(bT.view(torch.uint8), rq.T.contiguous().view(torch.uint8))
+    # twice in a row: the code scratch is left zero
+    bT2, qs2 = _relu2_fp8_colmajor(sp)
+    assert torch.equal(qs2, qs) and torch.equal(bT2.view(torch.uint8), bT.view(torch.uint8))
