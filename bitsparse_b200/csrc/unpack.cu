@@ -195,6 +195,31 @@ struct PidPos {
   }
 };
 
+// The ReLU^2 output for one stored code v (OUT 1: bf16 bits; OUT 2: e4m3
+// bits), with the roundings of the reference's kernel and of to_fp8.
+template <int SDT, int OUT, bool SCALE>
+__device__ __forceinline__ uint32_t relu2_out(const UnpackParams &P, uint32_t v) {
+  if constexpr (SDT == BS_BF16) {
+    // bf16 * bf16 in bf16 (triton_kernels.py:238): k*v rounded, then *v
+    const float x = bf16_bits_to_f32(v);
+    const float kx = bf16_bits_to_f32(f32_to_bf16_bits(P.k * x));
+    v = f32_to_bf16_bits(kx * x);
+  } else {
+    const float x = store_bits_to_f32<SDT>(v);  // fp8 squares in fp32 (:234-236)
+    v = f32_to_bf16_bits(P.k * x * x);
+  }
+  if constexpr (SCALE) {
+    const float sc = *P.scale;
+    const float s2 = bf16_bits_to_f32(f32_to_bf16_bits(sc * sc));  // scale.square() in bf16
+    v = f32_to_bf16_bits(bf16_bits_to_f32(v) * s2);
+  }
+  if constexpr (OUT == 2) {  // e4m3(bf16(v / qscale)), as to_fp8 on the bf16 tensor
+    const float qs = *P.qscale;
+    v = div_e4m3x2(bf16_bits_to_f32(v), 0.f, qs, __frcp_rn(qs)) & 0xFFu;
+  }
+  return v;
+}
+
 // OUT: 0 = elements of SDT (plain reconstruct), 1 = bf16 k*r^2 (ReLU^2),
 // 2 = the ReLU^2 reconstruction quantised to e4m3 with *qscale (to_fp8's
 // quantiser) and written transposed (out is [K, batch_rows]) -- the B
@@ -207,11 +232,18 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
   __shared__ __align__(16) uint8_t stage[kStageBytes];
   __shared__ uint32_t s_wt[G::S * 8];
   __shared__ __align__(16) uint8_t tstage[OUT == 2 ? kUT * kTileN * kTP : 16];
+  // fp8 storage: the ReLU^2 output is a function of the 8-bit code alone, so
+  // each CTA tabulates it once (256 codes, one per thread) and the element
+  // loop becomes a table lookup.
+  constexpr bool LUT = SDT != BS_BF16 && OUT >= 1;
+  __shared__ uint32_t lut[LUT ? 256 : 1];
+  static_assert(!LUT || kThreads == 256, "one table entry per thread");
 
   const int64_t pid0 = (int64_t)blockIdx.x * kUT;
   const int nt = tiles_here(P, pid0);
   const PidPos pp(pid0, P.grid_n);
   const int tid = threadIdx.x;
+  if constexpr (LUT) lut[tid] = relu2_out<SDT, OUT, SCALE>(P, tid);
   uint32_t m[G::S], cnt[G::S], ex[G::S];
 #pragma unroll
   for (int s = 0; s < G::S; ++s) {  // masks first: independent of the values
@@ -225,18 +257,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
   const uint32_t first = stage_values<SDT, PACK>(P, P.first_tile + pid0, nt, stage);
 #pragma unroll
   for (int s = 0; s < G::S; ++s) cnt[s] = __popc(m[s]);
-  block_excl_scan<G::S>(cnt, ex, s_wt);  // its barriers also publish the stage
-
-  float s2 = 0.f;
-  if constexpr (SCALE) {
-    const float sc = *P.scale;
-    s2 = bf16_bits_to_f32(f32_to_bf16_bits(sc * sc));  // scale.square(), cast to bf16
-  }
-  float qs = 1.f, qr = 1.f;
-  if constexpr (OUT == 2) {
-    qs = *P.qscale;
-    qr = __frcp_rn(qs);
-  }
+  block_excl_scan<G::S>(cnt, ex, s_wt);  // its barriers also publish the stage and table
 #pragma unroll
   for (int s = 0; s < G::S; ++s) {
     const int c = s * kThreads + tid;
@@ -251,14 +272,16 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     const uint32_t mm = m[s];
     uint32_t r = ex[s];
-    if constexpr (OUT == 0 && !PACK) {
+    if constexpr ((OUT == 0 || LUT) && !PACK) {
       // Branch-free expand: every element loads the value at its rank (the
       // stage has slack past the last value) and keeps it only if its bit
       // is set; divergent per-element branches cost more than the loads.
 #pragma unroll
       for (int e = 0; e < G::VEC; ++e) {
         const uint32_t bit = (mm >> e) & 1u;
-        const uint32_t v = staged_value<SDT, PACK>(stage, first, r) & (0u - bit);
+        uint32_t v = staged_value<SDT, PACK>(stage, first, r);
+        if constexpr (LUT) v = lut[v];
+        v &= 0u - bit;
         r += bit;
         if constexpr (OB == 1) w[e >> 2] |= v << (8 * (e & 3));
         else w[e >> 1] |= v << (16 * (e & 1));
@@ -266,23 +289,11 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
     }
 #pragma unroll
     for (int e = 0; e < G::VEC; ++e) {  // static indices keep w[] in registers
-      if constexpr (OUT == 0 && !PACK) break;
+      if constexpr ((OUT == 0 || LUT) && !PACK) break;
       if (!((mm >> e) & 1u)) continue;
       uint32_t v = staged_value<SDT, PACK>(stage, first, r++);
-      if constexpr (OUT >= 1) {
-        if constexpr (SDT == BS_BF16) {
-          // bf16 * bf16 in bf16 (triton_kernels.py:238): k*v rounded, then *v
-          const float x = bf16_bits_to_f32(v);
-          const float kx = bf16_bits_to_f32(f32_to_bf16_bits(P.k * x));
-          v = f32_to_bf16_bits(kx * x);
-        } else {
-          const float x = store_bits_to_f32<SDT>(v);  // fp8 squares in fp32 (:234-236)
-          v = f32_to_bf16_bits(P.k * x * x);
-        }
-        if constexpr (SCALE) v = f32_to_bf16_bits(bf16_bits_to_f32(v) * s2);
-        if constexpr (OUT == 2)  // e4m3(bf16(v / qscale)), as to_fp8 on the bf16 tensor
-          v = div_e4m3x2(bf16_bits_to_f32(v), 0.f, qs, qr) & 0xFFu;
-      }
+      if constexpr (LUT) v = lut[v];
+      else if constexpr (OUT >= 1) v = relu2_out<SDT, OUT, SCALE>(P, v);
       if constexpr (OB == 1) w[e >> 2] |= v << (8 * (e & 3));
       else w[e >> 1] |= v << (16 * (e & 1));
     }
@@ -375,16 +386,39 @@ __global__ void __launch_bounds__(kThreads) mask_kernel(const UnpackParams P) {
   }
 }
 
+// Two bf16 gradients (one word) times t0 / t1, rounded to bf16, then (scale)
+// times sb rounded again.  The hardware pair conversion rounds like
+// f32_to_bf16_bits except for NaN (canonical NaN vs sign | 0x7FC0), so a
+// pair holding a NaN takes the software rounding.
+__device__ __forceinline__ uint32_t grad_pair(uint32_t gw, float t0, float t1, float sb,
+                                              bool scale) {
+  const float p0 = bf16_bits_to_f32(gw & 0xFFFFu) * t0;
+  const float p1 = bf16_bits_to_f32(gw >> 16) * t1;
+  uint32_t y = bf16x2_from_f32(p0, p1);
+  const bool nan = (p0 != p0) | (p1 != p1);
+  if (nan) y = f32_to_bf16_bits(p0) | (f32_to_bf16_bits(p1) << 16);
+  if (!scale) return y;
+  const float q0 = bf16_bits_to_f32(y & 0xFFFFu) * sb;
+  const float q1 = bf16_bits_to_f32(y >> 16) * sb;
+  if (nan | (q0 != q0) | (q1 != q1)) return f32_to_bf16_bits(q0) | (f32_to_bf16_bits(q1) << 16);
+  return bf16x2_from_f32(q0, q1);
+}
+
 // grad <- bit ? bf16(grad * (2 k r)) : 0, then (SCALE) bf16(grad * bf16(scale)).
 template <int SDT, bool PACK, bool SCALE>
 __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams P) {
   using G = Chunk<2>;
   __shared__ __align__(16) uint8_t stage[kStageBytes];
   __shared__ uint32_t s_wt[G::S * 8];
+  // fp8 storage: 2 k r depends on the 8-bit code alone -> a 256-entry table
+  constexpr bool LUT = SDT != BS_BF16;
+  __shared__ float lut[LUT ? 256 : 1];
   const int64_t pid0 = (int64_t)blockIdx.x * kUT;
   const int nt = tiles_here(P, pid0);
   const PidPos pp(pid0, P.grid_n);
   const int tid = threadIdx.x;
+  const float two_k = 2.0f * P.k;
+  if constexpr (LUT) lut[tid] = two_k * store_bits_to_f32<SDT>(tid);
   uint32_t m[G::S], cnt[G::S], ex[G::S];
 #pragma unroll
   for (int s = 0; s < G::S; ++s) {  // masks first: independent of the values
@@ -399,7 +433,6 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
   block_excl_scan<G::S>(cnt, ex, s_wt);
   float sb = 0.f;
   if constexpr (SCALE) sb = bf16_bits_to_f32(f32_to_bf16_bits(*P.scale));
-  const float two_k = 2.0f * P.k;
 #pragma unroll
   for (int s = 0; s < G::S; ++s) {
     const int c = s * kThreads + tid;
@@ -423,12 +456,31 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
     }
     uint32_t o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     uint32_t r = ex[s];
+    if constexpr (LUT && !PACK) {
+      // branch-free: every element reads the code at its rank (the stage has
+      // slack past the last value), pairs are rounded by the hardware
+      // conversion and unset elements cleared afterwards
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t b0 = (mm >> (2 * i)) & 1u, b1 = (mm >> (2 * i + 1)) & 1u;
+        const float t0 = lut[staged_value<SDT, PACK>(stage, first, r)];
+        r += b0;
+        const float t1 = lut[staged_value<SDT, PACK>(stage, first, r)];
+        r += b1;
+        const uint32_t keep = (0u - b0) & 0xFFFFu | ((0u - b1) & 0xFFFF0000u);
+        o[i] = grad_pair(gw[i], t0, t1, sb, SCALE) & keep;
+      }
+    }
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
+      if constexpr (LUT && !PACK) break;
       if (!((mm >> e) & 1u)) continue;
-      const float rv = store_bits_to_f32<SDT>(staged_value<SDT, PACK>(stage, first, r++));
+      const uint32_t code = staged_value<SDT, PACK>(stage, first, r++);
+      float tk;
+      if constexpr (LUT) tk = lut[code];
+      else tk = two_k * store_bits_to_f32<SDT>(code);
       const uint32_t gb = (gw[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
-      uint32_t y = f32_to_bf16_bits(bf16_bits_to_f32(gb) * (two_k * rv));
+      uint32_t y = f32_to_bf16_bits(bf16_bits_to_f32(gb) * tk);
       if constexpr (SCALE) y = f32_to_bf16_bits(bf16_bits_to_f32(y) * sb);
       o[e >> 1] |= y << (16 * (e & 1));
     }
@@ -590,10 +642,24 @@ code_max_kernel(const uint8_t *vals, const int64_t *vals_offset, const uint32_t 
                 uint32_t *out) {
   const int64_t off = vals_offset ? *vals_offset : 0;
   const int64_t n = *prefix_last;
-  uint32_t m = 0;
+  const uint8_t *p = vals + off;
+  // bytes before the first 16-byte boundary and after the last one singly,
+  // the aligned body as 16-byte vectors with a byte-wise max
+  const int64_t h16 = (int64_t)((16 - (reinterpret_cast<uintptr_t>(p) & 15)) & 15);
+  const int64_t head = n < h16 ? n : h16;
+  const int64_t nv = (n - head) / 16;
+  const int64_t tail0 = head + nv * 16;
+  const int64_t gid = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
-  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride)
-    m = max(m, (uint32_t)vals[off + i] & 0x7Fu);
+  uint32_t m4 = 0;
+  const uint4 *pv = reinterpret_cast<const uint4 *>(p + head);
+  for (int64_t i = gid; i < nv; i += stride) {
+    const uint4 v = ld_nc_v4(pv + i);
+    m4 = __vmaxu4(m4, __vmaxu4(__vmaxu4(v.x, v.y), __vmaxu4(v.z, v.w)) & 0x7F7F7F7Fu);
+  }
+  if (gid < head) m4 = __vmaxu4(m4, p[gid] & 0x7Fu);
+  if (gid < n - tail0) m4 = __vmaxu4(m4, p[tail0 + gid] & 0x7Fu);
+  uint32_t m = max(max(m4 & 0xFFu, (m4 >> 8) & 0xFFu), max((m4 >> 16) & 0xFFu, m4 >> 24));
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, d));
   if ((threadIdx.x & 31) == 0 && m) atomicMax(out, m);
