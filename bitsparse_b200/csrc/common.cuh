@@ -135,6 +135,51 @@ __device__ __forceinline__ uint32_t div_e4m3x2(float x0, float x1, float s, floa
   return e4m3x2_bits(bf16_bits_to_f32(b & 0xFFFFu), bf16_bits_to_f32(b >> 16));
 }
 
+// div_e4m3x2 on eight bf16 values (four words, low half first) -> two words
+// of codes.  The corrected estimates of quotient_fp32 are taken branch-free;
+// only if one of them lies near a bf16 rounding midpoint is the group redone
+// with quotient_fp32's exact fallback -- one branch per eight values instead
+// of one per value, and the same codes as div_e4m3x2.
+// The rare exact case of div_e4m3x8, out of line so that the unrolled
+// callers stay small (their instruction footprint matters more than a call).
+static __device__ __noinline__ uint2 div_e4m3x8_exact(uint32_t w0, uint32_t w1, uint32_t w2,
+                                               uint32_t w3, float s, float r) {
+  const uint32_t w[4] = {w0, w1, w2, w3};
+  uint32_t o[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    o[i] = div_e4m3x2(bf16_bits_to_f32(w[2 * i] & 0xFFFFu), bf16_bits_to_f32(w[2 * i] >> 16), s, r) |
+           div_e4m3x2(bf16_bits_to_f32(w[2 * i + 1] & 0xFFFFu),
+                      bf16_bits_to_f32(w[2 * i + 1] >> 16), s, r) << 16;
+  return make_uint2(o[0], o[1]);
+}
+
+__device__ __forceinline__ void div_e4m3x8(const uint32_t (&w)[4], float s, float r,
+                                           uint32_t (&o)[2]) {
+  uint32_t near = 0;
+  float y[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float x = bf16_bits_to_f32(e & 1 ? w[e >> 1] >> 16 : w[e >> 1] & 0xFFFFu);
+    const float y0 = x * r;
+    const float y1 = fmaf(fmaf(-y0, s, x), r, y0);
+    near |= (__float_as_uint(y1) & 0xFFFFu) - 0x7FFCu <= 8u;
+    y[e] = copysignf(y1, x);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t b0 = bf16x2_from_f32(y[4 * i], y[4 * i + 1]);
+    const uint32_t b1 = bf16x2_from_f32(y[4 * i + 2], y[4 * i + 3]);
+    o[i] = e4m3x2_bits(bf16_bits_to_f32(b0 & 0xFFFFu), bf16_bits_to_f32(b0 >> 16)) |
+           e4m3x2_bits(bf16_bits_to_f32(b1 & 0xFFFFu), bf16_bits_to_f32(b1 >> 16)) << 16;
+  }
+  if (near) {
+    const uint2 e = div_e4m3x8_exact(w[0], w[1], w[2], w[3], s, r);
+    o[0] = e.x;
+    o[1] = e.y;
+  }
+}
+
 // torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;
 // -0 and NaN unchanged.
 __device__ __forceinline__ uint32_t relu_bf16x2(uint32_t w) {

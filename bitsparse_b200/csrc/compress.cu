@@ -195,11 +195,14 @@ __device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64
     if constexpr (DT_IN == BS_BF16) {
       // |x / scale| <= 448 * (1 + 2^-8): the fast paths are exact here
       const float r = __frcp_rn(qs);
+      static_assert(C::VEC % 8 == 0, "groups of eight values");
 #pragma unroll
-      for (int e = 0; e < C::VEC; e += 2) {
-        sv[e >> 2] |= div_e4m3x2(bf16_bits_to_f32(raw[e >> 1] & 0xFFFFu),
-                                 bf16_bits_to_f32(raw[e >> 1] >> 16), qs, r)
-                      << (8 * (e & 3));
+      for (int g = 0; g < C::VEC / 8; ++g) {
+        const uint32_t w4[4] = {raw[4 * g], raw[4 * g + 1], raw[4 * g + 2], raw[4 * g + 3]};
+        uint32_t o2[2];
+        div_e4m3x8(w4, qs, r, o2);
+        sv[2 * g] = o2[0];
+        sv[2 * g + 1] = o2[1];
       }
     } else {
 #pragma unroll
@@ -909,27 +912,30 @@ __global__ void __launch_bounds__(NW * 32, MINB)
           }
           if constexpr (QUANT) {
             uint32_t qw[2] = {0, 0}, side[2];
+            if constexpr (BIAS) {
+              const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
+              div_e4m3x8(h4, qs, qr, qw);
+            } else {
+              // (the per-value form measures faster here; the codes are the same)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint32_t qq = div_e4m3x2(bf16_bits_to_f32(v[s4][i] & 0xFFFFu),
-                                             bf16_bits_to_f32(v[s4][i] >> 16), qs, qr);
-              qw[i >> 1] |= qq << (16 * (i & 1));
+              for (int i = 0; i < 4; ++i)
+                qw[i >> 1] |= div_e4m3x2(bf16_bits_to_f32(v[s4][i] & 0xFFFFu),
+                                         bf16_bits_to_f32(v[s4][i] >> 16), qs, qr)
+                              << (16 * (i & 1));
             }
             side[0] = qw[0];
             side[1] = qw[1];
             if constexpr (BIAS) {
               if (P.qscale2 != nullptr) {
                 // side output: e4m3(bf16(h * h) / scale2) (h.square_() then to_fp8)
-                side[0] = side[1] = 0;
+                uint32_t sq[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                   const float h0 = bf16_bits_to_f32(v[s4][i] & 0xFFFFu);
                   const float h1 = bf16_bits_to_f32(v[s4][i] >> 16);
-                  const uint32_t sq = bf16x2_from_f32(h0 * h0, h1 * h1);  // h.square_()
-                  side[i >> 1] |= div_e4m3x2(bf16_bits_to_f32(sq & 0xFFFFu),
-                                             bf16_bits_to_f32(sq >> 16), qs2, qr2)
-                                  << (16 * (i & 1));
+                  sq[i] = bf16x2_from_f32(h0 * h0, h1 * h1);  // h.square_()
                 }
+                div_e4m3x8(sq, qs2, qr2, side);
               }
             }
             v[s4][0] = qw[0]; v[s4][1] = qw[1];

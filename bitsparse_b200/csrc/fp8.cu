@@ -157,11 +157,9 @@ quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q) {
     if constexpr (DT == BS_BF16) {
       // |x / scale| <= 448 * (1 + 2^-8) by construction of the scale, so the
       // fast e4m3 conversion applies (NaN stays NaN).
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        o[e >> 2] |= div_e4m3x2(bf16_bits_to_f32(b[e]), bf16_bits_to_f32(b[e + 1]), s, r)
-                     << (8 * (e & 3));
-      }
+      const uint32_t w4[4] = {b[0] | b[1] << 16, b[2] | b[3] << 16, b[4] | b[5] << 16,
+                              b[6] | b[7] << 16};
+      div_e4m3x8(w4, s, r, o);
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
