@@ -67,12 +67,13 @@ __global__ void __launch_bounds__(kThreads)
 amax_bias_relu_kernel(const uint8_t *z, int64_t M, int64_t N, int64_t ld, const uint8_t *bias,
                       uint32_t *amax_ws) {
   const int64_t cpr = (N + 7) / 8;  // 8-column chunks per row
-  const int64_t nch = M * cpr;
   const bool vec = (N % 8 == 0) && (ld % 8 == 0);
   float m = 0.f;
-  const int64_t stride = (int64_t)gridDim.x * kThreads;
-  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < nch; i += stride) {
-    const int64_t r = i / cpr, c0 = (i - r * cpr) * 8;
+  // a block walks rows blockIdx.x, + gridDim.x, ... chunk by chunk, its
+  // threads kThreads chunks apart: one division per thread, not per chunk
+  const int64_t dr = kThreads / cpr, di = kThreads % cpr;
+  for (int64_t i = threadIdx.x % cpr, r = blockIdx.x + (threadIdx.x / cpr) * gridDim.x; r < M;) {
+    const int64_t c0 = i * 8;
     uint32_t zw[4] = {0, 0, 0, 0}, bw[4] = {0, 0, 0, 0};
     if (vec) {
       const uint4 v = ld_nc_v4(z + (r * ld + c0) * 2);
@@ -92,6 +93,12 @@ amax_bias_relu_kernel(const uint8_t *z, int64_t M, int64_t N, int64_t ld, const 
       const uint32_t h = relu_bf16x2(bf16x2_from_f32(lo, hi));
       m = fmaxf(m, fabsf(bf16_bits_to_f32(h & 0xFFFFu)));
       m = fmaxf(m, fabsf(bf16_bits_to_f32(h >> 16)));
+    }
+    i += di;
+    r += dr * gridDim.x;
+    if (i >= cpr) {
+      i -= cpr;
+      r += gridDim.x;
     }
   }
 #pragma unroll

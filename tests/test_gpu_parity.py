@@ -398,3 +398,30 @@ def test_relu2_fp8_colmajor_equals_to_fp8_of_reconstruction(M, N, zero):
     # twice in a row: the code scratch is left zero
     bT2, qs2 = _relu2_fp8_colmajor(sp)
     assert torch.equal(qs2, qs) and torch.equal(bT2.view(torch.uint8), bT.view(torch.uint8))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M, N", [(512, 1024), (300, 200), (1, 40), (130, 8), (2048, 3072)])
+@pytest.mark.parametrize("square", [False, True])
+def test_compress_bias_relu_fp8_equals_separate_steps(M, N, square):
+    """Fused fp8 bias + ReLU (+ square) + quantise + compress == torch's
+    z + b, relu, to_fp8, compress; the side operand == to_fp8(h) or
+    to_fp8(h * h), bit for bit, scales included."""
+    from bitsparse_b200.src.operators import compress_bias_relu_fp8
+    g = torch.Generator(device="cuda").manual_seed(M * 3 + N)
+    z = (2 * torch.randn(M, N, generator=g, device="cuda")).to(torch.bfloat16)
+    b = (0.5 * torch.randn(N, generator=g, device="cuda")).to(torch.bfloat16)
+    h = torch.relu(z + b)
+    q, s = to_fp8(h)
+    ref = dense_to_tilesparse(q, s)
+    sq, ss = to_fp8(h * h) if square else (q, s)
+    out = compress_bias_relu_fp8(z, b, None, False, square=square)
+    assert out is not None
+    side, side_scale, sp = out
+    assert torch.equal(sp.scale.reshape(()), s.reshape(()))
+    assert torch.equal(side_scale.reshape(()), ss.reshape(()))
+    assert torch.equal(side.view(torch.uint8), sq.view(torch.uint8))
+    assert torch.equal(sp.bitmask, ref.bitmask)
+    assert torch.equal(sp.prefix.view(torch.int32), ref.prefix.view(torch.int32))
+    assert torch.equal(sp.vals.view(torch.uint8), ref.vals.view(torch.uint8))
+    B.check_status()
