@@ -610,28 +610,6 @@ __global__ void __launch_bounds__(kThreads) compact_kernel(const CompressParams 
 // inclusive prefixes through the CTAs) reached only ~20% of HBM bandwidth:
 // every CTA waited on the slowest of the hundreds of partitions ahead of it.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
 // 2-D tiled TMA load of one 64 x 64 tile (no multicast).
 __device__ __forceinline__ void tma_load_tile(void *dst, const CUtensorMap *map, int x, int y,
                                               uint64_t *bar) {
@@ -1057,6 +1035,7 @@ __global__ void __launch_bounds__(NW * 32, MINB)
       known = q;
     }
     if (tid == 0) s_sum[(r + 1) & 1] = 0;  // next round's accumulator (read this round: the other)
+    fence_proxy_async_smem();  // this round's stage accesses precede the next TMA writes
     __syncthreads();  // stage (r-D) % NS and s_sum are free again
   }
 }

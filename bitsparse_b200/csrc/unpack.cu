@@ -18,6 +18,8 @@
 // stream, bitmask and output is touched once.  The reference's separate
 // scale passes (output *= scale^2, grad *= scale) are fused, keeping the
 // reference's double rounding.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace bs {
@@ -40,6 +42,7 @@ struct UnpackParams {
   const float *scale;
   float k;       // RELU2_SCALE
   const float *qscale;  // OUT 2: to_fp8 scale of the ReLU^2 reconstruction
+  int32_t *status;  // bounded-wait timeouts (pipelined kernel), or null
   int vals_v16;  // vals base 16-byte aligned
   int out_v32;   // out base + row stride allow 32-byte accesses
 };
@@ -493,6 +496,153 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
   }
 }
 
+
+// Plain reconstruct (OUT 0), persistent and double-buffered.  CTA b takes
+// tile pairs b, b + G, ...; while it expands one pair, the bulk-copy engine
+// already brings the next pair's bitmask (1 KB) and value segment into the
+// other buffer, and thread 0 holds the prefix pair for the one after that
+// in registers -- the load chain (prefix -> values) that a short-lived CTA
+// waits through is off the critical path.  Raw and packed storage; vals
+// must be 16-byte aligned (the aligned 16-byte superset of a segment is
+// copied, as the per-CTA kernel's vector loads read it).
+constexpr int kPipeMaskBytes = kUT * kTileBytes;
+
+template <int SDT, bool PACK>
+__global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParams P) {
+  constexpr int SB = Elt<SDT>::bytes;
+  using G = Chunk<SB>;
+  __shared__ __align__(128) uint8_t stage[2][kStageBytes];
+  __shared__ __align__(128) uint8_t mbuf[2][kPipeMaskBytes];
+  __shared__ uint32_t s_wt[G::S * 8];
+  __shared__ uint32_t s_first[2];
+  __shared__ __align__(8) uint64_t bars[2];
+  const int tid = threadIdx.x;
+  const int64_t npairs = (P.ntiles + kUT - 1) / kUT;
+  const int64_t G_ = gridDim.x;
+
+  // thread 0: issue the copies of pair g into buffer `buf` (prefixes p0, p1)
+  const int64_t voff = (tid == 0 && P.vals_offset) ? *P.vals_offset : 0;
+  auto issue = [&](int64_t g, int buf, uint32_t p0, uint32_t p1) {
+    const int64_t t0 = g * kUT;
+    const int nt = (int)(P.ntiles - t0 < kUT ? P.ntiles - t0 : kUT);
+    uint32_t cnt = p1 - p0;
+    if (cnt > (uint32_t)(nt * kTileNumel)) cnt = nt * kTileNumel;
+    const int64_t base = (int64_t)p0 + voff;
+    int64_t a0, a1;
+    uint32_t first;
+    if constexpr (!PACK) {
+      const int64_t b0 = base * SB;
+      a0 = b0 & ~(int64_t)15;
+      a1 = (b0 + (int64_t)cnt * SB + 15) & ~(int64_t)15;
+      first = (uint32_t)((b0 - a0) / SB);
+    } else {
+      constexpr int B = pack_bits<SDT>();
+      const int64_t bit0 = base * B;
+      a0 = (bit0 >> 3) & ~(int64_t)15;
+      a1 = ((((base + cnt) * B + 7) >> 3) + 15) & ~(int64_t)15;
+      first = (uint32_t)(bit0 - a0 * 8);
+    }
+    const uint32_t vbytes = cnt ? (uint32_t)(a1 - a0) : 0u;
+    const uint32_t mbytes = (uint32_t)(nt * kTileBytes);
+    s_first[buf] = first;
+    mbar_expect_tx(&bars[buf], mbytes + vbytes);
+    bulk_load(mbuf[buf], P.bitmask + (P.first_tile + t0) * kTileBytes, mbytes, &bars[buf]);
+    if (vbytes) bulk_load(stage[buf], P.vals + a0, vbytes, &bars[buf]);
+  };
+  auto prefix_pair = [&](int64_t g, uint32_t &p0, uint32_t &p1) {
+    const int64_t t0 = g * kUT;
+    const int nt = (int)(P.ntiles - t0 < kUT ? P.ntiles - t0 : kUT);
+    p0 = P.prefix[P.first_tile + t0];
+    p1 = P.prefix[P.first_tile + t0 + nt];
+  };
+
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  uint32_t np0 = 0, np1 = 0;  // thread 0: prefixes of the pair after the one in flight
+  if (tid == 0 && blockIdx.x < npairs) {
+    uint32_t p0, p1;
+    prefix_pair(blockIdx.x, p0, p1);
+    issue(blockIdx.x, 0, p0, p1);
+    if (blockIdx.x + G_ < npairs) prefix_pair(blockIdx.x + G_, np0, np1);
+  }
+  for (int64_t it = 0;; ++it) {
+    const int64_t g = blockIdx.x + it * G_;
+    if (g >= npairs) break;
+    const int buf = (int)(it & 1);
+    if (tid == 0 && g + G_ < npairs) {
+      issue(g + G_, buf ^ 1, np0, np1);
+      if (g + 2 * G_ < npairs) prefix_pair(g + 2 * G_, np0, np1);
+    }
+    {
+      bool ok = false;
+      for (uint32_t n = 0; n < kMaxPolls && !(ok = mbar_try_wait(&bars[buf], (uint32_t)((it >> 1) & 1))); ++n) {
+      }
+      if (!ok && tid == 0) status_or(P.status, BS_STATUS_TIMEOUT);
+    }
+    const int64_t pid0 = g * kUT;
+    const int nt = tiles_here(P, pid0);
+    const PidPos pp(pid0, P.grid_n);
+    uint32_t m[G::S], cnt[G::S], ex[G::S];
+#pragma unroll
+    for (int s = 0; s < G::S; ++s) {
+      const int c = s * kThreads + tid;
+      const int j = c / G::CPT, cc = c % G::CPT;
+      m[s] = j < nt ? load_mask<G::VEC>(mbuf[buf] + j * kTileBytes + cc * (G::VEC / 8)) : 0u;
+      cnt[s] = __popc(m[s]);
+    }
+    block_excl_scan<G::S>(cnt, ex, s_wt);
+    const uint8_t *stg = stage[buf];
+    const uint32_t first = s_first[buf];
+#pragma unroll
+    for (int s = 0; s < G::S; ++s) {
+      const int c = s * kThreads + tid;
+      const int j = c / G::CPT, cc = c % G::CPT;
+      if (j >= nt) continue;
+      const int row = cc / G::CPR, colc = cc % G::CPR;
+      int64_t tr, tc;
+      pp.pos(j, tr, tc);
+      const int64_t grow = tr * kTileM + row;
+      const int64_t gcol = tc * kTileN + colc * G::VEC;
+      if (grow >= P.batch_rows) continue;
+      uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      const uint32_t mm = m[s];
+      uint32_t r = ex[s];
+#pragma unroll
+      for (int e = 0; e < G::VEC; ++e) {
+        uint32_t v;
+        if constexpr (!PACK) {
+          // branch-free: read the value at this element's rank (the stage
+          // has slack past the last value), keep it only if its bit is set
+          const uint32_t bit = (mm >> e) & 1u;
+          v = staged_value<SDT, PACK>(stg, first, r) & (0u - bit);
+          r += bit;
+        } else {
+          if (!((mm >> e) & 1u)) continue;
+          v = staged_value<SDT, PACK>(stg, first, r++);
+        }
+        if constexpr (SB == 1) w[e >> 2] |= v << (8 * (e & 3));
+        else w[e >> 1] |= v << (16 * (e & 1));
+      }
+      uint8_t *dst = P.out + (grow * P.out_ld + gcol) * SB;
+      if (P.out_v32 && gcol + G::VEC <= P.K) {
+        st_v8(dst, w);
+      } else {
+        for (int e = 0; e < G::VEC; ++e) {
+          if (gcol + e >= P.K) break;
+          if constexpr (SB == 1) dst[e] = (w[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+          else reinterpret_cast<uint16_t *>(dst)[e] = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+        }
+      }
+    }
+    fence_proxy_async_smem();  // this pair's buffer reads precede its next bulk copies
+    __syncthreads();
+  }
+}
+
 }  // namespace bs
 
 using namespace bs;
@@ -503,9 +653,36 @@ int launch_err() { return cudaGetLastError() == cudaSuccess ? BS_OK : BS_ERR_LAU
 bool aligned(const void *p, int a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 unsigned ctas(int64_t ntiles) { return (unsigned)((ntiles + kUT - 1) / kUT); }
 
+// Resident CTAs of the pipelined kernel on the current device (cached).
+template <int SDT, bool PACK>
+int pipe_resident() {
+  constexpr int kMaxDev = 64;
+  static int cache[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 0;
+  if (!cache[dev]) {
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, unpack_pipe_kernel<SDT, PACK>,
+                                                      kThreads, 0) != cudaSuccess)
+      return 0;
+    cache[dev] = sms * per_sm;  // benign race: every writer stores the same value
+  }
+  return cache[dev];
+}
+
 template <int SDT, bool PACK>
 int unpack_disp2(const UnpackParams &P, int relu2, bool scale, cudaStream_t st) {
   const dim3 g(ctas(P.ntiles));
+  if (!relu2 && P.vals_v16 && aligned(P.bitmask, 16) && !getenv("BS_UNPACK_PER_CTA")) {
+    const int res = pipe_resident<SDT, PACK>();
+    const int64_t npairs = (P.ntiles + kUT - 1) / kUT;
+    if (res > 0) {
+      unpack_pipe_kernel<SDT, PACK>
+          <<<(unsigned)(npairs < res ? npairs : res), kThreads, 0, st>>>(P);
+      return launch_err();
+    }
+  }
   if (!relu2) unpack_kernel<SDT, PACK, 0, false><<<g, kThreads, 0, st>>>(P);
   else if (scale) unpack_kernel<SDT, PACK, 1, true><<<g, kThreads, 0, st>>>(P);
   else unpack_kernel<SDT, PACK, 1, false><<<g, kThreads, 0, st>>>(P);
