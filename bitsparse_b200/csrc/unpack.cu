@@ -187,8 +187,13 @@ __device__ __forceinline__ int tiles_here(const UnpackParams &P, int64_t pid0) {
 // wrapping step per tile (a 64-bit divide per chunk costs ~70 instructions).
 struct PidPos {
   int64_t r0, c0, gn;
-  __device__ __forceinline__ PidPos(int64_t pid0, int64_t grid_n)
-      : r0(pid0 / grid_n), c0(pid0 % grid_n), gn(grid_n) {}
+  // batches hold < 2^31 tiles (checked on the host): a 32-bit division
+  __device__ __forceinline__ PidPos(int64_t pid0, int64_t grid_n) : gn(grid_n) {
+    const uint32_t p = (uint32_t)pid0, n = (uint32_t)grid_n;
+    const uint32_t q = p / n;
+    r0 = q;
+    c0 = p - q * n;
+  }
   __device__ __forceinline__ void pos(int j, int64_t &tr, int64_t &tc) const {
     tr = r0;
     tc = c0 + j;
@@ -757,6 +762,7 @@ extern "C" int bs_mask_with_bitmask(void *grad, int grad_dtype, int64_t M, int64
   if (M < 0 || N < 0 || ld < N) return BS_ERR_SHAPE;
   const int64_t gm = (M + 63) / 64, gn = (N + 63) / 64;
   if (gm * gn == 0) return BS_OK;
+  if (gm * gn > ((int64_t)1 << 31)) return BS_ERR_SHAPE;
   if (!grad || !bitmask) return BS_ERR_ARG;
   UnpackParams P{};
   P.bitmask = bitmask;
@@ -783,6 +789,7 @@ extern "C" int bs_relu2_grad(void *grad, int grad_dtype, int64_t M, int64_t N, i
   if (M < 0 || N < 0 || ld < N) return BS_ERR_SHAPE;
   const int64_t gm = (M + 63) / 64, gn = (N + 63) / 64;
   if (gm * gn == 0) return BS_OK;
+  if (gm * gn > ((int64_t)1 << 31)) return BS_ERR_SHAPE;
   if (!grad || !bitmask || !prefix) return BS_ERR_ARG;
   if (pack_sbit && !aligned(vals, 4)) return BS_ERR_ALIGN;
   UnpackParams P{};

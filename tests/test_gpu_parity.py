@@ -425,3 +425,33 @@ def test_compress_bias_relu_fp8_equals_separate_steps(M, N, square):
     assert torch.equal(sp.prefix.view(torch.int32), ref.prefix.view(torch.int32))
     assert torch.equal(sp.vals.view(torch.uint8), ref.vals.view(torch.uint8))
     B.check_status()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("per_cta", [False, True])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("pack", [False, True])
+def test_plain_reconstruct_both_kernels(monkeypatch, per_cta, dtype, pack):
+    """The persistent bulk-copy reconstruct and the per-CTA one (forced by
+    BS_UNPACK_PER_CTA) both give back the dense input: ragged shapes, row
+    batches and a shared arena at an odd offset."""
+    if per_cta:
+        monkeypatch.setenv("BS_UNPACK_PER_CTA", "1")
+    g = torch.Generator(device="cuda").manual_seed(11)
+    buf = TensorBuffer(1 << 24, device="cuda", dtype=dtype, pack_sbit=pack)
+    buf.offset.fill_(3)
+    for M, N, mu in ((1000, 3000, 0.0), (130, 70, -1.5), (64, 64, -3.0), (4096, 1024, 0.5)):
+        x = (torch.randn(M, N, generator=g, device="cuda") + mu).relu()
+        x = x.to(dtype) if dtype == torch.bfloat16 else to_fp8(x)[0]
+        sp = dense_to_tilesparse(x, None, buf, pack)
+        out = torch.empty_like(x)
+        unpack_batch_(sp, out, 0, sp.grid_n, N, M, sp.grid_m * sp.grid_n)
+        assert torch.equal(out.view(torch.uint8), x.view(torch.uint8))
+        # second half of the tile rows as one batch
+        m0 = sp.grid_m // 2
+        rows = M - m0 * 64
+        if rows > 0:
+            part = torch.zeros(rows, N, device="cuda", dtype=dtype)
+            unpack_batch_(sp, part, m0, sp.grid_n, N, rows, (sp.grid_m - m0) * sp.grid_n)
+            assert torch.equal(part.view(torch.uint8), x[m0 * 64:].view(torch.uint8))
+    B.check_status()
