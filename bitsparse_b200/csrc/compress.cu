@@ -644,6 +644,8 @@ struct Onepass {
   static constexpr int NS = D + 1 + A;
   // per stage: warp counts [NW], tile inclusive counts [TPP], total
   static constexpr int META = NW + TPP + 1;
+  // counts a thread reads per flush: the grid is capped at CV * NW * 32 + 1
+  static constexpr int CV = 2;
   static constexpr size_t OFF_META = (size_t)NS * IN_BYTES + 32;  // + emit read slack
   static constexpr size_t OFF_BAR = (OFF_META + 4 * NS * META + 7) / 8 * 8;
   static constexpr size_t SMEM = OFF_BAR + 8 * NS;
@@ -801,7 +803,7 @@ __global__ void __launch_bounds__(NW * 32, MINB)
     }
     // 2. counts of the partitions between this CTA's last flushed one and q
     //    (G - 1 of them; a thread reads at most kCv)
-    constexpr int kCv = 2;
+    constexpr int kCv = O::CV;
     uint32_t cv[kCv];
 #pragma unroll
     for (int i = 0; i < kCv; ++i) {
@@ -1140,8 +1142,8 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
   auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS>;
   int resident = resident_ctas(reinterpret_cast<const void *>(kernel), O::SMEM, NW * 32);
   if (resident <= 0) return BS_ERR_LAUNCH;
-  // a flush reads the counts of G - 1 partitions, at most 2 per thread
-  if (resident > 2 * NW * 32 + 1) resident = 2 * NW * 32 + 1;
+  // a flush reads the counts of G - 1 partitions, at most CV per thread
+  if (resident > O::CV * NW * 32 + 1) resident = O::CV * NW * 32 + 1;
   CompressParams Q = P;
   Q.num_parts = (P.num_tiles + O::TPP - 1) / O::TPP;
   if (cudaMemsetAsync(Q.counts_ws, 0, (size_t)Q.num_parts * sizeof(uint32_t), st) !=
