@@ -8,6 +8,8 @@ from __future__ import annotations
 
 import threading
 
+import ctypes as C
+
 import torch
 
 from . import _lib
@@ -108,6 +110,10 @@ def check_status(device: torch.device | None = None, reset: bool = True) -> int:
     device = device or torch.device("cuda", torch.cuda.current_device())
     s = status_word(device)
     v = int(s.item())
+    u = C.c_int32(0)
+    with torch.cuda.device(device):
+        _lib.call("bs_unpack_status", C.addressof(u), int(reset))
+    v |= u.value
     if v and reset:
         s.zero_()
         if v & _lib.BS_STATUS_TIMEOUT:

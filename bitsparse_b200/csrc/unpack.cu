@@ -42,7 +42,6 @@ struct UnpackParams {
   const float *scale;
   float k;       // RELU2_SCALE
   const float *qscale;  // OUT 2: to_fp8 scale of the ReLU^2 reconstruction
-  int32_t *status;  // bounded-wait timeouts (pipelined kernel), or null
   int vals_v16;  // vals base 16-byte aligned
   int out_v32;   // out base + row stride allow 32-byte accesses
 };
@@ -512,6 +511,10 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
 // copied, as the per-CTA kernel's vector loads read it).
 constexpr int kPipeMaskBytes = kUT * kTileBytes;
 
+// Status word of the reconstruct kernels (bs_unpack has no status argument):
+// BS_STATUS_TIMEOUT when a bounded wait gave up.  Read with bs_unpack_status.
+__device__ int32_t g_unpack_status = 0;
+
 template <int SDT, bool PACK>
 __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParams P) {
   constexpr int SB = Elt<SDT>::bytes;
@@ -586,7 +589,7 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
       bool ok = false;
       for (uint32_t n = 0; n < kMaxPolls && !(ok = mbar_try_wait(&bars[buf], (uint32_t)((it >> 1) & 1))); ++n) {
       }
-      if (!ok && tid == 0) status_or(P.status, BS_STATUS_TIMEOUT);
+      if (!ok && tid == 0) status_or(&g_unpack_status, BS_STATUS_TIMEOUT);
     }
     const int64_t pid0 = g * kUT;
     const int nt = tiles_here(P, pid0);
@@ -914,4 +917,17 @@ extern "C" int bs_unpack_relu2_fp8t(const void *vals, const uint8_t *bitmask,
     else unpack_kernel<BS_E5M2, false, 2, false><<<g, kThreads, 0, st>>>(P);
   }
   return launch_err();
+}
+
+extern "C" int bs_unpack_status(int32_t *status_out, int reset) {
+  if (!status_out) return BS_ERR_ARG;
+  // synchronous on the device: every reconstruct launched so far has finished
+  if (cudaMemcpyFromSymbol(status_out, g_unpack_status, sizeof(int32_t)) != cudaSuccess)
+    return BS_ERR_LAUNCH;
+  if (reset && *status_out) {
+    const int32_t zero = 0;
+    if (cudaMemcpyToSymbol(g_unpack_status, &zero, sizeof(int32_t)) != cudaSuccess)
+      return BS_ERR_LAUNCH;
+  }
+  return BS_OK;
 }

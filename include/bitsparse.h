@@ -212,6 +212,12 @@ int bs_unpack(const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
               int64_t K, int64_t batch_rows, int64_t num_tiles_in_batch,
               int relu2, const float *scale, void *stream);
 
+/* Status of the reconstruct kernels of the current device (bs_unpack has
+ * no status argument): *status_out = BS_STATUS_* bits OR-ed since the last
+ * reset (BS_STATUS_TIMEOUT: a bounded wait on the bulk copies of the
+ * persistent reconstruct gave up).  Synchronous; reset != 0 clears it. */
+int bs_unpack_status(int32_t *status_out, int reset);
+
 /* In place grad <- bit ? grad : 0 for a bf16 [M, N] gradient (row stride
  * ld).  Replaces mask_with_bitmask_ (lib_sparse/src/triton_operators.py:165-175,
  * lib_sparse/src/triton_kernels.py:249-276). */
