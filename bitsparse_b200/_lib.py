@@ -53,6 +53,7 @@ _SIGS = {
                          _i64, _i32, _vp, _vp]),
     "bs_mask_with_bitmask": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp]),
     "bs_unpack_status": (_i32, [_vp, _i32]),
+    "bs_quantize_e4m3_2d": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp]),
     "bs_unpack_relu2_fp8t": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _vp, C.c_float, _vp,
                                     _vp, _vp, _i64, _vp]),
     "bs_relu2_grad": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i32, _i32, _vp,

@@ -182,6 +182,78 @@ quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q) {
   }
 }
 
+// to_fp8's quantiser on a bf16 [R, C] tensor (row stride ld) into either or
+// both fp8 layouts: q [R, C] (row stride ldq) and qT [C, R] (row stride
+// ldqT), the transposed copy cuBLASLt's fp8 GEMMs want for an operand in the
+// other major order -- one read of the bf16 tensor instead of a quantise
+// pass plus a transpose pass over its fp8 copy.  A CTA quantises a 64 x 64
+// tile (16 values per thread, div_e4m3x8) and, for qT, turns it through
+// shared memory.
+__global__ void __launch_bounds__(kThreads)
+quant2d_kernel(const uint8_t *x, int64_t R, int64_t C, int64_t ld, const float *scale,
+               uint8_t *q, int64_t ldq, uint8_t *qT, int64_t ldqT, int vx, int vq, int vqT) {
+  __shared__ uint8_t t[64][64 + 4];
+  const float s = *scale;
+  const float rc = __frcp_rn(s);
+  const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
+  const int tid = threadIdx.x;
+  {  // row tid/4, 16 values at column (tid%4)*16
+    const int r = tid >> 2, cq = (tid & 3) * 16;
+    const int64_t gr = r0 + r, gc = c0 + cq;
+    uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const bool full = gr < R && gc + 16 <= C;
+    if (gr < R) {
+      const uint8_t *src = x + (gr * ld + gc) * 2;
+      if (vx && full) {
+        const uint4 v0 = ld_nc_v4(src), v1 = ld_nc_v4(src + 16);
+        w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
+        w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
+      } else {
+        for (int e = 0; e < 16; ++e)
+          if (gc + e < C)
+            w[e >> 1] |= (uint32_t)reinterpret_cast<const uint16_t *>(src)[e] << (16 * (e & 1));
+      }
+    }
+    uint32_t o[4];
+    {
+      const uint32_t lo[4] = {w[0], w[1], w[2], w[3]}, hi[4] = {w[4], w[5], w[6], w[7]};
+      uint32_t o2[2];
+      div_e4m3x8(lo, s, rc, o2);
+      o[0] = o2[0]; o[1] = o2[1];
+      div_e4m3x8(hi, s, rc, o2);
+      o[2] = o2[0]; o[3] = o2[1];
+    }
+    if (q != nullptr && gr < R) {
+      uint8_t *dst = q + gr * ldq + gc;
+      if (vq && full) {
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+      } else {
+        for (int e = 0; e < 16; ++e)
+          if (gc + e < C) dst[e] = (uint8_t)(o[e >> 2] >> (8 * (e & 3)));
+      }
+    }
+    if (qT == nullptr) return;  // uniform over the CTA
+#pragma unroll
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<uint32_t *>(&t[r][cq + 4 * i]) = o[i];
+  }
+  __syncthreads();
+  {  // qT row c0 + tid/4 (a column of x), 16 values of rows r0 + (tid%4)*16 ..
+    const int c = tid >> 2, rq = (tid & 3) * 16;
+    const int64_t gr = c0 + c, gc = r0 + rq;
+    if (gr >= C) return;
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w[e >> 2] |= (uint32_t)t[rq + e][c] << (8 * (e & 3));
+    uint8_t *dst = qT + gr * ldqT + gc;
+    if (vqT && gc + 16 <= R) {
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      for (int e = 0; e < 16; ++e)
+        if (gc + e < R) dst[e] = (uint8_t)(w[e >> 2] >> (8 * (e & 3)));
+    }
+  }
+}
+
 // dst[c][r] = src[r][c] for 1-byte elements (fp8 operands that cuBLASLt
 // wants in the other major order).  A CTA moves a 64 x 64 byte tile through
 // shared memory: 16-byte coalesced loads of source rows, 16-byte stores of
@@ -303,3 +375,19 @@ extern "C" int bs_transpose_b8(const void *src, int64_t rows, int64_t cols, int6
 }
 
 extern "C" const char *bs_version(void) { return "bitsparse_b200 0.1 sm_100a"; }
+
+extern "C" int bs_quantize_e4m3_2d(const void *x, int64_t R, int64_t C, int64_t ld,
+                                   const float *scale, uint8_t *q, int64_t ldq, uint8_t *qT,
+                                   int64_t ldqT, void *stream) {
+  if (R < 0 || C < 0 || ld < C || (q && ldq < C) || (qT && ldqT < R)) return BS_ERR_SHAPE;
+  if (R == 0 || C == 0 || (!q && !qT)) return BS_OK;
+  if (!x || !scale) return BS_ERR_ARG;
+  const dim3 grid((unsigned)((C + 63) / 64), (unsigned)((R + 63) / 64));
+  if ((C + 63) / 64 > 0x7FFFFFFF || grid.y > 65535) return BS_ERR_SHAPE;
+  const int vx = aligned16(x) && (ld * 2) % 16 == 0;
+  const int vq = q && aligned16(q) && ldq % 16 == 0;
+  const int vqT = qT && aligned16(qT) && ldqT % 16 == 0;
+  quant2d_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t *>(x), R, C, ld, scale, q, ldq, qT, ldqT, vx, vq, vqT);
+  return launch_err();
+}

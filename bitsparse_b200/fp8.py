@@ -39,10 +39,14 @@ def _dense_layout(x: Tensor) -> tuple[Tensor, bool]:
     that transpose, so no transposed copy is made; the result is transposed
     back as a view, keeping x's layout."""
     if x.is_contiguous():
-        return x, False
-    if x.dim() == 2 and x.T.is_contiguous():
-        return x.T, True
-    return x.contiguous(), False
+        t, tr = x, False
+    elif x.dim() == 2 and x.T.is_contiguous():
+        t, tr = x.T, True
+    else:
+        return x.contiguous(), False
+    if t.data_ptr() % 16:  # a view at an odd offset: the kernels read 16-byte vectors
+        t = t.clone(memory_format=torch.contiguous_format)
+    return t, tr
 
 
 @torch.no_grad()
@@ -81,6 +85,42 @@ def to_fp8(x: Tensor) -> tuple[Tensor, Tensor]:
     """(x_fp8, scale): per-tensor e4m3fn quantisation (lib_sparse/fp8.py:123-129)."""
     scale = fp8_scale(x)
     return quantize_e4m3(x, scale), scale
+
+
+@torch.no_grad()
+def quantize_e4m3_layouts(x: Tensor, scale: Tensor, row: bool = True,
+                          col: bool = False) -> tuple[Tensor | None, Tensor | None]:
+    """e4m3fn(x / scale) of a 2-D bf16 tensor in the layouts asked for:
+    ``row`` -> a row-major (unit column stride) tensor, ``col`` -> a
+    column-major one (unit row stride, the order cuBLASLt's fp8 GEMMs take
+    for operand B), both from one read of x (bs_quantize_e4m3_2d).  Same
+    codes as ``quantize_e4m3``."""
+    from . import _lib, _runtime as R
+
+    R.require_cuda(x, "x")
+    if x.dim() != 2 or x.dtype != torch.bfloat16:
+        raise TypeError("quantize_e4m3_layouts takes a 2-D bfloat16 tensor")
+    xc, transposed = _dense_layout(x)  # xc contiguous; x == xc.T when transposed
+    rows, cols = xc.shape
+    # q of xc is xc's row-major layout; qT of xc is its column-major one
+    want_q = col if transposed else row
+    want_qT = row if transposed else col
+    q = torch.empty((rows, cols), dtype=_FP8_DTYPE, device=x.device) if want_q else None
+    qT = torch.empty((cols, rows), dtype=_FP8_DTYPE, device=x.device) if want_qT else None
+    ld = xc.stride(0) if rows > 1 else cols  # a single row's stride is arbitrary
+    _lib.call("bs_quantize_e4m3_2d", xc.data_ptr(), rows, cols, ld, scale.data_ptr(),
+              R.ptr(q), cols, R.ptr(qT), rows, R.stream_handle(x.device))
+    if transposed:  # x = xc.T: x's row-major form is qT, its column-major form q.T
+        return (qT if row else None), (q.T if col else None)
+    return (q if row else None), (qT.T if col else None)
+
+
+def to_fp8_layouts(x: Tensor, row: bool = True, col: bool = False):
+    """(x_fp8 row-major or None, x_fp8 column-major or None, scale): to_fp8
+    with the layouts the fp8 GEMMs need, without a transpose pass."""
+    scale = fp8_scale(x)
+    r, c = quantize_e4m3_layouts(x, scale, row, col)
+    return r, c, scale
 
 
 def _transposed_b8(x: Tensor) -> Tensor:
@@ -128,13 +168,13 @@ class MatmulFp8(Function):
             ctx.a_scale, ctx.b_scale = a_scale, b_scale
         if a.dtype == torch.bfloat16:
             assert a_scale is None
-            a_fp8, a_scale = to_fp8(a)
+            a_fp8, _, a_scale = to_fp8_layouts(a, row=True)
         else:
             assert a_scale is not None
             a_fp8 = a
         if b.dtype == torch.bfloat16:
             assert b_scale is None
-            b_fp8, b_scale = to_fp8(b)
+            _, b_fp8, b_scale = to_fp8_layouts(b, row=False, col=True)  # B column-major
         else:
             assert b_scale is not None
             b_fp8 = b
@@ -145,20 +185,39 @@ class MatmulFp8(Function):
 
     @staticmethod
     def backward(ctx, grad_output: Tensor):
+        need_a, need_b = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         if CACHE_FP8_MATMUl:
             a_fp8, b_fp8, a_scale, b_scale = ctx.saved_tensors
         else:
             a, b = ctx.saved_tensors
             a_scale, b_scale = ctx.a_scale, ctx.b_scale
-            a_fp8, a_scale = to_fp8(a) if a.dtype == torch.bfloat16 else (a, a_scale)
-            b_fp8, b_scale = to_fp8(b) if b.dtype == torch.bfloat16 else (b, b_scale)
-        g_fp8, g_scale = to_fp8(grad_output.contiguous())
+            # each operand is quantised straight into the layout its GEMM
+            # takes: a^T row-major (a column-major) for grad_b, b row-major
+            # (so b^T is column-major) for grad_a
+            if a.dtype == torch.bfloat16 and a.dim() == 2 and need_b:
+                _, a_fp8, a_scale = to_fp8_layouts(a, row=False, col=True)
+            elif a.dtype == torch.bfloat16:
+                a_fp8, a_scale = to_fp8(a)
+            else:
+                a_fp8 = a
+            if b.dtype == torch.bfloat16 and b.dim() == 2 and need_a:
+                b_fp8, _, b_scale = to_fp8_layouts(b, row=True)
+            elif b.dtype == torch.bfloat16:
+                b_fp8, b_scale = to_fp8(b)
+            else:
+                b_fp8 = b
+        g = grad_output.contiguous()
+        if g.dim() == 2 and g.dtype == torch.bfloat16:
+            g_fp8, g_col, g_scale = to_fp8_layouts(g, row=need_a or not need_b, col=need_b)
+        else:
+            g_fp8, g_scale = to_fp8(g)
+            g_col = None
         grad_a = grad_b = None
-        if ctx.needs_input_grad[0]:
+        if need_a:
             grad_a = _scaled_mm(g_fp8, b_fp8.T, g_scale, b_scale, output_dtype=torch.bfloat16)
-        if ctx.needs_input_grad[1]:
-            grad_b = _scaled_mm(_row_major_fp8(a_fp8.T), g_fp8, a_scale, g_scale,
-                                output_dtype=torch.bfloat16)
+        if need_b:
+            grad_b = _scaled_mm(_row_major_fp8(a_fp8.T), g_col if g_col is not None else g_fp8,
+                                a_scale, g_scale, output_dtype=torch.bfloat16)
         return grad_a, grad_b, None, None
 
 

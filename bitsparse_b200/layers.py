@@ -13,7 +13,7 @@ from torch.autograd import Function
 
 from .bitsparse import BitsparseTensor, TensorBuffer
 from .config import RELU2_SCALE
-from .fp8 import is_fp8, matmul, to_fp8
+from .fp8 import is_fp8, matmul, to_fp8, to_fp8_layouts
 from .src.functions import dense_to_tilesparse, relu_to_tilesparse_fp8
 from .src.operators import (compress_bias_relu, compress_bias_relu_fp8, mask_with_bitmask_,
                             matmul_relu_mask, relu2_grad_sparse_)
@@ -89,11 +89,12 @@ class ReluLinear(Function):
         h: BitsparseTensor = ctx.h_sparse
         ctx.h_sparse = None
         fp8 = is_fp8(ctx.dtype)
-        if fp8:
-            grad_output, scale = to_fp8(grad_output.contiguous())
+        if fp8:  # both layouts of to_fp8(grad_output) from one pass
+            grad_output, go_col, scale = to_fp8_layouts(grad_output.contiguous(), row=needs_z,
+                                                        col=True)
         else:
-            scale = None
-        grad_W2 = AspB(grad_output.T, h, A_scale=scale)
+            go_col, scale = grad_output, None
+        grad_W2 = AspB(go_col.T, h, A_scale=scale)
         if needs_z and not fp8:
             grad_z = _relu_grad(grad_output, W, h)
         elif needs_z:
@@ -178,11 +179,12 @@ class Relu2Linear(Function):
         h: BitsparseTensor = ctx.h_sparse
         ctx.h_sparse = None
         fp8 = is_fp8(ctx.dtype)
-        if fp8:
-            grad_output, scale = to_fp8(grad_output.contiguous())
+        if fp8:  # both layouts of to_fp8(grad_output) from one pass
+            grad_output, go_col, scale = to_fp8_layouts(grad_output.contiguous(), row=needs_z,
+                                                        col=True)
         else:
-            scale = None
-        grad_W2 = AspRelu2B(grad_output.T, h, A_scale=scale)
+            go_col, scale = grad_output, None
+        grad_W2 = AspRelu2B(go_col.T, h, A_scale=scale)
         if needs_z:
             grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
             grad_z = relu2_grad_sparse_(grad_h, h)

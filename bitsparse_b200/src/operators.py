@@ -40,6 +40,12 @@ def _row_major(t: Tensor, name: str) -> tuple[Tensor, int]:
     return t, max(t.stride(0), t.shape[1])
 
 
+def _ld(t: Tensor) -> int:
+    """Row stride of a 2-D tensor for the C ABI (a single row's stride is
+    arbitrary in torch; the kernels want at least the row length)."""
+    return t.stride(0) if t.shape[0] > 1 else t.shape[1]
+
+
 def _stream(t: Tensor) -> int:
     return R.stream_handle(t.device)
 
@@ -189,7 +195,7 @@ def _unpack(sparse: BitsparseTensor, output: Tensor, first_m_tile: int, grid_n: 
     _lib.call("bs_unpack", sparse.vals.data_ptr(), sparse.bitmask.data_ptr(),
               sparse.prefix.data_ptr(), sparse.vals_offset.data_ptr(),
               R.dtype_code(sparse.dtype), int(sparse.pack_sbit), output.data_ptr(),
-              output.stride(0), first_m_tile, grid_n, K, batch_rows, num_tiles_in_batch,
+              _ld(output), first_m_tile, grid_n, K, batch_rows, num_tiles_in_batch,
               int(relu2), R.ptr(scale), _stream(output))
     return output
 
@@ -224,7 +230,7 @@ def mask_with_bitmask_(grad: Tensor, sparse: BitsparseTensor) -> Tensor:
     if tuple(grad.shape) != (M, N) or grad.stride(1) != 1:
         raise ValueError("grad must be [M, N] with unit column stride")
     _lib.call("bs_mask_with_bitmask", grad.data_ptr(), R.dtype_code(grad.dtype), M, N,
-              grad.stride(0), sparse.bitmask.data_ptr(), _stream(grad))
+              _ld(grad), sparse.bitmask.data_ptr(), _stream(grad))
     return grad
 
 
@@ -240,7 +246,7 @@ def relu2_grad_sparse_(grad: Tensor, sparse_z: BitsparseTensor) -> Tensor:
     if scale is not None:
         scale = scale.to(device=grad.device, dtype=torch.float32)
     _lib.call("bs_relu2_grad", grad.data_ptr(), R.dtype_code(grad.dtype), M, N,
-              grad.stride(0), sparse_z.vals.data_ptr(), sparse_z.bitmask.data_ptr(),
+              _ld(grad), sparse_z.vals.data_ptr(), sparse_z.bitmask.data_ptr(),
               sparse_z.prefix.data_ptr(), sparse_z.vals_offset.data_ptr(),
               R.dtype_code(sparse_z.dtype), int(sparse_z.pack_sbit), R.ptr(scale),
               _stream(grad))

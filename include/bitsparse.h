@@ -212,6 +212,15 @@ int bs_unpack(const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
               int64_t K, int64_t batch_rows, int64_t num_tiles_in_batch,
               int relu2, const float *scale, void *stream);
 
+/* to_fp8's quantiser e4m3(bf16(x / *scale)) (lib_sparse/fp8.py:127) on a
+ * bf16 [R, C] tensor x (row stride ld), written to q [R, C] (row stride
+ * ldq) and/or qT [C, R] (row stride ldqT, the transposed copy) -- the
+ * reference's to_fp8 followed by the column-major copy its FP8 GEMM makes
+ * of an operand (lib_sparse/fp8.py:15-17), in one read of x.  Either
+ * output may be NULL. */
+int bs_quantize_e4m3_2d(const void *x, int64_t R, int64_t C, int64_t ld, const float *scale,
+                        uint8_t *q, int64_t ldq, uint8_t *qT, int64_t ldqT, void *stream);
+
 /* Status of the reconstruct kernels of the current device (bs_unpack has
  * no status argument): *status_out = BS_STATUS_* bits OR-ed since the last
  * reset (BS_STATUS_TIMEOUT: a bounded wait on the bulk copies of the

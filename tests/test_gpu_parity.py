@@ -455,3 +455,34 @@ def test_plain_reconstruct_both_kernels(monkeypatch, per_cta, dtype, pack):
             unpack_batch_(sp, part, m0, sp.grid_n, N, rows, (sp.grid_m - m0) * sp.grid_n)
             assert torch.equal(part.view(torch.uint8), x[m0 * 64:].view(torch.uint8))
     B.check_status()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R, C", [(64, 64), (300, 200), (1, 17), (4096, 768), (129, 4097)])
+@pytest.mark.parametrize("view", ["plain", "transposed", "strided"])
+def test_quantize_layouts_equal_to_fp8_copies(R, C, view):
+    """bs_quantize_e4m3_2d: both layouts == to_fp8's codes and their
+    transposed copy, bit for bit, for plain, transposed (W.T) and row-strided
+    inputs."""
+    from bitsparse_b200.fp8 import fp8_scale, quantize_e4m3, quantize_e4m3_layouts
+    g = torch.Generator(device="cuda").manual_seed(R * 31 + C)
+    if view == "transposed":
+        x = (3 * torch.randn(C, R, generator=g, device="cuda")).to(torch.bfloat16).T
+    elif view == "strided":
+        x = (3 * torch.randn(R, C + 9, generator=g, device="cuda")).to(torch.bfloat16)[:, 5:5 + C]
+    else:
+        x = (3 * torch.randn(R, C, generator=g, device="cuda")).to(torch.bfloat16)
+    s = fp8_scale(x)
+    ref = quantize_e4m3(x.contiguous(), s).view(torch.uint8)
+    for row, col in ((True, False), (False, True), (True, True)):
+        r, c = quantize_e4m3_layouts(x, s, row, col)
+        if row:
+            assert r.stride(1) == 1 and tuple(r.shape) == (R, C)
+            assert torch.equal(r.view(torch.uint8), ref)
+        else:
+            assert r is None
+        if col:
+            assert c.stride(0) == 1 and tuple(c.shape) == (R, C)
+            assert torch.equal(c.T.contiguous().view(torch.uint8), ref.T.contiguous())
+        else:
+            assert c is None
