@@ -676,12 +676,24 @@ __device__ __forceinline__ void emit_words(const CompressParams &P, const uint8_
   const int tail0 = nfull ? head + nfull * EPV : 0;     // first element after them
   const uint32_t *s32 = reinterpret_cast<const uint32_t *>(stage);
   uint4 *dst = reinterpret_cast<uint4 *>(vals + (g0 + head) * C::SB);
+  // Vector v starts at stage byte head * SB + 16 v: its word offset within a
+  // 16-byte group (o) and byte shift (sh) are the same for every vector, so
+  // each lane reads the two aligned 16-byte groups covering its five words
+  // (consecutive lanes, consecutive groups: no bank conflicts) and picks the
+  // five with a warp-uniform offset.  The reads end at most 16 bytes past
+  // the stage's values (slack / the next stage).
+  const int rel0 = head * C::SB;
+  const int o = (rel0 >> 2) & 3;
+  const uint32_t sh = (uint32_t)(rel0 & 3) * 8u;
   for (int v = lane; v < nfull; v += NT) {
-    const int rel = (head + v * EPV) * C::SB;  // stage byte of the vector
-    const int j = rel >> 2;
-    const uint32_t sh = (uint32_t)(rel & 3) * 8u;
-    const uint32_t w0 = s32[j], w1 = s32[j + 1], w2 = s32[j + 2], w3 = s32[j + 3],
-                   w4 = s32[j + 4];
+    const int j0 = ((rel0 >> 2) & ~3) + 4 * v;  // first word of the aligned group
+    const uint4 A = *reinterpret_cast<const uint4 *>(s32 + j0);
+    const uint4 B = *reinterpret_cast<const uint4 *>(s32 + j0 + 4);
+    uint32_t w0, w1, w2, w3, w4;
+    if (o == 0) { w0 = A.x; w1 = A.y; w2 = A.z; w3 = A.w; w4 = B.x; }
+    else if (o == 1) { w0 = A.y; w1 = A.z; w2 = A.w; w3 = B.x; w4 = B.y; }
+    else if (o == 2) { w0 = A.z; w1 = A.w; w2 = B.x; w3 = B.y; w4 = B.z; }
+    else { w0 = A.w; w1 = B.x; w2 = B.y; w3 = B.z; w4 = B.w; }
     dst[v] = make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh),
                         __funnelshift_r(w2, w3, sh), __funnelshift_r(w3, w4, sh));
   }
