@@ -167,6 +167,14 @@ def run_reference(args):
 # our arm
 # ---------------------------------------------------------------------------
 def make_relu_bf16(M, N, mu, seed, device, variant="A", target=0.5):
+    """relu of a seeded N(mu, 1) bf16 [M, N] tensor; ``target`` is the
+    SPARSITY (fraction of zeros) the variant aims at.
+
+    A: the mean mu sets the sparsity (mu = -ndtri(target)).
+    B: each row's density is drawn from Beta(2,2) scaled around 1 - target.
+    C: a fraction target / 2 of the 64-column strips is zeroed outright and
+       the rest is N(mu', 1) with mu' chosen so that the total sparsity is
+       target (half of the zeros come from whole strips)."""
     import torch
 
     g = torch.Generator(device=device).manual_seed(seed)
@@ -176,11 +184,14 @@ def make_relu_bf16(M, N, mu, seed, device, variant="A", target=0.5):
         dens = (2 * (1 - target) * d).clamp(1e-4, 0.9999)
         mu_row = torch.special.ndtri(dens)  # P(N(mu,1) > 0) = dens
         x = x + mu_row
+    elif variant == "C":
+        zf = target / 2
+        rest = (target - zf) / (1 - zf)  # sparsity of the strips left alone
+        x = x - float(torch.special.ndtri(torch.tensor(rest, dtype=torch.float64)))
+        strips = torch.rand(N // 64, generator=g, device=device) < zf
+        x.view(M, N // 64, 64)[:, strips, :] = -1.0
     else:
         x = x + mu
-    if variant == "C":  # zero contiguous 64-column runs (half of all strips)
-        strips = torch.rand(N // 64, generator=g, device=device) < 0.5
-        x.view(M, N // 64, 64)[:, strips, :] = -1.0
     return x.relu_().to(torch.bfloat16)
 
 
@@ -462,7 +473,7 @@ def run_ours(args):
                                (0.99, -2.3263)):
                 if variant != "A" and target not in (0.5, 0.9):
                     continue
-                x2 = [make_relu_bf16(M, N, mu, 7 + i, dev, variant, 1 - target)
+                x2 = [make_relu_bf16(M, N, mu, 7 + i, dev, variant, target)
                       for i in range(2)]
                 s2, _ = time_round_trips(x2, bufs, outs, 4)
                 torch.cuda.synchronize()

@@ -53,11 +53,15 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if verbose:
         common += ["-Xptxas", "-v"]
     common += os.environ.get("BS_NVCC_EXTRA", "").split()
-    for src in sources():
+    from concurrent.futures import ThreadPoolExecutor
+
+    def compile_one(src):
         obj = build_dir / (src.stem + ".o")
-        cmd = common + ["-c", str(src), "-o", str(obj)]
-        subprocess.run(cmd, check=True)
-        objs.append(str(obj))
+        subprocess.run(common + ["-c", str(src), "-o", str(obj)], check=True)
+        return str(obj)
+
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(compile_one, sources()))
     tmp = LIB.with_suffix(".so.tmp")
     subprocess.run([nvcc, *ARCH, "-shared", "-o", str(tmp), *objs, "-lcudart"], check=True)
     os.replace(tmp, LIB)

@@ -1241,6 +1241,8 @@ static int fill_common(CompressParams &P, const void *dense, int dt, int64_t M, 
   P.M = M; P.N = N; P.ld = ld;
   P.grid_n = (N + kTileN - 1) / kTileN;
   const int64_t grid_m = (M + kTileM - 1) / kTileM;
+  // bound the factors before multiplying (M, N near 2^62 would wrap)
+  if (P.grid_n > 0 && grid_m > ((int64_t)1 << 31) / P.grid_n) return BS_ERR_SHAPE;
   P.num_tiles = grid_m * P.grid_n;
   if (P.num_tiles > (int64_t)1 << 31) return BS_ERR_SHAPE;
   const int tpp = tpp_for(eb, mode);
@@ -1448,7 +1450,9 @@ std::mutex g_scratch_mu;
 
 // Device address of the scratch array on the current device.  The symbol's
 // host-side name is only a stand-in; the address comes from
-// cudaGetSymbolAddress, once per device, with that device current.
+// cudaGetSymbolAddress, once per device, with that device current.  The
+// cached address is not refreshed after cudaDeviceReset: a process that
+// resets a device must not call bs_compress_noalloc on it again.
 int noalloc_scratch(void **out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BS_ERR_LAUNCH;
@@ -1473,17 +1477,27 @@ extern "C" int bs_compress_noalloc(const void *dense, int in_dtype, int64_t M, i
                                    int64_t *vals_offset_out, int64_t *nnz_out, int32_t *status,
                                    void *stream) {
   if (M < 0 || N < 0) return BS_ERR_SHAPE;
-  const int64_t tiles = ((M + kTileM - 1) / kTileM) * ((N + kTileN - 1) / kTileN);
-  if (tiles > kNoAllocMaxTiles) return BS_ERR_TOO_LARGE;
+  const int64_t gm = (M + kTileM - 1) / kTileM, gn = (N + kTileN - 1) / kTileN;
+  // bound the factors one at a time: their product could wrap
+  if (gn > 0 && gm > kNoAllocMaxTiles / gn) return BS_ERR_TOO_LARGE;
   void *scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
+  // Every host-side check runs before anything is queued: a call that is
+  // refused leaves the shared array alone.
+  CompressParams P{};
+  rc = setup_compress(P, dense, in_dtype, M, N, ld, quant_scale, quant_out, bitmask, prefix, vals,
+                      vals_capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out, scratch,
+                      kNoAllocScratchBytes, status);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (P.num_tiles == 0) {
+    if (cudaMemsetAsync(prefix, 0, sizeof(uint32_t), st) != cudaSuccess) return BS_ERR_LAUNCH;
+    return BS_OK;
+  }
   // The compressor leaves its scratch zeroed, but a call that gave up (a
   // bounded wait that expired) may not have; start every call from zero.
-  const size_t used = bs_compress_workspace_bytes(tiles);
-  if (cudaMemsetAsync(scratch, 0, used, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+  if (cudaMemsetAsync(scratch, 0, bs_compress_workspace_bytes(P.num_tiles), st) != cudaSuccess)
     return BS_ERR_LAUNCH;
-  return bs_compress(dense, in_dtype, M, N, ld, quant_scale, quant_out, bitmask, prefix, vals,
-                     vals_capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out, scratch,
-                     kNoAllocScratchBytes, status, stream);
+  return dispatch<0>(P, in_dtype, quant_scale != nullptr, pack_sbit, st);
 }

@@ -475,19 +475,26 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap 
                 const GemmParams &P, cudaStream_t st) {
   using G = GemmCfg<CG>;
   auto kernel = gemm_mask_kernel<MASK, CG>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM);
-  });
-  if (attr_err != cudaSuccess) return BS_ERR_LAUNCH;
-  static int sms = [] {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n > 0 ? n : 1;
-  }();
+  // The shared-memory attribute is per device and the SM count may differ
+  // between devices: both are set up once for each device this process uses.
+  constexpr int kMaxDev = 64;
+  static std::mutex mu;
+  static int sms_of[kMaxDev] = {};  // 0: not yet set up on that device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return BS_ERR_LAUNCH;
+  int sms;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!sms_of[dev]) {
+      int n = 0;
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)G::SMEM) != cudaSuccess ||
+          cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return BS_ERR_LAUNCH;
+      sms_of[dev] = n;
+    }
+    sms = sms_of[dev];
+  }
   const int64_t tiles = ((P.M + G::BM - 1) / G::BM) * ((P.N + kBN - 1) / kBN);
   const int64_t slots = sms / CG;  // persistent: one CTA (pair) per SM (pair)
   cudaLaunchConfig_t cfg = {};

@@ -40,7 +40,13 @@ def row_range(M: int, rank: int, world: int, block: int = BLOCK_M) -> tuple[int,
 
 
 def _values(sp: BitsparseTensor) -> torch.Tensor:
-    """The shard's own nnz raw values (a slice of an arena when shared)."""
+    """The shard's own nnz raw values (a slice of an arena when shared).
+
+    nnz is the uint32 prefix[-1], which wraps once a shard holds 2^32 values;
+    such shards are refused rather than merged with a truncated stream."""
+    if sp.shape[0] * sp.shape[1] >= 1 << 32:
+        raise ValueError("a shard of 2^32 or more elements cannot be merged: its value "
+                         "count does not fit the uint32 prefix")
     nnz = int(sp.prefix[-1].item())
     off = int(sp.vals_offset.reshape(-1)[0].item())
     return sp.vals[off: off + nnz]

@@ -86,26 +86,27 @@ class ReluLinear(Function):
     def backward(ctx, grad_output: Tensor):
         W = ctx.saved_tensors[0]
         needs_z = ctx.needs_input_grad[0]
+        needs_bias = ctx.has_bias and ctx.needs_input_grad[5]
+        # the bias gradient is the column sum of grad_z, so grad_z is formed
+        # whenever either of them is wanted
+        want_z = needs_z or needs_bias
         h: BitsparseTensor = ctx.h_sparse
         ctx.h_sparse = None
         fp8 = is_fp8(ctx.dtype)
         if fp8:  # both layouts of to_fp8(grad_output) from one pass
-            grad_output, go_col, scale = to_fp8_layouts(grad_output.contiguous(), row=needs_z,
+            grad_output, go_col, scale = to_fp8_layouts(grad_output.contiguous(), row=want_z,
                                                         col=True)
         else:
             go_col, scale = grad_output, None
-        grad_W2 = AspB(go_col.T, h, A_scale=scale)
-        if needs_z and not fp8:
+        grad_W2 = AspB(go_col.T, h, A_scale=scale) if ctx.needs_input_grad[1] else None
+        grad_z = None
+        if want_z and not fp8:
             grad_z = _relu_grad(grad_output, W, h)
-        elif needs_z:
+        elif want_z:
             grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
             grad_z = mask_with_bitmask_(grad_h, h)
-        else:
-            grad_z = None
-        grad_bias = None
-        if ctx.has_bias and ctx.needs_input_grad[5]:
-            grad_bias = grad_z.sum(0) if grad_z is not None else None
-        return grad_z, grad_W2, None, None, None, grad_bias
+        grad_bias = grad_z.sum(0) if needs_bias else None
+        return (grad_z if needs_z else None), grad_W2, None, None, None, grad_bias
 
 
 class FFNRelu:
@@ -124,8 +125,6 @@ class FFNRelu:
             # bias add and ReLU fused into the compression pass
             y = ReluLinear.apply(z, W2, sparse_data, pack_sbit, dtype, b1)
         else:
-            if b1 is not None:
-                z = z + b1
             y = ReluLinear.apply(z, W2, sparse_data, pack_sbit, dtype)
         y = y.reshape(*bs_dims, y.shape[-1])
         if b2 is not None:
@@ -176,24 +175,23 @@ class Relu2Linear(Function):
     def backward(ctx, grad_output: Tensor):
         W = ctx.saved_tensors[0]
         needs_z = ctx.needs_input_grad[0]
+        needs_bias = ctx.has_bias and ctx.needs_input_grad[5]
+        want_z = needs_z or needs_bias  # the bias gradient is grad_z's column sum
         h: BitsparseTensor = ctx.h_sparse
         ctx.h_sparse = None
         fp8 = is_fp8(ctx.dtype)
         if fp8:  # both layouts of to_fp8(grad_output) from one pass
-            grad_output, go_col, scale = to_fp8_layouts(grad_output.contiguous(), row=needs_z,
+            grad_output, go_col, scale = to_fp8_layouts(grad_output.contiguous(), row=want_z,
                                                         col=True)
         else:
             go_col, scale = grad_output, None
-        grad_W2 = AspRelu2B(go_col.T, h, A_scale=scale)
-        if needs_z:
+        grad_W2 = AspRelu2B(go_col.T, h, A_scale=scale) if ctx.needs_input_grad[1] else None
+        grad_z = None
+        if want_z:
             grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
             grad_z = relu2_grad_sparse_(grad_h, h)
-        else:
-            grad_z = None
-        grad_bias = None
-        if ctx.has_bias and ctx.needs_input_grad[5] and grad_z is not None:
-            grad_bias = grad_z.sum(0)
-        return grad_z, grad_W2, None, None, None, grad_bias
+        grad_bias = grad_z.sum(0) if needs_bias else None
+        return (grad_z if needs_z else None), grad_W2, None, None, None, grad_bias
 
 
 class FFNRelu2:

@@ -172,9 +172,11 @@ int bs_fp8_scales_bias_relu(const void *z, int64_t M, int64_t N, int64_t ld,
  * may have at most bs_compress_noalloc_max_tiles() 64x64 tiles (262144, e.g.
  * 16384 x 65536 elements); larger tensors return BS_ERR_TOO_LARGE.  The
  * first call on a device looks up the array's device address (make that
- * first call before any stream capture).  Each call clears the scratch it
- * uses with cudaMemsetAsync on `stream`; all calls share the array, so calls
- * that overlap on the GPU race -- serialise them. */
+ * first call before any stream capture; the address is not looked up again,
+ * so do not use this entry point on a device after cudaDeviceReset).  Every
+ * argument is checked before anything is queued; a call that passes clears
+ * the scratch it uses with cudaMemsetAsync on `stream`.  All calls share the
+ * array, so calls that overlap on the GPU race -- serialise them. */
 int bs_compress_noalloc(const void *dense, int in_dtype, int64_t M, int64_t N,
                         int64_t ld, const float *quant_scale, uint8_t *quant_out,
                         uint8_t *bitmask, uint32_t *prefix, void *vals,

@@ -63,6 +63,13 @@ def test_version_and_workspace_size():
      _lib.BS_ERR_DTYPE),
     # fp8 scale: misaligned input
     (lambda L: L.bs_fp8_scale(17, 0, 100, 16, 16, None), _lib.BS_ERR_ALIGN),
+    # huge M and N: the tile count must not wrap
+    (lambda L: L.bs_compress(16, 0, 1 << 40, 1 << 40, 1 << 40, None, None, 16, 16, 16, 16, 0,
+                             None, None, None, 16, 1 << 20, None, None), _lib.BS_ERR_SHAPE),
+    (lambda L: L.bs_compress(16, 0, 1 << 62, 1 << 62, 1 << 62, None, None, 16, 16, 16, 16, 0,
+                             None, None, None, 16, 1 << 20, None, None), _lib.BS_ERR_SHAPE),
+    (lambda L: L.bs_compress_noalloc(16, 0, 1 << 40, 1 << 40, 1 << 40, None, None, 16, 16, 16,
+                                     16, 0, None, None, None, None, None), _lib.BS_ERR_TOO_LARGE),
 ])
 def test_host_argument_checks(call, code):
     assert call(_lib.load()) == code

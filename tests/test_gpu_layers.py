@@ -200,3 +200,24 @@ def test_ffn_fused_masked_gemm_path_bit_exact(monkeypatch):
     for n, a, p in zip(("x", "W1", "W2", "b1", "b2"), grads, ps):
         assert torch.equal(a, p.grad), n
     B.check_status()
+
+
+@pytest.mark.parametrize("relu2", [False, True])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_bias_only_gradient(relu2, fp8):
+    """x, W1 and W2 frozen, only b1 trains: b1 still gets its gradient (the
+    column sum of grad_z), equal to the dense-activation twin's."""
+    T, d, H, do = 512, 256, 1024, 256
+    x, W1, W2, b1, b2, gy = make(T, d, H, do, seed=6, bias_shift=-0.01)
+    layer = FFNRelu2 if relu2 else FFNRelu
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    kw = {("storage_dtype" if relu2 else "dtype"): dt}
+    bb = b1.detach().clone().requires_grad_()
+    y = layer.apply(x, W1, W2, bb, b2, **kw)
+    y.backward(gy)
+    bt = b1.detach().clone().requires_grad_()
+    yt = _twin_ffn(x, W1, W2, bt, b2, relu2, fp8)
+    yt.backward(gy)
+    assert bb.grad is not None
+    assert torch.equal(bb.grad, bt.grad)
+    B.check_status()
