@@ -2,7 +2,7 @@
 
 The reference (Maxzhu123/bitsparse, a Python + Triton package) runs on the CPU
 under the Triton interpreter.  This script imports it from a checkout given by
-``--reference`` (default ``/root/reference``), applies three harness shims that
+``--reference`` (the path of the reference checkout, required), applies three harness shims that
 leave the reference's code untouched, runs every operator of the compression
 path on seeded inputs and writes the results as ``golden.npz`` beside this
 file.  It only runs where the reference checkout exists; the fixtures it writes
@@ -30,7 +30,7 @@ Cases written (key prefixes):
 * ``a/<dtype>/<pack>/`` -- eight tensors compressed into one shared
   TensorBuffer (experiments/validate.py:128-139): whole arena bytes, each
   tensor's vals_offset and the final offset;
-* ``c1/``: ``x = randn(1024, 3072)`` fp32, CPU
+* ``c1/`` -- config 1: ``x = randn(1024, 3072)`` fp32, CPU
   generator seed 0, ``to_fp8(relu(x))`` then compress; SHA-256 digests of
   every output, the fp8 scale, and the bf16-cast variant;
 * ``ffn/`` -- FFNRelu fwd+bwd at a small bf16 shape (outputs and grads).
@@ -137,7 +137,7 @@ def packed_payload(vals_u8, start_value, nnz, bits):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--out", default=str(HERE / "golden.npz"))
     args = ap.parse_args()
     _setup(args.reference)

@@ -95,7 +95,7 @@ def test_golden_shared_arena(golden):
 
 
 def test_config1_fp8_and_bf16(golden):
-    """x ~ N(0,1) [1024, 3072] fp32 seed 0, to_fp8(relu(x))."""
+    """Config 1: x ~ N(0,1) [1024, 3072] fp32 seed 0, to_fp8(relu(x))."""
     g = torch.Generator().manual_seed(0)
     x = torch.randn(1024, 3072, generator=g, dtype=torch.float32)
     assert digest(x.numpy()) == str(golden["c1/x_sha"])
