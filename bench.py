@@ -520,6 +520,7 @@ def run_ours(args):
         line["sweep"] = sweep
         del xs, bufs, outs
         torch.cuda.empty_cache()
+    if rank == 0 and not args.no_extras and not args.sweep_only:
         line["mlp"] = mlp_suite(dev)
         if world == 1:
             gbs, dt, cores = cpu_baseline(2048, 1, 1)
@@ -613,6 +614,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the sweep, MLP and CPU-baseline extras")
+    ap.add_argument("--sweep-only", action="store_true",
+                    help="of the extras run only the sparsity / structure sweep")
     ap.add_argument("--mlp-only", action="store_true",
                     help="run only the sparse-MLP fwd+bwd comparison (configs 2 and 4)")
     ap.add_argument("--gemm-case", action="store_true",

@@ -501,6 +501,51 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
 }
 
 
+// Sparse chunk of the persistent reconstruct: the chunk's values (ranks r,
+// r + 1, ... in the stage) scattered by their set bits into this thread's
+// zeroed 32-byte row of `scratch` and written out with one 32-byte store
+// (element stores at the right edge).  `trips`: the largest count of any
+// lane of the warp (the loop runs in step across the warp).
+template <int SDT, bool PACK>
+__device__ __forceinline__ void scatter_chunk(const uint8_t *stg, uint32_t first, uint32_t r,
+                                           uint32_t mm, uint32_t trips, uint8_t *scratch,
+                                           uint8_t *dst, bool vec, int valid) {
+  constexpr int SB = Elt<SDT>::bytes;
+  constexpr int VEC = 32 / SB;
+  const int tid = threadIdx.x;
+  // the row's two 16-byte halves lie 512 bytes apart inside the warp's
+  // kilobyte, so the zeroing stores and read-back loads of a warp touch
+  // consecutive 16-byte words (no bank conflicts)
+  uint8_t *h0 = scratch + (tid >> 5) * 1024 + (tid & 31) * 16;
+  uint4 *q0 = reinterpret_cast<uint4 *>(h0), *q1 = reinterpret_cast<uint4 *>(h0 + 512);
+  *q0 = make_uint4(0, 0, 0, 0);
+  *q1 = make_uint4(0, 0, 0, 0);
+  uint32_t left = mm;
+  for (uint32_t k = 0; k < trips; ++k) {
+    if (left) {
+      const int e = __ffs(left) - 1;
+      left &= left - 1;
+      const uint32_t v = staged_value<SDT, PACK>(stg, first, r++);
+      const int byte = e * SB;
+      uint8_t *d = h0 + byte + (byte >= 16 ? 512 - 16 : 0);
+      if constexpr (SB == 1) *d = (uint8_t)v;
+      else *reinterpret_cast<uint16_t *>(d) = (uint16_t)v;
+    }
+  }
+  const uint4 lo = *q0, hi = *q1;
+  const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  if (vec) {
+    st_v8(dst, w);
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {  // static indices keep w[] in registers
+      if (e >= valid) break;
+      if constexpr (SB == 1) dst[e] = (w[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+      else reinterpret_cast<uint16_t *>(dst)[e] = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+    }
+  }
+}
+
 // Plain reconstruct (OUT 0), persistent and double-buffered.  CTA b takes
 // tile pairs b, b + G, ...; while it expands one pair, the bulk-copy engine
 // already brings the next pair's bitmask (1 KB) and value segment into the
@@ -524,6 +569,7 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
   __shared__ uint32_t s_wt[G::S * 8];
   __shared__ uint32_t s_first[2];
   __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(16) uint8_t scratch[kThreads * 32];  // a 32-byte row per thread
   const int tid = threadIdx.x;
   const int64_t npairs = (P.ntiles + kUT - 1) / kUT;
   const int64_t G_ = gridDim.x;
@@ -603,8 +649,35 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
       cnt[s] = __popc(m[s]);
     }
     block_excl_scan<G::S>(cnt, ex, s_wt);
+    // Warp-uniform choice per slot: when no chunk of the warp holds more
+    // than a quarter of its elements, each lane scatters only its chunk's
+    // values into its own zeroed 32-byte row of shared scratch (a loop over
+    // the set bits, as many trips as the fullest lane of the warp needs) and
+    // writes the row out with one 32-byte store -- the cost follows the number
+    // of values, not of elements.  Otherwise every element reads the value at
+    // its rank (branch-free).
+    uint32_t most = 0;
+#pragma unroll
+    for (int s = 0; s < G::S; ++s) most = max(most, __reduce_max_sync(0xFFFFFFFFu, cnt[s]));
     const uint8_t *stg = stage[buf];
     const uint32_t first = s_first[buf];
+    if (most <= (uint32_t)(G::VEC / 4)) {
+#pragma unroll
+      for (int s = 0; s < G::S; ++s) {
+        const int c = s * kThreads + tid;
+        const int j = c / G::CPT, cc = c % G::CPT;
+        if (j >= nt) continue;
+        const int row = cc / G::CPR, colc = cc % G::CPR;
+        int64_t tr, tc;
+        pp.pos(j, tr, tc);
+        const int64_t grow = tr * kTileM + row;
+        const int64_t gcol = tc * kTileN + colc * G::VEC;
+        if (grow >= P.batch_rows) continue;
+        scatter_chunk<SDT, PACK>(stg, first, ex[s], m[s], most, scratch,
+                                 P.out + (grow * P.out_ld + gcol) * SB,
+                                 P.out_v32 && gcol + G::VEC <= P.K, (int)(P.K - gcol));
+      }
+    } else {
 #pragma unroll
     for (int s = 0; s < G::S; ++s) {
       const int c = s * kThreads + tid;
@@ -616,9 +689,10 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
       const int64_t grow = tr * kTileM + row;
       const int64_t gcol = tc * kTileN + colc * G::VEC;
       if (grow >= P.batch_rows) continue;
-      uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      uint8_t *dst = P.out + (grow * P.out_ld + gcol) * SB;
       const uint32_t mm = m[s];
       uint32_t r = ex[s];
+      uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
       for (int e = 0; e < G::VEC; ++e) {
         uint32_t v;
@@ -635,7 +709,6 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
         if constexpr (SB == 1) w[e >> 2] |= v << (8 * (e & 3));
         else w[e >> 1] |= v << (16 * (e & 1));
       }
-      uint8_t *dst = P.out + (grow * P.out_ld + gcol) * SB;
       if (P.out_v32 && gcol + G::VEC <= P.K) {
         st_v8(dst, w);
       } else {
@@ -645,6 +718,7 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
           else reinterpret_cast<uint16_t *>(dst)[e] = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
         }
       }
+    }
     }
     fence_proxy_async_smem();  // this pair's buffer reads precede its next bulk copies
     __syncthreads();
