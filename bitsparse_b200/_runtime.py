@@ -2,7 +2,9 @@
 
 All device memory is owned by PyTorch's caching allocator.  Per device the
 library keeps one int32 status word (device errors OR-ed in by kernels) and,
-per (device, stream), a self-resetting scan workspace for bs_compress.
+per (device, stream), a scan workspace for bs_compress (zeroed when it is
+allocated and after a bounded wait gave up; consistent between launches
+otherwise).
 """
 from __future__ import annotations
 
@@ -80,6 +82,9 @@ def workspace(device: torch.device, num_tiles: int, stream: int | None = None) -
     need = _ws_bytes.get(num_tiles)
     if need is None:
         need = _ws_bytes[num_tiles] = int(_lib.load().bs_compress_workspace_bytes(int(num_tiles)))
+    ws = _workspaces.get(key)
+    if ws is not None and ws.numel() >= need:  # the common case: no lock
+        return ws
     with _lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < need:

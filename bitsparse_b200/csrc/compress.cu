@@ -54,11 +54,17 @@
 
 namespace bs {
 
-// Workspace: header {off0}, uint64 segment totals (zeroed by a memset before
-// the count kernel), uint32 per-partition counts.
+// Workspace: header {off0, epoch}, uint64 segment totals (zeroed by a memset
+// before the count kernel), per-partition counts (uint32 in the two-kernel
+// form, cleared after it; epoch-tagged uint64 in the one-pass form).
 struct WsHeader {
   long long off0;  // logical index of this tensor's first value
-  unsigned long long pad[15];
+  // one-pass kernel: epoch of the last launch that completed on this
+  // workspace (0 in a zeroed workspace); a launch publishes its partition
+  // counts tagged with epoch + 1, so the counts of earlier launches read as
+  // "not yet published" and the workspace needs no clearing between launches
+  unsigned long long epoch;
+  unsigned long long pad[14];
 };
 constexpr int kSeg = 256;  // partitions per segment
 
@@ -627,6 +633,15 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
 __device__ __forceinline__ void st_relaxed_u32(uint32_t *p, uint32_t v) {
   asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// A partition count of the one-pass kernel as published for launch epoch
+// `ep`: (ep << 32) | (count + 1).  Returns count + 1, or 0 when the word
+// holds no count of this launch yet.
+__device__ __forceinline__ uint32_t count_of(unsigned long long w, uint32_t ep) {
+  return (uint32_t)(w >> 32) == ep ? (uint32_t)w : 0u;
+}
 
 // Shared-memory plan of the one-pass kernel.
 template <int DT_IN, bool QUANT, int TPP_, int NW, int D, int A>
@@ -763,6 +778,8 @@ __global__ void __launch_bounds__(NW * 32, MINB)
   uint32_t *s_meta = reinterpret_cast<uint32_t *>(smem_dyn + O::OFF_META);
   __shared__ uint32_t s_sum[2];  // per round parity: sum of the flush's counts
   __shared__ long long s_off0;
+  __shared__ uint32_t s_epoch;
+  unsigned long long *cnt64 = reinterpret_cast<unsigned long long *>(P.counts_ws);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long G = gridDim.x, b = blockIdx.x, nparts = P.num_parts;
 
@@ -792,7 +809,9 @@ __global__ void __launch_bounds__(NW * 32, MINB)
     s_off0 = off;
     s_sum[0] = 0;
     s_sum[1] = 0;
-    __threadfence();  // the arena-offset read precedes every count this CTA publishes
+    uint32_t ep = (uint32_t)*reinterpret_cast<volatile unsigned long long *>(&P.hdr->epoch) + 1u;
+    s_epoch = ep ? ep : 1u;
+    __threadfence();  // the arena-offset / epoch reads precede every count this CTA publishes
   }
   __syncthreads();
   if (tid == 0)
@@ -803,6 +822,7 @@ __global__ void __launch_bounds__(NW * 32, MINB)
   const float qr = QUANT ? __frcp_rn(qs) : 1.f;
   const float qs2 = (QUANT && BIAS && P.qscale2 != nullptr) ? *P.qscale2 : 1.f;
   const float qr2 = __frcp_rn(qs2);
+  const uint32_t epoch = s_epoch;
   long long known_end = 0, known = -1;  // end (count) through this CTA's last flushed partition
   for (long long r = 0;; ++r) {
     const long long p = r * G + b;
@@ -820,7 +840,7 @@ __global__ void __launch_bounds__(NW * 32, MINB)
 #pragma unroll
     for (int i = 0; i < kCv; ++i) {
       const long long ci = known + 1 + tid + (long long)i * NW * 32;
-      cv[i] = (q >= 0 && ci < q) ? ld_relaxed_u32(P.counts_ws + ci) : 1u;
+      cv[i] = (q >= 0 && ci < q) ? count_of(ld_relaxed_u64(cnt64 + ci), epoch) : 1u;
     }
     // 3. compact partition p in place
     if (p < nparts) {
@@ -984,7 +1004,7 @@ __global__ void __launch_bounds__(NW * 32, MINB)
           meta[NW + t] = acc;  // inclusive count after tile t
         }
         meta[NW + TPP] = acc;
-        st_relaxed_u32(P.counts_ws + p, acc + 1);
+        st_relaxed_u64(cnt64 + p, ((unsigned long long)epoch << 32) | (acc + 1));
       }
       if (valid && P.vals != nullptr) {
         const uint32_t t = lane < warp ? meta[lane] : 0u;
@@ -1014,7 +1034,7 @@ __global__ void __launch_bounds__(NW * 32, MINB)
         for (uint32_t n = 0; cv[i] == 0; ++n) {  // published yet?  (0 only for ci < q)
           if (n >= kMaxPolls) { late = true; cv[i] = 1; break; }
           __nanosleep(64);
-          cv[i] = ld_relaxed_u32(P.counts_ws + ci);
+          cv[i] = count_of(ld_relaxed_u64(cnt64 + ci), epoch);
         }
         sum += cv[i] - 1;
       }
@@ -1035,6 +1055,8 @@ __global__ void __launch_bounds__(NW * 32, MINB)
           if (P.arena_offset) *P.arena_offset = off0 + nnz;
           if (P.vals_offset_out) *P.vals_offset_out = off0;
           if (P.nnz_out) *P.nnz_out = nnz;
+          // every CTA has read the epoch: this flush needed a count from each
+          *reinterpret_cast<volatile unsigned long long *>(&P.hdr->epoch) = epoch;
         }
       }
       if (P.vals != nullptr) {
@@ -1158,9 +1180,10 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
   if (resident > O::CV * NW * 32 + 1) resident = O::CV * NW * 32 + 1;
   CompressParams Q = P;
   Q.num_parts = (P.num_tiles + O::TPP - 1) / O::TPP;
-  if (cudaMemsetAsync(Q.counts_ws, 0, (size_t)Q.num_parts * sizeof(uint32_t), st) !=
-      cudaSuccess)
-    return BS_ERR_LAUNCH;
+  // counts are published as 64-bit epoch-tagged words (no clearing needed);
+  // a partition holds at least four tiles, so they fit in the 2 bytes per
+  // tile that bs_compress_workspace_bytes provides
+  static_assert(O::TPP >= 4, "8-byte counts need at least four tiles per partition");
   // Every CTA waits on counts that others publish: all must be resident,
   // which a cooperative launch guarantees (or refuses).
   cudaLaunchConfig_t cfg = {};
@@ -1195,6 +1218,12 @@ static int launch_t(const CompressParams &P, cudaStream_t st) {
     count_kernel<DT_IN, QUANT, PACK, TPP><<<grid, kThreads, 0, st>>>(P);
     if (cudaGetLastError() != cudaSuccess) return BS_ERR_LAUNCH;
     compact_kernel<DT_IN, QUANT, PACK, TPP><<<grid, kThreads, smem, st>>>(P);
+    if (cudaGetLastError() != cudaSuccess) return BS_ERR_LAUNCH;
+    // leave the counts zero: the one-pass kernel reads these words as
+    // epoch-tagged 64-bit counts, and plain counts must not look like one
+    if (cudaMemsetAsync(P.counts_ws, 0, (size_t)P.num_parts * sizeof(uint32_t), st) !=
+        cudaSuccess)
+      return BS_ERR_LAUNCH;
   } else {
     compress_kernel<DT_IN, QUANT, PACK, TPP, MODE><<<grid, kThreads, smem, st>>>(P);
   }

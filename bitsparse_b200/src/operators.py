@@ -286,19 +286,18 @@ def matmul_relu_mask(a: Tensor, b: Tensor, sparse: BitsparseTensor | None = None
     return out
 
 
-def _fused_compress(fn, head: tuple, tail: tuple, dev, stored, M: int, N: int, T: int,
-                    bitmask: Tensor, prefix: Tensor, sparse_data, pack_sbit: bool):
+def _fused_compress(fn, name: str, head: tuple, dev, stream: int, stored, M: int, N: int,
+                    T: int, bitmask: Tensor, prefix: Tensor, sparse_data, pack_sbit: bool):
     """Run a fused compress entry point ``fn(*head, bitmask, prefix, vals,
     capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out, workspace,
-    workspace_bytes, status, stream)`` in either storage mode.  Returns
-    (vals, vals_offset), or None when the entry point reports BS_ERR_ALIGN
-    (the one-pass kernel cannot read the tensors)."""
-    bits = bits_per_value(stored)
-    st = _stream(head[0]) if isinstance(head[0], Tensor) else R.stream_handle(dev)
-    ws = R.workspace(dev, T, st)
+    workspace_bytes, status, stream)`` (``head``: its leading arguments,
+    already plain ints) in either storage mode.  Returns (vals, vals_offset),
+    or None when the entry point reports BS_ERR_ALIGN (the one-pass kernel
+    cannot read the tensors)."""
+    ws = R.workspace(dev, T, stream)
     status = R.status_word(dev)
-    head = tuple(h.data_ptr() if isinstance(h, Tensor) else h for h in head)
     if sparse_data is None:
+        bits = bits_per_value(stored)
         if pack_sbit:
             tmp = torch.empty(packed_storage_nbytes(M * N, bits), device=dev, dtype=torch.uint8)
         else:
@@ -306,10 +305,10 @@ def _fused_compress(fn, head: tuple, tail: tuple, dev, stored, M: int, N: int, T
         nnz_t = torch.empty((), device=dev, dtype=torch.int64)
         rc = fn(*head, bitmask.data_ptr(), prefix.data_ptr(), tmp.data_ptr(), tmp.numel(),
                 int(pack_sbit), None, None, nnz_t.data_ptr(), ws.data_ptr(), ws.numel(),
-                status.data_ptr(), st)
+                status.data_ptr(), stream)
         if rc == _lib.BS_ERR_ALIGN:
             return None
-        _lib.check(rc, fn.__name__)
+        _lib.check(rc, name)
         nnz = int(nnz_t.item())  # host sync (triton_operators.py:50)
         size = packed_storage_nbytes(nnz, bits) if pack_sbit else nnz
         return tmp[:size].clone(), torch.zeros((), device=dev, dtype=torch.int64)
@@ -321,10 +320,10 @@ def _fused_compress(fn, head: tuple, tail: tuple, dev, stored, M: int, N: int, T
     vals_offset = torch.empty(1, device=dev, dtype=torch.int64)
     rc = fn(*head, bitmask.data_ptr(), prefix.data_ptr(), vals.data_ptr(), vals.numel(),
             int(pack_sbit), sparse_data.offset.data_ptr(), vals_offset.data_ptr(), None,
-            ws.data_ptr(), ws.numel(), status.data_ptr(), st)
+            ws.data_ptr(), ws.numel(), status.data_ptr(), stream)
     if rc == _lib.BS_ERR_ALIGN:
         return None
-    _lib.check(rc, fn.__name__)
+    _lib.check(rc, name)
     return vals, vals_offset
 
 
@@ -339,20 +338,30 @@ def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: boo
     """
     if z.dtype != torch.bfloat16 or bias.dtype != torch.bfloat16:
         return None
-    z, ld = _row_major(z, "z")
+    if not z.is_cuda:
+        R.require_cuda(z, "z")
+    if z.dim() != 2:
+        raise ValueError("z must be 2-D")
     M, N = z.shape
-    bias = bias.contiguous()
+    if z.stride(1) != 1 or z.stride(0) < N:
+        z = z.contiguous()
+    ld = max(z.stride(0), N)
+    if not bias.is_contiguous():
+        bias = bias.contiguous()
     if bias.numel() != N:
         raise ValueError(f"bias has {bias.numel()} elements, z has {N} columns")
-    grid_m, grid_n, T, _, TB = tile_grid(M, N, _BM, _BN)
+    grid_m, grid_n = (M + _BM - 1) // _BM, (N + _BN - 1) // _BN
+    T = grid_m * grid_n
     if T == 0:
         return None
     dev = z.device
     h = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
-    bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
+    bitmask = torch.empty(T * (_BM * _BN // 8), device=dev, dtype=torch.uint8)
     prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
-    out = _fused_compress(_lib.load().bs_compress_bias_relu, (z, M, N, ld, bias, h, N), (),
-                          dev, torch.bfloat16, M, N, T, bitmask, prefix, sparse_data, pack_sbit)
+    st = R.stream_handle(dev)
+    out = _fused_compress(_lib.load().bs_compress_bias_relu, "bs_compress_bias_relu",
+                          (z.data_ptr(), M, N, ld, bias.data_ptr(), h.data_ptr(), N), dev, st,
+                          torch.bfloat16, M, N, T, bitmask, prefix, sparse_data, pack_sbit)
     if out is None:
         return None
     vals, vals_offset = out
@@ -395,8 +404,9 @@ def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit:
     side = torch.empty((M, N), device=dev, dtype=torch.float8_e4m3fn)
     bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
     prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
-    out = _fused_compress(lib.bs_compress_bias_relu_fp8,
-                          (z, M, N, ld, bias, scale_h, scale_s, side), (), dev,
+    out = _fused_compress(lib.bs_compress_bias_relu_fp8, "bs_compress_bias_relu_fp8",
+                          (z.data_ptr(), M, N, ld, bias.data_ptr(), scale_h.data_ptr(),
+                           R.ptr(scale_s), side.data_ptr()), dev, st,
                           torch.float8_e4m3fn, M, N, T, bitmask, prefix, sparse_data, pack_sbit)
     if out is None:
         return None

@@ -72,10 +72,13 @@ enum {
 const char *bs_version(void);
 
 /* Bytes of workspace bs_compress needs for `num_tiles` tiles (per-partition
- * counts and running totals, about 2 bytes per tile; no initial contents are
- * required).  Launches
- * that may overlap on the GPU (different streams) must use different
- * workspaces. */
+ * counts and running totals, about 2 bytes per tile).  Zero the workspace
+ * once before its first use (and again after a launch that reported
+ * BS_STATUS_TIMEOUT); the library keeps it consistent between launches, so
+ * no clearing is queued per call -- the counts of each launch carry an epoch
+ * kept in the workspace, which also makes the calls safe to capture in a
+ * CUDA graph.  Launches that may overlap on the GPU (different streams) must
+ * use different workspaces. */
 size_t bs_compress_workspace_bytes(int64_t num_tiles);
 
 /* Fused compress: dense [M, N] (row stride `ld` elements) -> bitmask

@@ -258,6 +258,50 @@ def test_workspace_reuse_many_launches():
     B.check_status()
 
 
+def test_workspace_epochs_across_paths_and_graph_replays():
+    """The one-pass kernel tags its published counts with an epoch kept in
+    the workspace instead of clearing the workspace per call: one-pass
+    launches interleaved with two-kernel launches (an input whose row stride
+    TMA cannot read) on the same workspace, then a CUDA graph replayed on
+    changing inputs, all reconstruct exactly."""
+    g = torch.Generator().manual_seed(21)
+    for i in range(6):
+        M, N = 1024 + 64 * i, 2048
+        d = torch.randn(M, N, generator=g).relu().to(torch.bfloat16).cuda()
+        if i % 2:  # row stride of N + 3 elements: not 16-byte aligned -> two kernels
+            wide = torch.zeros(M, N + 3, dtype=torch.bfloat16, device="cuda")
+            wide[:, :N] = d
+            d = wide[:, :N]
+        sp = dense_to_tilesparse(d, None)
+        assert int(sp.prefix[-1].item()) == int((d > 0).sum().item())
+        torch.testing.assert_close(_reconstruct(sp), d.contiguous(), rtol=0, atol=0)
+    M, N = 2048, 4096
+    x = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    buf = TensorBuffer(M * N * 2, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(x)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+
+    def body():
+        buf.offset.zero_()
+        sp = dense_to_tilesparse(x, None, buf)
+        unpack_batch_(sp, out, 0, sp.grid_n, N, M, sp.grid_m * sp.grid_n)
+
+    with torch.cuda.stream(s):
+        x.copy_(torch.randn(M, N, generator=g).relu().to(torch.bfloat16))
+        body()  # warm up (workspace of this stream allocated outside capture)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        body()
+    for i in range(5):
+        x.copy_((torch.randn(M, N, generator=g) - 0.3 * i).relu().to(torch.bfloat16))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, x), i
+    B.check_status()
+
+
 def test_deterministic():
     d = torch.randn(3000, 4000, generator=torch.Generator().manual_seed(4)).relu()
     d = d.to(torch.bfloat16).cuda()
