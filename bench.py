@@ -245,6 +245,48 @@ def time_round_trips(xs, bufs, outs, steps, sps=None):
     return sps, ev
 
 
+class _DenseReluLinearFP8:
+    """The FP8 ReLU / ReLU^2 FFN half of the reference (lib_sparse/layers.py:
+    20-66, 100-151) with the activation kept DENSE: the same FP8 GEMM calls
+    (``bitsparse_b200.fp8.matmul``), the saved activation ``to_fp8(h)`` as a
+    dense e4m3 tensor.  The config-4 baseline that differs from the
+    compressed FFN only in how the activation is stored."""
+
+    @staticmethod
+    def make():
+        import torch
+        from bitsparse_b200.fp8 import matmul, to_fp8
+
+        class F(torch.autograd.Function):
+            @staticmethod
+            def forward(ctx, z, W, relu2):
+                ctx.relu2 = relu2
+                ctx.save_for_backward(W)
+                h = z.relu_()
+                h_st, scale = to_fp8(h)
+                ctx.h_st, ctx.scale = h_st, scale
+                if relu2:
+                    return matmul(h.square_(), W.T, True)
+                return matmul(h_st, W.T, True, a_scale=scale)
+
+            @staticmethod
+            def backward(ctx, go):
+                W = ctx.saved_tensors[0]
+                h, scale = ctx.h_st, ctx.scale
+                go8, gscale = to_fp8(go.contiguous())
+                r = h.float() * scale
+                if ctx.relu2:
+                    gW = matmul(go8.T, (r * r).to(torch.bfloat16), True, a_scale=gscale)
+                    gh = matmul(go8, W, True, a_scale=gscale)
+                    gz = (gh.float() * (2.0 * r)).to(torch.bfloat16)
+                else:
+                    gW = matmul(go8.T, h, True, a_scale=gscale, b_scale=scale)
+                    gz = matmul(go8, W, True, a_scale=gscale) * (r > 0)
+                return gz, gW, None
+
+        return F
+
+
 def mlp_bench(cfg, steps, warmup, device):
     """Sparse FFN fwd+bwd tokens/s vs a dense-activation torch FFN."""
     import torch
@@ -282,6 +324,16 @@ def mlp_bench(cfg, steps, warmup, device):
         y = h @ params[2].T + params[4]
         y.backward(gy)
 
+    fp8 = storage != torch.bfloat16
+    if fp8:
+        from bitsparse_b200.fp8 import matmul as mm8
+        DenseFP8 = _DenseReluLinearFP8.make()
+
+    def dense_fp8_step():
+        z = mm8(params[0], params[1].T, True) + params[3]
+        y = DenseFP8.apply(z, params[2], relu2) + params[4]
+        y.backward(gy)
+
     def graphed(fn):
         """fn captured once in a CUDA graph (launch overhead removed)."""
         s = torch.cuda.Stream()
@@ -296,10 +348,13 @@ def mlp_bench(cfg, steps, warmup, device):
         return g.replay
 
     out = {}
-    for name, fn in (("sparse", sparse_step), ("sparse_arena", lambda: sparse_step(arena)),
-                     ("dense", dense_step),
-                     ("sparse_arena_graph", graphed(lambda: sparse_step(arena))),
-                     ("dense_graph", graphed(dense_step))):
+    arms = [("sparse", sparse_step), ("sparse_arena", lambda: sparse_step(arena)),
+            ("dense", dense_step),
+            ("sparse_arena_graph", graphed(lambda: sparse_step(arena))),
+            ("dense_graph", graphed(dense_step))]
+    if fp8:
+        arms.append(("dense_fp8", dense_fp8_step))
+    for name, fn in arms:
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
@@ -322,6 +377,11 @@ def mlp_bench(cfg, steps, warmup, device):
                                      / out["dense"]["tokens_per_s"])
     out["speedup_graph_vs_dense_graph"] = (out["sparse_arena_graph"]["tokens_per_s"]
                                            / out["dense_graph"]["tokens_per_s"])
+    if fp8:  # like for like: the same FP8 GEMMs, only the activation storage differs
+        out["speedup_vs_dense_fp8"] = (out["sparse"]["tokens_per_s"]
+                                       / out["dense_fp8"]["tokens_per_s"])
+        out["speedup_arena_vs_dense_fp8"] = (out["sparse_arena"]["tokens_per_s"]
+                                             / out["dense_fp8"]["tokens_per_s"])
     return out
 
 
@@ -492,10 +552,22 @@ def run_ours(args):
     line["e2e"] = {"value": e_bytes * world / (e_ms.item() * 1e-3) / 1e9, "unit": "GB/s",
                    "h2d_bytes_per_step": M * N * 2, "d2h_bytes_per_step": M * N * 2,
                    "ms_per_step": e_ms.item() / ksteps}
-    del hx, hout, dx
 
-    # ---- extras on rank 0: sweep, MLP, CPU baseline -------------------------
-    if rank == 0 and not args.no_extras:
+    del hx, hout, dx
+    torch.cuda.empty_cache()
+
+    # ---- multi-GPU sections (every rank) -----------------------------------
+    if not args.no_extras and not args.sweep_only and not args.no_train:
+        del xs, bufs, outs, sps
+        torch.cuda.empty_cache()
+        line["train"] = train_suite(dev, world, rank)
+        xs = [make_relu_bf16(M, N, 0.0, 1000 * rank + i, dev) for i in range(2)]
+        bufs = [TensorBuffer(M * N * 2, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+        outs = [torch.empty_like(x) for x in xs]
+
+    # ---- extras on rank 0 at N = 1: sweep, MLP, CPU baseline ----------------
+    # (per-GPU measurements; at N > 1 the other ranks would only wait)
+    if rank == 0 and world == 1 and not args.no_extras:
         sweep = {}
         for variant in ("A", "B", "C"):
             for target, mu in ((0.5, 0.0), (0.7, -0.5244), (0.9, -1.2816), (0.95, -1.6449),
@@ -520,7 +592,7 @@ def run_ours(args):
         line["sweep"] = sweep
         del xs, bufs, outs
         torch.cuda.empty_cache()
-    if rank == 0 and not args.no_extras and not args.sweep_only:
+    if rank == 0 and world == 1 and not args.no_extras and not args.sweep_only:
         line["mlp"] = mlp_suite(dev)
         if world == 1:
             gbs, dt, cores = cpu_baseline(2048, 1, 1)
@@ -533,6 +605,146 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def _max_over_ranks(v: float, world: int, dev) -> float:
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return v
+    t = torch.tensor([v], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def dp_train(dev, world, rank, compressed, steps=4, warmup=2):
+    """Config 5: one data-parallel training step (forward, backward with the
+    gradients summed over the ranks by NCCL all-reduce overlapped with the
+    backward pass, AdamW) of the 24-layer d1024 decoder on a global batch of
+    64 x 1024 synthetic tokens (64 / world sequences per rank: strong
+    scaling).  Returns tokens/s (device time, max over ranks) and the peak
+    memory the forward pass adds on top of parameters, gradients and
+    optimizer state (the saved activations, logits included)."""
+    import torch
+    import torch.distributed as dist
+    from bitsparse_b200.decoder import Decoder, DecoderConfig
+    from bitsparse_b200.distributed import GradAllReduce
+
+    cfg = DecoderConfig(compressed=compressed)
+    torch.manual_seed(0)  # the same initial weights on every rank
+    model = Decoder(cfg).to(device=dev, dtype=torch.bfloat16)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-5, fused=True)
+    red = GradAllReduce(model.parameters()) if world > 1 else None
+    B = max(1, 64 // world)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    tok = torch.randint(0, cfg.vocab, (B, cfg.seq + 1), generator=g, device=dev)
+    x, y = tok[:, :-1], tok[:, 1:]
+
+    def step():
+        loss = model(x, y)
+        loss.backward()
+        if red is not None:
+            red.wait()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated(dev)
+    torch.cuda.reset_peak_memory_stats(dev)
+    loss = model(x, y)
+    torch.cuda.synchronize()
+    fwd_peak = torch.cuda.max_memory_allocated(dev) - base
+    loss.backward()
+    if red is not None:
+        red.wait()
+    opt.step()
+    opt.zero_grad(set_to_none=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        last = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+    out = {"tokens_per_s": B * world * cfg.seq / ms * 1e3, "ms_per_step": ms,
+           "local_batch": B, "peak_forward_mem_mb": fwd_peak / 2**20,
+           "loss_per_token": float(last.item()) / (B * cfg.seq)}
+    if red is not None:
+        red.remove()
+    del model, opt, red
+    torch.cuda.empty_cache()
+    return out
+
+
+def c4_sharded(dev, world, rank, steps=5, warmup=2, bias_sigma=0.0):
+    """Config 4 token-sharded: the 16384 tokens split over the ranks, each
+    rank runs the compressed ReLU^2 FFN (e4m3 storage) forward and backward
+    on its tokens and the weight / bias gradients are summed over the ranks
+    (GradAllReduce, overlapped with the backward pass)."""
+    import torch
+    import torch.distributed as dist
+    from bitsparse_b200.distributed import GradAllReduce
+    from bitsparse_b200.layers import FFNRelu2
+
+    d, H = 4096, 16384
+    T = 16384 // world
+    gw = torch.Generator(device=dev).manual_seed(123)  # shared weights
+    W1 = (0.02 * torch.randn(H, d, generator=gw, device=dev)).to(torch.bfloat16)
+    W2 = (0.02 * torch.randn(d, H, generator=gw, device=dev)).to(torch.bfloat16)
+    gx = torch.Generator(device=dev).manual_seed(500 + rank)
+    x = torch.randn(T, d, generator=gx, device=dev).to(torch.bfloat16)
+    gy = torch.randn(T, d, generator=gx, device=dev).to(torch.bfloat16)
+    with torch.no_grad():
+        z = (x @ W1.T).float()
+        b1 = (-bias_sigma * z.std()).to(torch.bfloat16).expand(H).contiguous()
+        del z
+    b2 = torch.zeros(d, device=dev, dtype=torch.bfloat16)
+    params = [t.requires_grad_() for t in (x, W1, W2, b1, b2)]
+    red = GradAllReduce(params[1:]) if world > 1 else None
+
+    def step():
+        y = FFNRelu2.apply(*params, storage_dtype=torch.float8_e4m3fn)
+        y.backward(gy)
+        if red is not None:
+            red.wait()
+        for p in params:
+            p.grad = None
+
+    for _ in range(warmup):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+    out = {"tokens_per_s": 16384 / ms * 1e3, "ms_per_step": ms, "tokens_per_rank": T}
+    if red is not None:
+        red.remove()
+    return out
+
+
+def train_suite(dev, world, rank):
+    """Multi-GPU sections, run by every rank: config 5 (DP decoder step,
+    compressed vs dense MLP activations) and config 4 token-sharded."""
+    out = {"scaling": "strong (global batch fixed)", "world": world}
+    out["config5_dp_decoder_compressed"] = dp_train(dev, world, rank, True)
+    out["config5_dp_decoder_dense"] = dp_train(dev, world, rank, False)
+    c, dn = out["config5_dp_decoder_compressed"], out["config5_dp_decoder_dense"]
+    out["config5_speedup_vs_dense"] = c["tokens_per_s"] / dn["tokens_per_s"]
+    out["config5_activation_mem_ratio"] = c["peak_forward_mem_mb"] / dn["peak_forward_mem_mb"]
+    out["config4_token_sharded_relu2_fp8"] = c4_sharded(dev, world, rank)
+    return out
 
 
 def mlp_suite(dev):
@@ -552,6 +764,9 @@ def mlp_suite(dev):
             "config4_nemotron_relu2_fp8": mlp_bench(
                 {"tokens": 16384, "d": 4096, "H": 16384, "relu2": True,
                  "storage": torch.float8_e4m3fn, "bias_sigma": 0.0}, 5, 2, dev),
+            "config4_nemotron_relu2_fp8_90pct_sparse": mlp_bench(
+                {"tokens": 16384, "d": 4096, "H": 16384, "relu2": True,
+                 "storage": torch.float8_e4m3fn, "bias_sigma": 1.2816}, 5, 2, dev),
     }
 
 
@@ -614,6 +829,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the sweep, MLP and CPU-baseline extras")
+    ap.add_argument("--no-train", action="store_true",
+                    help="skip the config-5 DP decoder and config-4 token-sharded sections")
+    ap.add_argument("--train-only", action="store_true",
+                    help="run only the config-5 / config-4 multi-GPU sections")
     ap.add_argument("--sweep-only", action="store_true",
                     help="of the extras run only the sparsity / structure sweep")
     ap.add_argument("--mlp-only", action="store_true",
@@ -633,6 +852,22 @@ def main():
         import torch
         dev = torch.device("cuda", 0)
         print(json.dumps(mlp_suite(dev)), flush=True)
+        return
+    if args.train_only:
+        import torch
+        import torch.distributed as dist
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dev = torch.device("cuda", local)
+        if world > 1:
+            dist.init_process_group("nccl", device_id=dev)
+        out = train_suite(dev, world, rank)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return
     if args.warmup < 3:
         args.warmup = 3

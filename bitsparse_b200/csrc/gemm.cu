@@ -55,9 +55,19 @@ struct GemmParams {
   int64_t M, N, K, ldc;
   const uint8_t *mask;  // bitmask of a bitsparse [M, N] tensor, or null
   int64_t mask_grid_n;  // its tile columns: ceil(N / 64)
+  int64_t mask_grid_m;  // its tile rows: ceil(M / 64)
   int c_tma;            // C is written by TMA stores (aligned base and row stride)
   int32_t *status;
+  // ReLU^2 epilogue: the stored activation's raw bf16 values, tile prefix
+  // and value offset, and 2k (RELU2_SCALE k)
+  const uint16_t *vals;
+  const uint32_t *prefix;
+  const int64_t *vals_offset;
+  float two_k;
 };
+
+// Epilogues: none, the ReLU mask, the ReLU^2 gradient.
+enum { kEpiNone = 0, kEpiMask = 1, kEpiRelu2 = 2 };
 
 __device__ __forceinline__ uint32_t saddr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -138,6 +148,13 @@ __device__ __forceinline__ uint32_t bf16x2_rn(uint32_t lo, uint32_t hi) {
   return r;
 }
 
+// Elementwise bf16x2 product, rounded to nearest even.
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane (no wait).
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t *r) {
   asm volatile(
@@ -173,14 +190,22 @@ __device__ __forceinline__ void tile_coords(int64_t t, int64_t mt, int64_t nt, i
 // 256 x 256 tile through tcgen05's cta_group::2, each CTA loading its 128
 // rows of A and 128 of the 256 columns of B, so a stage is 32 KB instead
 // of 48 KB and the operand bytes per flop drop by a third).
-template <int CG>
+// ReLU^2 epilogue: per epilogue warp two staging buffers, each for the
+// values of its 32 rows of one 64 x 64 tile (at most 2048 bf16, as the
+// 16-byte aligned superset); chunk c + 2's values are copied in while chunk
+// c is expanded.
+constexpr int kValStage = 2048 * 2 + 32;
+constexpr int kValBufs = 2;
+template <int CG, int EPI = kEpiNone>
 struct GemmCfg {
   static constexpr int BM = kBM * CG;           // rows of C per tile
   static constexpr int BNL = kBN / CG;          // columns of B this CTA loads
   static constexpr int BBYTES = kBK * BNL * 2;  // B bytes per stage and CTA
   static constexpr int STAGE = kABytes + BBYTES;
-  static constexpr int NST = CG == 2 ? 6 : 4;   // stages
-  static constexpr size_t SMEM = 1024 + (size_t)NST * STAGE + kEpiBytes + 256;
+  // stages (one fewer with the ReLU^2 epilogue's value staging)
+  static constexpr int NST = (CG == 2 ? 6 : 4) - (EPI == kEpiRelu2 ? 1 : 0);
+  static constexpr int VBYTES = EPI == kEpiRelu2 ? 4 * kValBufs * kValStage : 0;
+  static constexpr size_t SMEM = 1024 + (size_t)NST * STAGE + kEpiBytes + VBYTES + 256;
   // instruction descriptor: M = BM, N = kBN
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) |
                                     (1u << 16) | ((uint32_t)(kBN >> 3) << 17) |
@@ -198,24 +223,37 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
+// 16-byte global -> shared copy (cp.async, completion per thread by group).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
 }
 
-template <bool MASK, int CG>
+template <int EPI, int CG>
 __global__ void __launch_bounds__(kThreadsG, 1)
     gemm_mask_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmParams P) {
-  using G = GemmCfg<CG>;
+  using G = GemmCfg<CG, EPI>;
+  constexpr bool MASK = EPI != kEpiNone;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms (same offsets in both
   // CTAs of a pair, which the cta_group::2 descriptors rely on)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t *epi = smem + (size_t)G::NST * G::STAGE;  // staging boxes
-  uint64_t *full = reinterpret_cast<uint64_t *>(epi + kEpiBytes);
+  uint8_t *vstage = epi + kEpiBytes;                 // ReLU^2: value staging
+  uint64_t *full = reinterpret_cast<uint64_t *>(vstage + G::VBYTES);
   uint64_t *empty = full + G::NST;
   uint64_t *acc_full = empty + G::NST;  // [2]: MMA -> epilogue
   uint64_t *acc_empty = acc_full + 2;   // [2]: epilogue -> MMA
@@ -355,11 +393,60 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       uint64_t keep[kBN / 64];
 #pragma unroll
       for (int i = 0; i < kBN / 64; ++i) {
-        keep[i] = ~0ull;
+        keep[i] = EPI == kEpiRelu2 ? 0ull : ~0ull;
         if constexpr (MASK) {
-          if (m < P.M && n0 + 64 * i < P.N)
+          // ReLU^2 counts values, so every row of an existing tile is read
+          // (rows past M have clear bits there)
+          const bool in = EPI == kEpiRelu2 ? (m >> 6) < P.mask_grid_m : m < P.M;
+          if (in && n0 + 64 * i < P.N)
             keep[i] = *reinterpret_cast<const uint64_t *>(
                 P.mask + ((m >> 6) * P.mask_grid_n + (n0 >> 6) + i) * kTileBytes + (m & 63) * 8);
+        }
+      }
+      // ReLU^2: this warp's 32 rows of each of the tile's four 64 x 64 tiles
+      // of h hold one contiguous run of the value stream; its bounds depend
+      // only on the bitmask, so they are found -- and the first two runs'
+      // copies into shared memory started -- before the accumulator is ready
+      uint32_t rexcl[kBN / 64], rfirst[kBN / 64];
+      int64_t ra0[kBN / 64];
+      int rnv[kBN / 64];
+      uint8_t *vs0 = vstage + (size_t)q * kValBufs * kValStage;
+      if constexpr (EPI == kEpiRelu2) {
+#pragma unroll
+        for (int c = 0; c < kBN / 64; ++c) {
+          rexcl[c] = 0; rfirst[c] = 0; ra0[c] = 0; rnv[c] = 0;
+          const int64_t tile = (row0 >> 6) * P.mask_grid_n + (n0 >> 6) + c;
+          if ((row0 >> 6) < P.mask_grid_m && n0 + 64 * c < P.N) {  // warp-uniform
+            const uint32_t cnt = (uint32_t)__popcll(keep[c]);
+            uint32_t before = 0;
+            if (row0 & 32) {  // rows 0..31 of the tile belong to the other warp
+              const uint64_t ow =
+                  *reinterpret_cast<const uint64_t *>(P.mask + tile * kTileBytes + lane * 8);
+              before = __reduce_add_sync(0xFFFFFFFFu, (uint32_t)__popcll(ow));
+            }
+            uint32_t inc = cnt;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+              const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, d);
+              if (lane >= d) inc += t;
+            }
+            const uint32_t total = __shfl_sync(0xFFFFFFFFu, inc, 31);
+            const int64_t seg0 = (int64_t)P.prefix[tile] + *P.vals_offset + before;
+            const int64_t a0 = (seg0 * 2) & ~(int64_t)15;
+            const int64_t a1 = ((seg0 + (int64_t)total) * 2 + 15) & ~(int64_t)15;
+            rexcl[c] = inc - cnt;
+            rfirst[c] = (uint32_t)((seg0 * 2 - a0) >> 1);
+            ra0[c] = a0;
+            rnv[c] = (int)((a1 - a0) >> 4);
+          }
+        }
+        __syncwarp();  // the previous tile's reads of both buffers are done
+#pragma unroll
+        for (int c = 0; c < kValBufs; ++c) {
+          const uint8_t *src = reinterpret_cast<const uint8_t *>(P.vals) + ra0[c];
+          for (int v = lane; v < rnv[c]; v += 32)
+            cp_async16(vs0 + (size_t)c * kValStage + v * 16, src + v * 16);
+          cp_async_commit();
         }
       }
       const int buf = j & 1;
@@ -375,12 +462,56 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         tmem_wait_ld();
         const uint64_t kw = keep[c];
         uint32_t w[32];
+        if constexpr (EPI == kEpiRelu2) {
+          // grad_z = bit ? bf16(float(bf16(acc)) * (2k r)) : 0, r the stored
+          // value at the element's rank, read from the staged run
+          if (c + 1 < kBN / 64) cp_async_wait<1>();  // this chunk's copies are in
+          else cp_async_wait<0>();
+          __syncwarp();
+          uint8_t *vs = vs0 + (size_t)(c % kValBufs) * kValStage;
+          const uint32_t first = rfirst[c], excl = rexcl[c];
+          const uint16_t *sv = reinterpret_cast<const uint16_t *>(vs);
+          uint32_t rk = first + excl;
+          // k = 1 (the reference's RELU2_SCALE): 2r is exact in bf16 and the
+          // fp32 product of two bf16 values is exact, so bf16(g * 2r) is one
+          // bf16x2 multiply (round to nearest even); other k: fp32 as written
+          const bool two = P.two_k == 2.0f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          // mask bits 2i, 2i+1 -> 0x0000FFFF / 0xFFFF0000 halves
-          const uint32_t two = (uint32_t)(kw >> (2 * i)) & 3u;
-          const uint32_t keep_w = ((two & 1u) ? 0x0000FFFFu : 0u) | ((two & 2u) ? 0xFFFF0000u : 0u);
-          w[i] = bf16x2_rn(r[2 * i], r[2 * i + 1]) & keep_w & zero_guard;
+          for (int i = 0; i < 32; ++i) {
+            const uint32_t g2 = bf16x2_rn(r[2 * i], r[2 * i + 1]);  // grad_h, rounded
+            const uint32_t b0 = (uint32_t)(kw >> (2 * i)) & 1u;
+            const uint32_t b1 = (uint32_t)(kw >> (2 * i + 1)) & 1u;
+            const uint32_t u0 = sv[rk];
+            rk += b0;
+            const uint32_t u1 = sv[rk];
+            rk += b1;
+            uint32_t y;
+            if (two) {
+              y = bf16x2_mul(g2, bf16x2_mul(u0 | (u1 << 16), 0x40004000u));  // g * (2 r)
+            } else {
+              const float y0 = __uint_as_float(g2 << 16) * (P.two_k * __uint_as_float(u0 << 16));
+              const float y1 =
+                  __uint_as_float(g2 & 0xFFFF0000u) * (P.two_k * __uint_as_float(u1 << 16));
+              y = bf16x2_rn(__float_as_uint(y0), __float_as_uint(y1));
+            }
+            const uint32_t keep_w = (b0 ? 0x0000FFFFu : 0u) | (b1 ? 0xFFFF0000u : 0u);
+            w[i] = y & keep_w & zero_guard;
+          }
+          if (c + kValBufs < kBN / 64) {  // refill this buffer with chunk c + 2
+            __syncwarp();
+            const uint8_t *src = reinterpret_cast<const uint8_t *>(P.vals) + ra0[c + kValBufs];
+            for (int v = lane; v < rnv[c + kValBufs]; v += 32)
+              cp_async16(vs + v * 16, src + v * 16);
+          }
+          cp_async_commit();  // (possibly empty) group: the wait counts stay uniform
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            // mask bits 2i, 2i+1 -> 0x0000FFFF / 0xFFFF0000 halves
+            const uint32_t two = (uint32_t)(kw >> (2 * i)) & 3u;
+            const uint32_t keep_w = ((two & 1u) ? 0x0000FFFFu : 0u) | ((two & 2u) ? 0xFFFF0000u : 0u);
+            w[i] = bf16x2_rn(r[2 * i], r[2 * i + 1]) & keep_w & zero_guard;
+          }
         }
         const int64_t n = n0 + 64 * c;
         if (P.c_tma) {
@@ -470,11 +601,12 @@ bool make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, in
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool MASK, int CG>
+template <int EPI, int CG>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
                 const GemmParams &P, cudaStream_t st) {
-  using G = GemmCfg<CG>;
-  auto kernel = gemm_mask_kernel<MASK, CG>;
+  using G = GemmCfg<CG, EPI>;
+  static_assert(G::SMEM <= 227 * 1024, "shared memory of one CTA");
+  auto kernel = gemm_mask_kernel<EPI, CG>;
   // The shared-memory attribute is per device and the SM count may differ
   // between devices: both are set up once for each device this process uses.
   constexpr int kMaxDev = 64;
@@ -518,9 +650,12 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap 
 
 using namespace bs;
 
-extern "C" int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int64_t ldb,
-                                 void *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
-                                 const uint8_t *mask, int32_t *status, void *stream) {
+namespace bs {
+namespace {
+// Shared by the entry points: checks, tensor maps, and the launch of the
+// epilogue variant EPI (P's epilogue fields already set by the caller).
+int gemm_run(const void *A, int64_t lda, const void *B, int64_t ldb, void *C, int64_t ldc,
+             int64_t M, int64_t N, int64_t K, int epi, GemmParams &P, cudaStream_t st) {
   if (M < 0 || N < 0 || K < 0) return BS_ERR_SHAPE;
   if (M == 0 || N == 0) return BS_OK;
   if (!A || !B || !C) return BS_ERR_ARG;
@@ -531,19 +666,17 @@ extern "C" int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int6
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
       ((lda * 2) & 15) || ((ldb * 2) & 15))
     return BS_ERR_ALIGN;
-  if (mask && (reinterpret_cast<uintptr_t>(mask) & 3)) return BS_ERR_ALIGN;
-  GemmParams P{};
+  if (P.mask && (reinterpret_cast<uintptr_t>(P.mask) & 7)) return BS_ERR_ALIGN;
   P.C = static_cast<uint8_t *>(C);
   P.M = M; P.N = N; P.K = K; P.ldc = ldc;
-  P.mask = mask;
   P.mask_grid_n = (N + kTileN - 1) / kTileN;
+  P.mask_grid_m = (M + kTileM - 1) / kTileM;
   P.c_tma = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((ldc * 2) % 16 == 0);
-  P.status = status;
   CUtensorMap ta, tb, tc;
-  if (K == 0) {  // empty reduction: C = 0
+  if (K == 0) {  // empty reduction: C = 0 (so is every epilogue of it)
     for (int64_t r = 0; r < M; ++r)
-      if (cudaMemsetAsync(static_cast<uint8_t *>(C) + r * ldc * 2, 0, (size_t)N * 2,
-                          static_cast<cudaStream_t>(stream)) != cudaSuccess)
+      if (cudaMemsetAsync(static_cast<uint8_t *>(C) + r * ldc * 2, 0, (size_t)N * 2, st) !=
+          cudaSuccess)
         return BS_ERR_LAUNCH;
     return BS_OK;
   }
@@ -553,8 +686,42 @@ extern "C" int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int6
   const bool pair = M >= 2 * kBM && !getenv("BS_GEMM_ONE_CTA");
   if (P.c_tma && !make_map(&tc, C, M, N, ldc, 64, 32)) P.c_tma = 0;
   if (!P.c_tma) tc = ta;  // unused
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (pair)
-    return mask ? launch_gemm<true, 2>(ta, tb, tc, P, st) : launch_gemm<false, 2>(ta, tb, tc, P, st);
-  return mask ? launch_gemm<true, 1>(ta, tb, tc, P, st) : launch_gemm<false, 1>(ta, tb, tc, P, st);
+  if (pair) {
+    if (epi == kEpiRelu2) return launch_gemm<kEpiRelu2, 2>(ta, tb, tc, P, st);
+    return epi == kEpiMask ? launch_gemm<kEpiMask, 2>(ta, tb, tc, P, st)
+                           : launch_gemm<kEpiNone, 2>(ta, tb, tc, P, st);
+  }
+  if (epi == kEpiRelu2) return launch_gemm<kEpiRelu2, 1>(ta, tb, tc, P, st);
+  return epi == kEpiMask ? launch_gemm<kEpiMask, 1>(ta, tb, tc, P, st)
+                         : launch_gemm<kEpiNone, 1>(ta, tb, tc, P, st);
+}
+}  // namespace
+}  // namespace bs
+
+extern "C" int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int64_t ldb,
+                                 void *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                 const uint8_t *mask, int32_t *status, void *stream) {
+  GemmParams P{};
+  P.mask = mask;
+  P.status = status;
+  return gemm_run(A, lda, B, ldb, C, ldc, M, N, K, mask ? kEpiMask : kEpiNone, P,
+                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bs_gemm_bf16_relu2(const void *A, int64_t lda, const void *B, int64_t ldb,
+                                  void *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                  const void *vals, const uint8_t *bitmask,
+                                  const uint32_t *prefix, const int64_t *vals_offset, float k,
+                                  int32_t *status, void *stream) {
+  if (!vals || !bitmask || !prefix || !vals_offset) return BS_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(vals) & 15) return BS_ERR_ALIGN;  // 16-byte staging loads
+  GemmParams P{};
+  P.mask = bitmask;
+  P.vals = static_cast<const uint16_t *>(vals);
+  P.prefix = prefix;
+  P.vals_offset = vals_offset;
+  P.two_k = 2.0f * k;
+  P.status = status;
+  return gemm_run(A, lda, B, ldb, C, ldc, M, N, K, kEpiRelu2, P,
+                  static_cast<cudaStream_t>(stream));
 }

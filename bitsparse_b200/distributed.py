@@ -126,3 +126,87 @@ def gather_bitsparse(local: BitsparseTensor, group=None) -> BitsparseTensor:
                                       local.dtype, gm, gn, local.BLOCK_M, local.BLOCK_N,
                                       scale=local.scale, pack_sbit=False))
     return concat_row_shards(shards)
+
+
+class GradAllReduce:
+    """Data-parallel gradient reduction overlapped with the backward pass.
+
+    The reference's nanoGPT trainer sums every parameter's gradient over the
+    ranks after the backward pass, one ``all_reduce`` per parameter
+    (``dist.all_reduce(p.grad, op=SUM)``, nanogpt/logs/...txt:385-387).  Here
+    the parameters are grouped, in reverse registration order (roughly the
+    order the backward pass produces their gradients), into buckets of about
+    ``bucket_mb`` MB; a post-accumulate-grad hook counts the gradients of
+    each bucket, and when the last one is ready the bucket is flattened and
+    its ``all_reduce`` starts asynchronously (NCCL on GPUs, gloo on CPUs)
+    while the backward pass continues.  ``wait()`` completes the reductions
+    and writes the summed (``op="sum"``) or averaged (``"avg"``) gradients
+    back.  One instance serves every step; a parameter without a gradient in
+    a step is reduced as zeros.
+    """
+
+    def __init__(self, params, group=None, bucket_mb: float = 32.0, op: str = "sum"):
+        if op not in ("sum", "avg"):
+            raise ValueError("op must be 'sum' or 'avg'")
+        self.group, self.op = group, op
+        self.params = [p for p in params if p.requires_grad]
+        limit = int(bucket_mb * 2**20)
+        self.buckets: list[list] = []
+        cur, size = [], 0
+        for p in reversed(self.params):
+            cur.append(p)
+            size += p.numel() * p.element_size()
+            if size >= limit:
+                self.buckets.append(cur)
+                cur, size = [], 0
+        if cur:
+            self.buckets.append(cur)
+        self._bucket_of = {}
+        for i, b in enumerate(self.buckets):
+            for p in b:
+                self._bucket_of[p] = i
+        self._pending = [len(b) for b in self.buckets]
+        self._works: list = [None] * len(self.buckets)
+        self._flat: list = [None] * len(self.buckets)
+        self._hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in self.params]
+
+    def _launch(self, i: int) -> None:
+        grads = [p.grad if p.grad is not None else torch.zeros_like(p) for p in self.buckets[i]]
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        self._flat[i] = flat
+        self._works[i] = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group,
+                                         async_op=True)
+
+    def _ready(self, p) -> None:
+        i = self._bucket_of[p]
+        self._pending[i] -= 1
+        if self._pending[i] == 0:
+            self._launch(i)
+
+    def wait(self) -> None:
+        """Finish every bucket's reduction (launching those whose gradients
+        did not all arrive) and write the results into ``p.grad``."""
+        world = dist.get_world_size(self.group)
+        for i, b in enumerate(self.buckets):
+            if self._works[i] is None:
+                self._launch(i)
+            self._works[i].wait()
+            flat = self._flat[i]
+            if self.op == "avg":
+                flat.div_(world)
+            off = 0
+            for p in b:
+                n = p.numel()
+                g = flat[off: off + n].view_as(p)
+                if p.grad is None:
+                    p.grad = g.clone()
+                else:
+                    p.grad.copy_(g)
+                off += n
+            self._works[i] = self._flat[i] = None
+            self._pending[i] = len(b)
+
+    def remove(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []

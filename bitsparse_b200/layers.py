@@ -16,7 +16,7 @@ from .config import RELU2_SCALE
 from .fp8 import is_fp8, matmul, to_fp8, to_fp8_layouts
 from .src.functions import dense_to_tilesparse, relu_to_tilesparse_fp8
 from .src.operators import (compress_bias_relu, compress_bias_relu_fp8, mask_with_bitmask_,
-                            matmul_relu_mask, relu2_grad_sparse_)
+                            matmul_relu2_grad, matmul_relu_mask, relu2_grad_sparse_)
 from .src.sparse_matmul import AspB, AspRelu2B
 
 
@@ -187,7 +187,14 @@ class Relu2Linear(Function):
             go_col, scale = grad_output, None
         grad_W2 = AspRelu2B(go_col.T, h, A_scale=scale) if ctx.needs_input_grad[1] else None
         grad_z = None
-        if want_z:
+        if want_z and not fp8:
+            # one tcgen05 GEMM with the ReLU^2 gradient in its epilogue where
+            # it applies (bf16 raw storage), else the two steps
+            go = grad_output if grad_output.is_contiguous() else grad_output.contiguous()
+            grad_z = matmul_relu2_grad(go, W, h) if _tma_ok(go) and _tma_ok(W) else None
+            if grad_z is None:
+                grad_z = relu2_grad_sparse_(matmul(grad_output, W, False), h)
+        elif want_z:
             grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
             grad_z = relu2_grad_sparse_(grad_h, h)
         grad_bias = grad_z.sum(0) if needs_bias else None

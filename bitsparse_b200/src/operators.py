@@ -286,6 +286,37 @@ def matmul_relu_mask(a: Tensor, b: Tensor, sparse: BitsparseTensor | None = None
     return out
 
 
+def matmul_relu2_grad(a: Tensor, b: Tensor, sparse: BitsparseTensor) -> Tensor | None:
+    """``relu2_grad_sparse_(a @ b, sparse)`` for bf16 storage in one tcgen05
+    GEMM: the ReLU^2 gradient ``grad * (2 k r)`` (r the stored activation)
+    is applied in the epilogue, so the dense ``a @ b`` never reaches memory
+    (lib_sparse/layers.py:146-147).  Same roundings as the two-step form.
+    Returns ``None`` when this path does not apply (FP8 or packed storage, a
+    value base not 16-byte aligned, operands TMA cannot read), and the
+    caller uses the two steps."""
+    if (sparse.dtype != torch.bfloat16 or sparse.pack_sbit or sparse.scale is not None
+            or a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16):
+        return None
+    if a.dim() != 2 or b.dim() != 2 or a.stride(1) != 1 or b.stride(1) != 1:
+        return None
+    M, K = a.shape
+    K2, N = b.shape
+    if K != K2 or tuple(sparse.shape) != (M, N) or sparse.vals.data_ptr() % 16:
+        return None
+    if (sparse.BLOCK_M, sparse.BLOCK_N) != (_BM, _BN):
+        return None
+    out = torch.empty((M, N), device=a.device, dtype=torch.bfloat16)
+    rc = _lib.load().bs_gemm_bf16_relu2(
+        a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), out.data_ptr(), N, M, N, K,
+        sparse.vals.data_ptr(), sparse.bitmask.data_ptr(), sparse.prefix.data_ptr(),
+        sparse.vals_offset.data_ptr(), float(RELU2_SCALE), R.status_word(a.device).data_ptr(),
+        _stream(a))
+    if rc == _lib.BS_ERR_ALIGN:
+        return None
+    _lib.check(rc, "bs_gemm_bf16_relu2")
+    return out
+
+
 def _fused_compress(fn, name: str, head: tuple, dev, stream: int, stored, M: int, N: int,
                     T: int, bitmask: Tensor, prefix: Tensor, sparse_data, pack_sbit: bool):
     """Run a fused compress entry point ``fn(*head, bitmask, prefix, vals,

@@ -276,6 +276,20 @@ int bs_gemm_bf16_mask(const void *A, int64_t lda, const void *B, int64_t ldb,
                       void *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
                       const uint8_t *mask, int32_t *status, void *stream);
 
+/* The backward of Relu2Linear for bf16 storage in one tcgen05 GEMM:
+ * C = (A @ B) with the ReLU^2 gradient applied in the epilogue --
+ * C[i, j] = bit ? bf16(float(bf16(acc)) * (2 k r)) : +0, r the stored value
+ * of the bitsparse [M, N] tensor h = relu(z) at (i, j) (raw bf16 storage:
+ * `vals` 16-byte aligned, its `bitmask`, `prefix`, device `vals_offset`),
+ * k = RELU2_SCALE.  Replaces grad_h = matmul(grad_output, W) followed by
+ * relu2_grad_sparse_ (lib_sparse/layers.py:146-147,
+ * lib_sparse/src/triton_kernels.py:288-330) with the same roundings,
+ * without the dense grad_h reaching memory.  Operands as bs_gemm_bf16_mask. */
+int bs_gemm_bf16_relu2(const void *A, int64_t lda, const void *B, int64_t ldb,
+                       void *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                       const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
+                       const int64_t *vals_offset, float k, int32_t *status, void *stream);
+
 /* Per-tensor fp8 scale of to_fp8 (lib_sparse/fp8.py:123-129):
  * *scale_out = max(amax(|x|) / 448, 1e-9), with the amax / 448 rounded to
  * bf16 for bf16 input (eager PyTorch semantics).  `amax_ws` is a device

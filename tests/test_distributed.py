@@ -114,3 +114,57 @@ def test_sharded_gpu_compress_concat():
     assert torch.equal(merged.bitmask, whole.bitmask)
     assert torch.equal(merged.prefix.view(torch.int32), whole.prefix.view(torch.int32))
     assert torch.equal(merged.vals, whole.vals)
+
+
+def _small_model(seed):
+    torch.manual_seed(seed)
+    return torch.nn.Sequential(torch.nn.Linear(16, 64), torch.nn.ReLU(), torch.nn.Linear(64, 8),
+                               torch.nn.ReLU(), torch.nn.Linear(8, 3))
+
+
+def _rank_batch(rank):
+    g = torch.Generator().manual_seed(100 + rank)
+    return torch.randn(32, 16, generator=g), torch.randn(32, 3, generator=g)
+
+
+def _grad_worker(rank, world, port, op, steps):
+    from bitsparse_b200.distributed import GradAllReduce
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        model = _small_model(0)
+        red = GradAllReduce(model.parameters(), bucket_mb=0.001, op=op)  # several buckets
+        assert len(red.buckets) > 1
+        x, y = _rank_batch(rank)
+        # the expected result: every rank's gradients, computed here, summed
+        ref = [torch.zeros_like(p) for p in model.parameters()]
+        for r in range(world):
+            m = _small_model(0)
+            xr, yr = _rank_batch(r)
+            ((m(xr) - yr) ** 2).sum().backward()
+            for acc, p in zip(ref, m.parameters()):
+                acc += p.grad
+        if op == "avg":
+            ref = [g / world for g in ref]
+        for _ in range(steps):  # the same instance across steps
+            model.zero_grad(set_to_none=True)
+            ((model(x) - y) ** 2).sum().backward()
+            red.wait()
+            for p, g in zip(model.parameters(), ref):
+                torch.testing.assert_close(p.grad, g, rtol=1e-5, atol=1e-6)
+        red.remove()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("op", ["sum", "avg"])
+def test_grad_all_reduce_gloo(op):
+    """world_size-2 gloo ranks on the CPU: the bucketed, backward-overlapped
+    gradient reduction equals the sum (or mean) of every rank's gradients,
+    over repeated steps."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_grad_worker, args=(2, port, op, 3), nprocs=2, join=True)

@@ -52,3 +52,53 @@ def test_gemm_rejects_misaligned_operands():
     a, b, _ = _operands(64, 64, 64, 1)
     with pytest.raises(RuntimeError):
         matmul_relu_mask(a, b[:, 1:].contiguous()[:, :60].T.contiguous().T)  # ldb not 8-aligned
+
+
+@pytest.mark.parametrize("M, N, K", [(256, 512, 128), (200, 304, 72), (1024, 3072, 768),
+                                     (8192, 3072, 768), (130, 72, 40)])
+@pytest.mark.parametrize("arena", [False, True])
+def test_relu2_epilogue_equals_two_steps(M, N, K, arena):
+    """The ReLU^2 gradient in the GEMM epilogue == the same GEMM's bf16
+    output followed by relu2_grad_sparse_, bit for bit (standalone storage
+    and a TensorBuffer at an odd offset); and within RTOL of an fp32
+    reference of grad_h * 2r."""
+    from bitsparse_b200 import TensorBuffer
+    from bitsparse_b200.src.operators import matmul_relu2_grad, relu2_grad_sparse_
+    a, b, h = _operands(M, N, K, 3 * M + K)
+    buf = None
+    if arena:
+        buf = TensorBuffer(2 * M * N + 64, device="cuda", dtype=torch.bfloat16)
+        buf.offset.fill_(37)
+    sp = dense_to_tilesparse(h, None, buf)
+    out = matmul_relu2_grad(a, b, sp)
+    assert out is not None
+    two = relu2_grad_sparse_(matmul_relu_mask(a, b), sp)
+    assert torch.equal(out, two)
+    ref = torch.where(h > 0, (a.float() @ b.float()) * (2 * h.float()), torch.zeros(()).cuda())
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2 * RTOL * ref.abs().max().item()
+    assert not torch.any(torch.signbit(out[h == 0]))
+    B.check_status()
+
+
+def test_relu2_epilogue_extreme_values():
+    """Stored activations over the whole bf16 exponent range (subnormals to
+    the largest finite values) and gradients from tiny to large: the fused
+    ReLU^2 epilogue still equals the GEMM followed by relu2_grad_sparse_
+    (overflow to inf and underflow to zero included)."""
+    from bitsparse_b200.src.operators import matmul_relu2_grad, relu2_grad_sparse_
+    M, N, K = 512, 512, 64
+    g = torch.Generator(device="cuda").manual_seed(11)
+    a = (torch.randn(M, K, generator=g, device="cuda")
+         * torch.exp2(torch.randint(-60, 60, (M, 1), generator=g, device="cuda").float()))
+    a = a.to(torch.bfloat16)
+    b = torch.randn(K, N, generator=g, device="cuda").to(torch.bfloat16)
+    e = torch.randint(-133, 127, (M, N), generator=g, device="cuda").float()
+    h = (torch.rand(M, N, generator=g, device="cuda") * torch.exp2(e))
+    h = torch.where(torch.rand(M, N, generator=g, device="cuda") < 0.4, 0.0, h).to(torch.bfloat16)
+    sp = dense_to_tilesparse(h, None)
+    out = matmul_relu2_grad(a, b, sp)
+    two = relu2_grad_sparse_(matmul_relu_mask(a, b), sp)
+    finite = torch.isfinite(two.float()) | torch.isinf(two.float())
+    assert torch.equal(out[finite], two[finite])
+    B.check_status()

@@ -124,7 +124,11 @@ class _DenseTwin(torch.autograd.Function):
             if scale is not None:
                 dense.mul_(scale.square())
             gW = matmul(go.T, dense, fp8, a_scale=gscale)
-            gh = matmul(go, W, fp8=fp8, a_scale=gscale)
+            if fp8:
+                gh = matmul(go, W, fp8=fp8, a_scale=gscale)
+            else:  # the layer's grad_h comes from the tcgen05 GEMM (ReLU^2 epilogue)
+                from bitsparse_b200.src.operators import matmul_relu_mask
+                gh = matmul_relu_mask(go.contiguous(), W)
             gz = torch.where(mask, (gh.float() * (2.0 * r)).to(torch.bfloat16),
                              torch.zeros((), dtype=torch.bfloat16, device=gh.device))
             if scale is not None:
