@@ -46,6 +46,10 @@ _SIGS = {
     "bs_transpose_b8": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
     "bs_gemm_bf16_mask": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
                                  _vp]),
+    "bs_gemm_fp8": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp,
+                           _vp]),
+    "bs_gemm_fp8_relu2": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
+                                 _vp, _vp, _vp, _vp, C.c_float, _vp, _vp, _vp]),
     "bs_gemm_bf16_relu2": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
                                   _vp, _vp, C.c_float, _vp, _vp]),
     "bs_tile_pack": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),

@@ -64,10 +64,24 @@ struct GemmParams {
   const uint32_t *prefix;
   const int64_t *vals_offset;
   float two_k;
+  // FP8 form: the per-tensor scales of A and B (device fp32 scalars)
+  const float *scale_a, *scale_b;
+  // FP8 ReLU^2 epilogue: the stored activation's e4m3 scale, or null
+  const float *hscale;
 };
 
-// Epilogues: none, the ReLU mask, the ReLU^2 gradient.
-enum { kEpiNone = 0, kEpiMask = 1, kEpiRelu2 = 2 };
+// Epilogues: none, the ReLU mask, the ReLU^2 gradient; kEpiFp8 is the FP8
+// form of the GEMM (e4m3 operands, both K-major, C = bf16(acc * sa * sb)).
+// kEpiFp8Relu2 is the FP8 GEMM with the ReLU^2 gradient of an e4m3-stored
+// activation in its epilogue.
+enum { kEpiNone = 0, kEpiMask = 1, kEpiRelu2 = 2, kEpiFp8 = 3, kEpiFp8Relu2 = 4 };
+template <int EPI>
+constexpr bool epi_f8() { return EPI == kEpiFp8 || EPI == kEpiFp8Relu2; }
+template <int EPI>
+constexpr bool epi_relu2() { return EPI == kEpiRelu2 || EPI == kEpiFp8Relu2; }
+// K elements per stage: 64 bf16 or 128 e4m3 -- 128-byte rows either way
+template <int EPI>
+constexpr int stage_k() { return epi_f8<EPI>() ? 128 : kBK; }
 
 __device__ __forceinline__ uint32_t saddr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -94,10 +108,20 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
-template <int CG>
+template <int CG, bool F8 = false>
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
-  if constexpr (CG == 2)
+  if constexpr (F8 && CG == 2)
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  else if constexpr (F8)
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  else if constexpr (CG == 2)
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
@@ -203,13 +227,16 @@ struct GemmCfg {
   static constexpr int BBYTES = kBK * BNL * 2;  // B bytes per stage and CTA
   static constexpr int STAGE = kABytes + BBYTES;
   // stages (one fewer with the ReLU^2 epilogue's value staging)
-  static constexpr int NST = (CG == 2 ? 6 : 4) - (EPI == kEpiRelu2 ? 1 : 0);
-  static constexpr int VBYTES = EPI == kEpiRelu2 ? 4 * kValBufs * kValStage : 0;
+  static constexpr int NST = (CG == 2 ? 6 : 4) - (epi_relu2<EPI>() ? 1 : 0);
+  static constexpr int VBYTES = epi_relu2<EPI>() ? 4 * kValBufs * kValStage + 512 : 0;
   static constexpr size_t SMEM = 1024 + (size_t)NST * STAGE + kEpiBytes + VBYTES + 256;
-  // instruction descriptor: M = BM, N = kBN
-  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) |
-                                    (1u << 16) | ((uint32_t)(kBN >> 3) << 17) |
-                                    ((uint32_t)(BM >> 4) << 24);
+  // instruction descriptor: fp32 accumulator, M = BM, N = kBN; bf16 A
+  // (K-major) and B (MN-major), or e4m3 A and B (both K-major)
+  static constexpr uint32_t IDESC =
+      epi_f8<EPI>()
+          ? ((1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24))
+          : ((1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) |
+             ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24));
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -245,7 +272,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
                      const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmParams P) {
   using G = GemmCfg<CG, EPI>;
-  constexpr bool MASK = EPI != kEpiNone;
+  constexpr bool F8 = epi_f8<EPI>();
+  constexpr bool RELU2 = epi_relu2<EPI>();
+  constexpr bool MASK = EPI == kEpiMask || RELU2;
+  constexpr int VB = EPI == kEpiFp8Relu2 ? 1 : 2;  // bytes per stored value
+  constexpr int BKE = stage_k<EPI>();  // K elements per stage
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms (same offsets in both
   // CTAs of a pair, which the cta_group::2 descriptors rely on)
@@ -263,10 +294,17 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   const uint32_t rank = CG == 2 ? cluster_rank() : 0;
   const bool leader = rank == 0;
   const int64_t cid = (int64_t)blockIdx.x / CG, ncl = (int64_t)gridDim.x / CG;
-  const int nk = (int)((P.K + kBK - 1) / kBK);
+  const int nk = (int)((P.K + BKE - 1) / BKE);
   const int64_t mt = (P.M + G::BM - 1) / G::BM, nt = (P.N + kBN - 1) / kBN;
   const int64_t ntiles = mt * nt;
 
+  // FP8 ReLU^2: bf16 bits of every e4m3 code (exact: e4m3 values are bf16
+  // values), filled before the start-up barrier below
+  uint16_t *code_bf16 = reinterpret_cast<uint16_t *>(vstage + 4 * kValBufs * kValStage);
+  if constexpr (EPI == kEpiFp8Relu2) {
+    for (int c = threadIdx.x; c < 256; c += blockDim.x)
+      code_bf16[c] = (uint16_t)(__float_as_uint(store_bits_to_f32<BS_E4M3>((uint32_t)c)) >> 16);
+  }
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
@@ -323,16 +361,24 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           if constexpr (CG == 2) {
             if (leader) mbar_expect_tx(&full[s], 2 * G::STAGE);
             const uint32_t bar = map_rank(saddr(&full[s]), 0);
-            tma_load_2d_pair(a, &tmA, kb * kBK, ay, bar);
+            tma_load_2d_pair(a, &tmA, kb * BKE, ay, bar);
 #pragma unroll
-            for (int j = 0; j < G::BNL / 64; ++j)
-              tma_load_2d_pair(b + j * (kBK * 64 * 2), &tmB, bx + 64 * j, kb * kBK, bar);
+            for (int j = 0; j < G::BNL / 64; ++j) {
+              if constexpr (F8)  // B^T rows (K-major): 64 rows of 128 K-bytes per box
+                tma_load_2d_pair(b + j * 8192, &tmB, kb * BKE, bx + 64 * j, bar);
+              else
+                tma_load_2d_pair(b + j * 8192, &tmB, bx + 64 * j, kb * BKE, bar);
+            }
           } else {
             mbar_expect_tx(&full[s], G::STAGE);
-            tma_load_2d(a, &tmA, kb * kBK, ay, &full[s]);
+            tma_load_2d(a, &tmA, kb * BKE, ay, &full[s]);
 #pragma unroll
-            for (int j = 0; j < G::BNL / 64; ++j)
-              tma_load_2d(b + j * (kBK * 64 * 2), &tmB, bx + 64 * j, kb * kBK, &full[s]);
+            for (int j = 0; j < G::BNL / 64; ++j) {
+              if constexpr (F8)
+                tma_load_2d(b + j * 8192, &tmB, kb * BKE, bx + 64 * j, &full[s]);
+              else
+                tma_load_2d(b + j * 8192, &tmB, bx + 64 * j, kb * BKE, &full[s]);
+            }
           }
         }
       }
@@ -367,9 +413,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             // A: K-major, 128-byte rows, 8-row atoms 1024 B apart; +32 B per K=16.
             // B: MN-major, 64-column atoms 8 KB apart (LBO), 8-row K groups
             //    1024 B apart (SBO); +2048 B per K=16.
+            // (e4m3: K = 32 per MMA, 32 bytes as well; B K-major like A)
             const uint64_t ad = smem_desc(a + 32 * k, 16, 1024);
-            const uint64_t bd = smem_desc(b + 2048 * k, kBK * 64 * 2, 1024);
-            mma_bf16<CG>(d, ad, bd, G::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            const uint64_t bd = F8 ? smem_desc(b + 32 * k, 16, 1024)
+                                   : smem_desc(b + 2048 * k, kBK * 64 * 2, 1024);
+            mma_bf16<CG, F8>(d, ad, bd, G::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
           }
           // the stage is free (in both CTAs) once these MMAs have read it
           mma_commit_to<CG>(saddr(&empty[s]));
@@ -382,6 +430,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   } else {
     // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (this CTA's rows)
     const int q = warp & 3;
+    const float alpha = F8 ? (*P.scale_a) * (*P.scale_b) : 1.f;  // FP8: sa * sb
     const uint32_t acc_empty_leader = map_rank(saddr(acc_empty), 0);
     int j = 0;
     for (int64_t t = cid; t < ntiles; t += ncl, ++j) {
@@ -393,11 +442,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       uint64_t keep[kBN / 64];
 #pragma unroll
       for (int i = 0; i < kBN / 64; ++i) {
-        keep[i] = EPI == kEpiRelu2 ? 0ull : ~0ull;
+        keep[i] = RELU2 ? 0ull : ~0ull;
         if constexpr (MASK) {
           // ReLU^2 counts values, so every row of an existing tile is read
           // (rows past M have clear bits there)
-          const bool in = EPI == kEpiRelu2 ? (m >> 6) < P.mask_grid_m : m < P.M;
+          const bool in = RELU2 ? (m >> 6) < P.mask_grid_m : m < P.M;
           if (in && n0 + 64 * i < P.N)
             keep[i] = *reinterpret_cast<const uint64_t *>(
                 P.mask + ((m >> 6) * P.mask_grid_n + (n0 >> 6) + i) * kTileBytes + (m & 63) * 8);
@@ -411,7 +460,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       int64_t ra0[kBN / 64];
       int rnv[kBN / 64];
       uint8_t *vs0 = vstage + (size_t)q * kValBufs * kValStage;
-      if constexpr (EPI == kEpiRelu2) {
+      if constexpr (RELU2) {
 #pragma unroll
         for (int c = 0; c < kBN / 64; ++c) {
           rexcl[c] = 0; rfirst[c] = 0; ra0[c] = 0; rnv[c] = 0;
@@ -432,10 +481,10 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             }
             const uint32_t total = __shfl_sync(0xFFFFFFFFu, inc, 31);
             const int64_t seg0 = (int64_t)P.prefix[tile] + *P.vals_offset + before;
-            const int64_t a0 = (seg0 * 2) & ~(int64_t)15;
-            const int64_t a1 = ((seg0 + (int64_t)total) * 2 + 15) & ~(int64_t)15;
+            const int64_t a0 = (seg0 * VB) & ~(int64_t)15;
+            const int64_t a1 = ((seg0 + (int64_t)total) * VB + 15) & ~(int64_t)15;
             rexcl[c] = inc - cnt;
-            rfirst[c] = (uint32_t)((seg0 * 2 - a0) >> 1);
+            rfirst[c] = (uint32_t)((seg0 * VB - a0) / VB);
             ra0[c] = a0;
             rnv[c] = (int)((a1 - a0) >> 4);
           }
@@ -462,15 +511,20 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         tmem_wait_ld();
         const uint64_t kw = keep[c];
         uint32_t w[32];
-        if constexpr (EPI == kEpiRelu2) {
+        if constexpr (RELU2) {
           // grad_z = bit ? bf16(float(bf16(acc)) * (2k r)) : 0, r the stored
-          // value at the element's rank, read from the staged run
+          // value at the element's rank, read from the staged run; FP8: acc
+          // is scaled by sa * sb before the rounding (the GEMM's output), r
+          // is the e4m3 value, and the result is multiplied by the stored
+          // tensor's scale with a second rounding (grad.mul_(scale))
           if (c + 1 < kBN / 64) cp_async_wait<1>();  // this chunk's copies are in
           else cp_async_wait<0>();
           __syncwarp();
           uint8_t *vs = vs0 + (size_t)(c % kValBufs) * kValStage;
           const uint32_t first = rfirst[c], excl = rexcl[c];
           const uint16_t *sv = reinterpret_cast<const uint16_t *>(vs);
+          const uint8_t *sv8 = vs;
+          const float hs = (EPI == kEpiFp8Relu2 && P.hscale) ? *P.hscale : 1.f;
           uint32_t rk = first + excl;
           // k = 1 (the reference's RELU2_SCALE): 2r is exact in bf16 and the
           // fp32 product of two bf16 values is exact, so bf16(g * 2r) is one
@@ -478,12 +532,15 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           const bool two = P.two_k == 2.0f;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const uint32_t g2 = bf16x2_rn(r[2 * i], r[2 * i + 1]);  // grad_h, rounded
+            const uint32_t g2 =  // grad_h, rounded
+                F8 ? bf16x2_rn(__float_as_uint(__uint_as_float(r[2 * i]) * alpha),
+                               __float_as_uint(__uint_as_float(r[2 * i + 1]) * alpha))
+                   : bf16x2_rn(r[2 * i], r[2 * i + 1]);
             const uint32_t b0 = (uint32_t)(kw >> (2 * i)) & 1u;
             const uint32_t b1 = (uint32_t)(kw >> (2 * i + 1)) & 1u;
-            const uint32_t u0 = sv[rk];
+            const uint32_t u0 = VB == 1 ? code_bf16[sv8[rk]] : sv[rk];
             rk += b0;
-            const uint32_t u1 = sv[rk];
+            const uint32_t u1 = VB == 1 ? code_bf16[sv8[rk]] : sv[rk];
             rk += b1;
             uint32_t y;
             if (two) {
@@ -493,6 +550,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
               const float y1 =
                   __uint_as_float(g2 & 0xFFFF0000u) * (P.two_k * __uint_as_float(u1 << 16));
               y = bf16x2_rn(__float_as_uint(y0), __float_as_uint(y1));
+            }
+            if constexpr (EPI == kEpiFp8Relu2) {
+              if (P.hscale)
+                y = bf16x2_rn(__float_as_uint(__uint_as_float(y << 16) * hs),
+                              __float_as_uint(__uint_as_float(y & 0xFFFF0000u) * hs));
             }
             const uint32_t keep_w = (b0 ? 0x0000FFFFu : 0u) | (b1 ? 0xFFFF0000u : 0u);
             w[i] = y & keep_w & zero_guard;
@@ -510,7 +572,12 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             // mask bits 2i, 2i+1 -> 0x0000FFFF / 0xFFFF0000 halves
             const uint32_t two = (uint32_t)(kw >> (2 * i)) & 3u;
             const uint32_t keep_w = ((two & 1u) ? 0x0000FFFFu : 0u) | ((two & 2u) ? 0xFFFF0000u : 0u);
-            w[i] = bf16x2_rn(r[2 * i], r[2 * i + 1]) & keep_w & zero_guard;
+            if constexpr (F8)
+              w[i] = bf16x2_rn(__float_as_uint(__uint_as_float(r[2 * i]) * alpha),
+                               __float_as_uint(__uint_as_float(r[2 * i + 1]) * alpha)) &
+                     zero_guard;
+            else
+              w[i] = bf16x2_rn(r[2 * i], r[2 * i + 1]) & keep_w & zero_guard;
           }
         }
         const int64_t n = n0 + 64 * c;
@@ -585,17 +652,18 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// 2-D bf16 tensor map: rows x cols (cols contiguous), box box_cols x box_rows,
-// 128-byte swizzle.
+// 2-D bf16 (or, with eb = 1, 8-bit) tensor map: rows x cols (cols
+// contiguous), box box_cols x box_rows, 128-byte swizzle.
 bool make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld,
-              uint32_t box_cols, uint32_t box_rows) {
+              uint32_t box_cols, uint32_t box_rows, int eb = 2) {
   EncodeTiledFn encode = encode_tiled();
   if (!encode) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * eb};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+  return encode(map, eb == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                2, const_cast<void *>(base), dims,
                 strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -659,12 +727,16 @@ int gemm_run(const void *A, int64_t lda, const void *B, int64_t ldb, void *C, in
   if (M < 0 || N < 0 || K < 0) return BS_ERR_SHAPE;
   if (M == 0 || N == 0) return BS_OK;
   if (!A || !B || !C) return BS_ERR_ARG;
-  if (lda < K || ldb < N || ldc < N) return BS_ERR_SHAPE;
+  if (lda < K || (epi != kEpiFp8 && epi != kEpiFp8Relu2 && ldb < N) || ldc < N)
+    return BS_ERR_SHAPE;
   if (M >= ((int64_t)1 << 31) || N >= ((int64_t)1 << 31) || K >= ((int64_t)1 << 31))
     return BS_ERR_TOO_LARGE;
-  // TMA: 16-byte aligned bases and row strides
+  // TMA: 16-byte aligned bases and row strides (FP8: B is B^T [N, K], ldb >= K)
+  const bool f8 = epi == kEpiFp8 || epi == kEpiFp8Relu2;
+  const int eb = f8 ? 1 : 2;
+  if (f8 && ldb < K) return BS_ERR_SHAPE;
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
-      ((lda * 2) & 15) || ((ldb * 2) & 15))
+      ((lda * eb) & 15) || ((ldb * eb) & 15))
     return BS_ERR_ALIGN;
   if (P.mask && (reinterpret_cast<uintptr_t>(P.mask) & 7)) return BS_ERR_ALIGN;
   P.C = static_cast<uint8_t *>(C);
@@ -680,17 +752,25 @@ int gemm_run(const void *A, int64_t lda, const void *B, int64_t ldb, void *C, in
         return BS_ERR_LAUNCH;
     return BS_OK;
   }
-  if (!make_map(&ta, A, M, K, lda, kBK, kBM) || !make_map(&tb, B, K, N, ldb, 64, kBK))
+  if (f8) {
+    if (!make_map(&ta, A, M, K, lda, 128, kBM, 1) || !make_map(&tb, B, N, K, ldb, 128, 64, 1))
+      return BS_ERR_ALIGN;
+  } else if (!make_map(&ta, A, M, K, lda, kBK, kBM) || !make_map(&tb, B, K, N, ldb, 64, kBK)) {
     return BS_ERR_ALIGN;
+  }
   // CTA pairs (cta_group::2) once there are two 128-row blocks to share
   const bool pair = M >= 2 * kBM && !getenv("BS_GEMM_ONE_CTA");
   if (P.c_tma && !make_map(&tc, C, M, N, ldc, 64, 32)) P.c_tma = 0;
   if (!P.c_tma) tc = ta;  // unused
   if (pair) {
+    if (epi == kEpiFp8) return launch_gemm<kEpiFp8, 2>(ta, tb, tc, P, st);
+    if (epi == kEpiFp8Relu2) return launch_gemm<kEpiFp8Relu2, 2>(ta, tb, tc, P, st);
     if (epi == kEpiRelu2) return launch_gemm<kEpiRelu2, 2>(ta, tb, tc, P, st);
     return epi == kEpiMask ? launch_gemm<kEpiMask, 2>(ta, tb, tc, P, st)
                            : launch_gemm<kEpiNone, 2>(ta, tb, tc, P, st);
   }
+  if (epi == kEpiFp8) return launch_gemm<kEpiFp8, 1>(ta, tb, tc, P, st);
+  if (epi == kEpiFp8Relu2) return launch_gemm<kEpiFp8Relu2, 1>(ta, tb, tc, P, st);
   if (epi == kEpiRelu2) return launch_gemm<kEpiRelu2, 1>(ta, tb, tc, P, st);
   return epi == kEpiMask ? launch_gemm<kEpiMask, 1>(ta, tb, tc, P, st)
                          : launch_gemm<kEpiNone, 1>(ta, tb, tc, P, st);
@@ -723,5 +803,39 @@ extern "C" int bs_gemm_bf16_relu2(const void *A, int64_t lda, const void *B, int
   P.two_k = 2.0f * k;
   P.status = status;
   return gemm_run(A, lda, B, ldb, C, ldc, M, N, K, kEpiRelu2, P,
+                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bs_gemm_fp8(const void *A, int64_t lda, const void *Bt, int64_t ldb, void *C,
+                           int64_t ldc, int64_t M, int64_t N, int64_t K, const float *scale_a,
+                           const float *scale_b, int32_t *status, void *stream) {
+  if (!scale_a || !scale_b) return BS_ERR_ARG;
+  GemmParams P{};
+  P.scale_a = scale_a;
+  P.scale_b = scale_b;
+  P.status = status;
+  return gemm_run(A, lda, Bt, ldb, C, ldc, M, N, K, kEpiFp8, P,
+                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bs_gemm_fp8_relu2(const void *A, int64_t lda, const void *Bt, int64_t ldb,
+                                 void *C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                 const float *scale_a, const float *scale_b, const void *vals,
+                                 const uint8_t *bitmask, const uint32_t *prefix,
+                                 const int64_t *vals_offset, float k, const float *hscale,
+                                 int32_t *status, void *stream) {
+  if (!scale_a || !scale_b || !vals || !bitmask || !prefix || !vals_offset) return BS_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(vals) & 15) return BS_ERR_ALIGN;  // 16-byte staging loads
+  GemmParams P{};
+  P.scale_a = scale_a;
+  P.scale_b = scale_b;
+  P.mask = bitmask;
+  P.vals = static_cast<const uint16_t *>(vals);
+  P.prefix = prefix;
+  P.vals_offset = vals_offset;
+  P.two_k = 2.0f * k;
+  P.hscale = hscale;
+  P.status = status;
+  return gemm_run(A, lda, Bt, ldb, C, ldc, M, N, K, kEpiFp8Relu2, P,
                   static_cast<cudaStream_t>(stream));
 }

@@ -15,6 +15,8 @@ Two deliberate differences from the reference, both bug fixes:
 """
 from __future__ import annotations
 
+import os
+
 import torch
 from torch import Tensor
 from torch.autograd import Function
@@ -143,13 +145,57 @@ def _row_major_fp8(x: Tensor) -> Tensor:
     return x.contiguous()
 
 
+# FP8 GEMMs: "tcgen05" -- this library's kernels for every FP8 GEMM
+# (bs_gemm_fp8, and the fused ReLU^2 backward bs_gemm_fp8_relu2);
+# "cublaslt" -- F.scaled_mm throughout, as the reference; "hybrid" --
+# F.scaled_mm for the plain GEMMs and the fused kernel for the ReLU^2
+# backward.  BS_FP8_GEMM in the environment overrides the default.
+FP8_GEMM = os.environ.get("BS_FP8_GEMM", "cublaslt")
+
+
+def gemm_fp8(a: Tensor, bt: Tensor, a_scale: Tensor, b_scale: Tensor) -> Tensor | None:
+    """bf16(a @ bt.T * a_scale * b_scale) for e4m3 ``a`` [M, K] and ``bt``
+    [N, K] (both with unit column stride: the K-major operands of the
+    reference's scaled_mm call, lib_sparse/fp8.py:25-49) on the tcgen05
+    tensor cores (``kind::f8f6f4``, fp32 accumulation).  ``None`` when the
+    operands' alignment rules out the kernel (TMA needs 16-byte aligned bases
+    and row strides)."""
+    from . import _lib, _runtime as R
+
+    M, K = a.shape
+    N = bt.shape[0]
+    if (a.dtype != _FP8_DTYPE or bt.dtype != _FP8_DTYPE or a.stride(1) != 1
+            or bt.stride(1) != 1 or bt.shape[1] != K):
+        return None
+    lda = a.stride(0) if M > 1 else K
+    ldb = bt.stride(0) if N > 1 else K
+    if a.data_ptr() % 16 or bt.data_ptr() % 16 or lda % 16 or ldb % 16:
+        return None
+    out = torch.empty((M, N), device=a.device, dtype=torch.bfloat16)
+    sa = a_scale.reshape(()).to(torch.float32)
+    sb = b_scale.reshape(()).to(torch.float32)
+    rc = _lib.load().bs_gemm_fp8(a.data_ptr(), lda, bt.data_ptr(), ldb, out.data_ptr(), N,
+                                 M, N, K, sa.data_ptr(), sb.data_ptr(),
+                                 R.status_word(a.device).data_ptr(), R.stream_handle(a.device))
+    if rc == _lib.BS_ERR_ALIGN:
+        return None
+    _lib.check(rc, "bs_gemm_fp8")
+    return out
+
+
 def _scaled_mm(a: Tensor, b: Tensor, a_scale: Tensor, b_scale: Tensor,
                output_dtype: torch.dtype) -> Tensor:
-    """FP8 GEMM with tensor-wise scales (lib_sparse/fp8.py:25-49)."""
+    """FP8 GEMM with tensor-wise scales (lib_sparse/fp8.py:25-49): A
+    row-major, B column-major, on this library's tcgen05 kernel when
+    ``FP8_GEMM == "tcgen05"`` and the operands allow it, else cuBLASLt."""
     if a.stride(1) != 1:
         a = _row_major_fp8(a)
     if b.stride(0) != 1:
         b = _row_major_fp8(b.T).T
+    if FP8_GEMM == "tcgen05" and output_dtype == torch.bfloat16:
+        out = gemm_fp8(a, b.T, a_scale, b_scale)
+        if out is not None:
+            return out
     return F.scaled_mm(
         mat_a=a, mat_b=b,
         scale_a=a_scale, scale_b=b_scale, output_dtype=output_dtype,

@@ -16,7 +16,8 @@ from .config import RELU2_SCALE
 from .fp8 import is_fp8, matmul, to_fp8, to_fp8_layouts
 from .src.functions import dense_to_tilesparse, relu_to_tilesparse_fp8
 from .src.operators import (compress_bias_relu, compress_bias_relu_fp8, mask_with_bitmask_,
-                            matmul_relu2_grad, matmul_relu_mask, relu2_grad_sparse_)
+                            matmul_fp8_relu2_grad, matmul_relu2_grad, matmul_relu_mask,
+                            relu2_grad_sparse_)
 from .src.sparse_matmul import AspB, AspRelu2B
 
 
@@ -195,8 +196,15 @@ class Relu2Linear(Function):
             if grad_z is None:
                 grad_z = relu2_grad_sparse_(matmul(grad_output, W, False), h)
         elif want_z:
-            grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
-            grad_z = relu2_grad_sparse_(grad_h, h)
+            # FP8: one tcgen05 FP8 GEMM with the ReLU^2 gradient (and the
+            # stored tensor's scale) in its epilogue where it applies
+            from . import fp8 as F8
+            if F8.FP8_GEMM in ("tcgen05", "hybrid"):
+                _, w_col, w_scale = to_fp8_layouts(W, row=False, col=True)
+                grad_z = matmul_fp8_relu2_grad(grad_output, w_col.T, scale, w_scale, h)
+            if grad_z is None:
+                grad_h = matmul(grad_output, W, fp8=fp8, a_scale=scale)
+                grad_z = relu2_grad_sparse_(grad_h, h)
         grad_bias = grad_z.sum(0) if needs_bias else None
         return (grad_z if needs_z else None), grad_W2, None, None, None, grad_bias
 

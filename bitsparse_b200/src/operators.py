@@ -317,6 +317,45 @@ def matmul_relu2_grad(a: Tensor, b: Tensor, sparse: BitsparseTensor) -> Tensor |
     return out
 
 
+def matmul_fp8_relu2_grad(a: Tensor, bt: Tensor, a_scale: Tensor, b_scale: Tensor,
+                          sparse: BitsparseTensor) -> Tensor | None:
+    """``relu2_grad_sparse_(scaled_mm(a, bt.T), sparse)`` for e4m3 storage in
+    one tcgen05 FP8 GEMM (``kind::f8f6f4``): the ReLU^2 gradient ``grad * (2
+    k r)`` and the ``grad *= scale`` of the stored tensor's scale applied in
+    the epilogue (lib_sparse/layers.py:146-147 with the FP8 matmul of
+    lib_sparse/fp8.py:52-115), with the same roundings as the separate
+    steps on this library's FP8 GEMM.  ``a`` [M, K], ``bt`` [N, K] e4m3 with
+    unit column stride.  ``None`` when the path does not apply (packed or
+    non-e4m3 storage, alignment), and the caller uses the two steps."""
+    if (sparse.dtype != torch.float8_e4m3fn or sparse.pack_sbit
+            or a.dtype != torch.float8_e4m3fn or bt.dtype != torch.float8_e4m3fn):
+        return None
+    if a.dim() != 2 or bt.dim() != 2 or a.stride(1) != 1 or bt.stride(1) != 1:
+        return None
+    M, K = a.shape
+    N = bt.shape[0]
+    lda = a.stride(0) if M > 1 else K
+    ldb = bt.stride(0) if N > 1 else K
+    if (bt.shape[1] != K or tuple(sparse.shape) != (M, N) or sparse.vals.data_ptr() % 16
+            or a.data_ptr() % 16 or bt.data_ptr() % 16 or lda % 16 or ldb % 16):
+        return None
+    if (sparse.BLOCK_M, sparse.BLOCK_N) != (_BM, _BN):
+        return None
+    out = torch.empty((M, N), device=a.device, dtype=torch.bfloat16)
+    sa = a_scale.reshape(()).to(torch.float32)
+    sb = b_scale.reshape(()).to(torch.float32)
+    hs = None if sparse.scale is None else sparse.scale.reshape(()).to(torch.float32)
+    rc = _lib.load().bs_gemm_fp8_relu2(
+        a.data_ptr(), lda, bt.data_ptr(), ldb, out.data_ptr(), N, M, N, K, sa.data_ptr(),
+        sb.data_ptr(), sparse.vals.data_ptr(), sparse.bitmask.data_ptr(),
+        sparse.prefix.data_ptr(), sparse.vals_offset.data_ptr(), float(RELU2_SCALE),
+        R.ptr(hs), R.status_word(a.device).data_ptr(), _stream(a))
+    if rc == _lib.BS_ERR_ALIGN:
+        return None
+    _lib.check(rc, "bs_gemm_fp8_relu2")
+    return out
+
+
 def _fused_compress(fn, name: str, head: tuple, dev, stream: int, stored, M: int, N: int,
                     T: int, bitmask: Tensor, prefix: Tensor, sparse_data, pack_sbit: bool):
     """Run a fused compress entry point ``fn(*head, bitmask, prefix, vals,

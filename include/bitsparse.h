@@ -290,6 +290,33 @@ int bs_gemm_bf16_relu2(const void *A, int64_t lda, const void *B, int64_t ldb,
                        const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
                        const int64_t *vals_offset, float k, int32_t *status, void *stream);
 
+/* C[M, N] = bf16((A @ Bt^T) * (*scale_a) * (*scale_b)) for e4m3 operands on
+ * the tcgen05 tensor cores (kind::f8f6f4, fp32 accumulation): the FP8 GEMM
+ * with tensor-wise scales that MatmulFp8 issues through F.scaled_mm
+ * (lib_sparse/fp8.py:25-49, 52-115).  A [M, K] and Bt [N, K] (B column-major,
+ * as scaled_mm takes it) with unit column stride, row strides lda, ldb >= K
+ * bytes, multiples of 16, bases 16-byte aligned (BS_ERR_ALIGN otherwise);
+ * C bf16 row-major, row stride ldc >= N; scales device fp32 scalars. */
+int bs_gemm_fp8(const void *A, int64_t lda, const void *Bt, int64_t ldb, void *C,
+                int64_t ldc, int64_t M, int64_t N, int64_t K, const float *scale_a,
+                const float *scale_b, int32_t *status, void *stream);
+
+/* bs_gemm_fp8 with the ReLU^2 gradient of an e4m3-stored activation in the
+ * epilogue: g = bf16(acc * sa * sb) (the FP8 GEMM's output), then
+ * C[i, j] = bit ? bf16(float(bf16(g * 2 k r)) * (*hscale)) : +0, r the stored
+ * e4m3 value of the bitsparse [M, N] tensor (raw storage: `vals` 16-byte
+ * aligned, `bitmask`, `prefix`, device `vals_offset`) and hscale its
+ * per-tensor scale (NULL: no scaling).  The backward of Relu2Linear in FP8
+ * (lib_sparse/layers.py:146-147: grad_h = matmul(grad_output, W, fp8) then
+ * relu2_grad_sparse_, lib_sparse/src/triton_kernels.py:288-330 and the
+ * grad.mul_(scale) of lib_sparse/src/triton_operators.py:200-201) in one
+ * kernel.  Operands as bs_gemm_fp8. */
+int bs_gemm_fp8_relu2(const void *A, int64_t lda, const void *Bt, int64_t ldb, void *C,
+                      int64_t ldc, int64_t M, int64_t N, int64_t K, const float *scale_a,
+                      const float *scale_b, const void *vals, const uint8_t *bitmask,
+                      const uint32_t *prefix, const int64_t *vals_offset, float k,
+                      const float *hscale, int32_t *status, void *stream);
+
 /* Per-tensor fp8 scale of to_fp8 (lib_sparse/fp8.py:123-129):
  * *scale_out = max(amax(|x|) / 448, 1e-9), with the amax / 448 rounded to
  * bf16 for bf16 input (eager PyTorch semantics).  `amax_ws` is a device

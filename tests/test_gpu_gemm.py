@@ -102,3 +102,56 @@ def test_relu2_epilogue_extreme_values():
     finite = torch.isfinite(two.float()) | torch.isinf(two.float())
     assert torch.equal(out[finite], two[finite])
     B.check_status()
+
+
+@pytest.mark.parametrize("M, N, K", [(128, 256, 128), (256, 512, 256), (200, 304, 96),
+                                     (1000, 776, 768), (3, 8, 16), (4096, 4096, 4096)])
+def test_fp8_gemm_matches_fp32_reference(M, N, K):
+    """The tcgen05 FP8 GEMM (kind::f8f6f4) against an fp32 restatement of
+    the reference's tensor-wise scaled product, (a * sa) @ (b * sb)
+    (lib_sparse/fp8.py:25-49), within RTOL, and against cuBLASLt's
+    F.scaled_mm on the same operands."""
+    import torch.nn.functional as F
+    from bitsparse_b200.fp8 import gemm_fp8
+    g = torch.Generator(device="cuda").manual_seed(M + 3 * N + K)
+    a = (torch.randn(M, K, generator=g, device="cuda") * 3).to(torch.float8_e4m3fn)
+    bt = (torch.randn(N, K, generator=g, device="cuda") * 3).to(torch.float8_e4m3fn)
+    sa = torch.tensor(0.37, device="cuda")
+    sb = torch.tensor(1.9e-2, device="cuda")
+    out = gemm_fp8(a, bt, sa, sb)
+    assert out is not None and out.dtype == torch.bfloat16 and out.shape == (M, N)
+    ref = (a.float() * sa) @ (bt.float() * sb).T
+    err = (out.float() - ref).abs().max().item()
+    assert err <= RTOL * ref.abs().max().item(), (err, ref.abs().max().item())
+    if M % 16 == 0 and N % 16 == 0:
+        cub = F.scaled_mm(a, bt.T, scale_a=sa, scale_b=sb, output_dtype=torch.bfloat16,
+                          scale_recipe_a=F.ScalingType.TensorWise,
+                          scale_recipe_b=F.ScalingType.TensorWise)
+        assert (out.float() - cub.float()).abs().max().item() <= RTOL * ref.abs().max().item()
+    B.check_status()
+
+
+@pytest.mark.parametrize("M, N, K", [(256, 512, 256), (200, 304, 96), (2048, 3072, 768)])
+@pytest.mark.parametrize("scaled", [False, True])
+def test_fp8_relu2_epilogue_equals_two_steps(M, N, K, scaled):
+    """The FP8 GEMM with the ReLU^2 gradient of an e4m3-stored activation in
+    its epilogue == the same FP8 GEMM followed by relu2_grad_sparse_ (which
+    also applies the stored tensor's scale), bit for bit."""
+    from bitsparse_b200.fp8 import gemm_fp8, to_fp8
+    from bitsparse_b200.src.operators import matmul_fp8_relu2_grad, relu2_grad_sparse_
+    g = torch.Generator(device="cuda").manual_seed(5 * M + N)
+    a = (torch.randn(M, K, generator=g, device="cuda") * 3).to(torch.float8_e4m3fn)
+    bt = (torch.randn(N, K, generator=g, device="cuda") * 3).to(torch.float8_e4m3fn)
+    sa, sb = torch.tensor(0.21, device="cuda"), torch.tensor(0.033, device="cuda")
+    h = (torch.randn(M, N, generator=g, device="cuda") - 0.5).relu().to(torch.bfloat16)
+    if scaled:
+        hq, hs = to_fp8(h)
+    else:
+        hq, hs = h.to(torch.float8_e4m3fn), None
+    sp = dense_to_tilesparse(hq, hs)
+    out = matmul_fp8_relu2_grad(a, bt, sa, sb, sp)
+    assert out is not None
+    two = relu2_grad_sparse_(gemm_fp8(a, bt, sa, sb), sp)
+    assert torch.equal(out, two)
+    assert torch.all(out[hq.float() == 0] == 0)
+    B.check_status()
