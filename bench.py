@@ -617,7 +617,7 @@ def _max_over_ranks(v: float, world: int, dev) -> float:
     return t.item()
 
 
-def dp_train(dev, world, rank, compressed, steps=4, warmup=2):
+def dp_train(dev, world, rank, compressed, steps=4, warmup=2, arena_fraction=0.0):
     """Config 5: one data-parallel training step (forward, backward with the
     gradients summed over the ranks by NCCL all-reduce overlapped with the
     backward pass, AdamW) of the 24-layer d1024 decoder on a global batch of
@@ -630,7 +630,7 @@ def dp_train(dev, world, rank, compressed, steps=4, warmup=2):
     from bitsparse_b200.decoder import Decoder, DecoderConfig
     from bitsparse_b200.distributed import GradAllReduce
 
-    cfg = DecoderConfig(compressed=compressed)
+    cfg = DecoderConfig(compressed=compressed, arena_fraction=arena_fraction)
     torch.manual_seed(0)  # the same initial weights on every rank
     model = Decoder(cfg).to(device=dev, dtype=torch.bfloat16)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-5, fused=True)
@@ -672,8 +672,14 @@ def dp_train(dev, world, rank, compressed, steps=4, warmup=2):
     e1.record()
     torch.cuda.synchronize()
     ms = _max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+    arena_mb = 0.0
+    if model.arena is not None:  # preallocated, so outside fwd_peak: count it here
+        import bitsparse_b200 as B_
+        B_.check_status(dev)  # no capacity overflow
+        arena_mb = model.arena.vals.numel() * model.arena.vals.element_size() / 2**20
     out = {"tokens_per_s": B * world * cfg.seq / ms * 1e3, "ms_per_step": ms,
-           "local_batch": B, "peak_forward_mem_mb": fwd_peak / 2**20,
+           "local_batch": B, "peak_forward_mem_mb": fwd_peak / 2**20 + arena_mb,
+           "arena_mb": arena_mb,
            "loss_per_token": float(last.item()) / (B * cfg.seq)}
     if red is not None:
         red.remove()
@@ -739,10 +745,17 @@ def train_suite(dev, world, rank):
     compressed vs dense MLP activations) and config 4 token-sharded."""
     out = {"scaling": "strong (global batch fixed)", "world": world}
     out["config5_dp_decoder_compressed"] = dp_train(dev, world, rank, True)
+    # the same with one TensorBuffer arena for every layer's values (sized
+    # for 60% density: random-init ReLU activations are about 50% dense)
+    out["config5_dp_decoder_compressed_arena"] = dp_train(dev, world, rank, True,
+                                                          arena_fraction=0.6)
     out["config5_dp_decoder_dense"] = dp_train(dev, world, rank, False)
-    c, dn = out["config5_dp_decoder_compressed"], out["config5_dp_decoder_dense"]
-    out["config5_speedup_vs_dense"] = c["tokens_per_s"] / dn["tokens_per_s"]
-    out["config5_activation_mem_ratio"] = c["peak_forward_mem_mb"] / dn["peak_forward_mem_mb"]
+    dn = out["config5_dp_decoder_dense"]
+    for k in ("", "_arena"):
+        c = out["config5_dp_decoder_compressed" + k]
+        out["config5_speedup_vs_dense" + k] = c["tokens_per_s"] / dn["tokens_per_s"]
+        out["config5_activation_mem_ratio" + k] = (c["peak_forward_mem_mb"]
+                                                   / dn["peak_forward_mem_mb"])
     out["config4_token_sharded_relu2_fp8"] = c4_sharded(dev, world, rank)
     return out
 

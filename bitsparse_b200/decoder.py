@@ -33,6 +33,11 @@ class DecoderConfig:
     mlp: int = 4096
     seq: int = 1024
     compressed: bool = True
+    # compressed MLP activations kept in one TensorBuffer arena shared by all
+    # layers (no host sync per layer) holding this fraction of the dense
+    # activations' values; 0: each layer allocates its own exact storage
+    # (one host sync per layer, the reference's default)
+    arena_fraction: float = 0.0
 
 
 class _Block(nn.Module):
@@ -47,20 +52,20 @@ class _Block(nn.Module):
         self.fc = nn.Linear(d, h)      # W1 [mlp, dim]
         self.fc_out = nn.Linear(h, d)  # W2 [dim, mlp]
 
-    def _mlp(self, x: Tensor) -> Tensor:
+    def _mlp(self, x: Tensor, arena) -> Tensor:
         W1, b1, W2, b2 = self.fc.weight, self.fc.bias, self.fc_out.weight, self.fc_out.bias
         if self.cfg.compressed:
-            return FFNRelu.apply(x, W1, W2, b1, b2)
+            return FFNRelu.apply(x, W1, W2, b1, b2, sparse_data=arena)
         return F.linear(torch.relu(F.linear(x, W1, b1)), W2, b2)
 
-    def forward(self, x: Tensor) -> Tensor:
+    def forward(self, x: Tensor, arena=None) -> Tensor:
         B, T, D = x.shape
         H = self.cfg.heads
         q, k, v = self.qkv(self.norm1(x)).view(B, T, 3, H, D // H).unbind(2)
         y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
                                            v.transpose(1, 2), is_causal=True)
         x = x + self.proj(y.transpose(1, 2).reshape(B, T, D))
-        return x + self._mlp(self.norm2(x))
+        return x + self._mlp(self.norm2(x), arena)
 
 
 class Decoder(nn.Module):
@@ -79,12 +84,27 @@ class Decoder(nn.Module):
         for m in self.modules():
             if isinstance(m, nn.RMSNorm):
                 nn.init.ones_(m.weight)
+        self.arena = None
+
+    def _arena(self, tokens: int, device, dtype):
+        """The shared value arena (allocated on first use, reset per step)."""
+        from .bitsparse import TensorBuffer
+        cfg = self.cfg
+        if not cfg.compressed or cfg.arena_fraction <= 0:
+            return None
+        elt = torch.empty((), dtype=dtype).element_size()
+        n = int(cfg.arena_fraction * cfg.layers * tokens * cfg.mlp)
+        if self.arena is None or self.arena.vals.numel() < n:
+            self.arena = TensorBuffer(n * elt, device=device, dtype=dtype)
+        self.arena.offset.zero_()
+        return self.arena
 
     def forward(self, tokens: Tensor, targets: Tensor) -> Tensor:
         T = tokens.shape[1]
         x = self.embed(tokens) + self.pos.weight[:T]
+        arena = self._arena(tokens.numel(), x.device, x.dtype)
         for blk in self.blocks:
-            x = blk(x)
+            x = blk(x, arena)
         logits = self.head(self.norm(x)).float()
         return F.cross_entropy(logits.view(-1, logits.shape[-1]), targets.reshape(-1),
                                reduction="sum")
