@@ -812,6 +812,77 @@ def gemm_case():
     print("gemm case ok")
 
 
+def kernel_cases(which: str):
+    """Small ncu capture cases of the kernels added beside K1 / K2 / K3:
+    "fp8" -- the tcgen05 FP8 GEMM at 8192^3 (e4m3, tensor-wise scales);
+    "relu2" -- the bf16 GEMM with the ReLU^2 gradient in its epilogue at the
+    config-2 backward shape (8192 x 768 @ 768 x 3072, h 84% sparse);
+    "sparse_recon" -- the persistent reconstruct of an [8192, 8192] bf16
+    tensor at 99% sparsity (the sparse-chunk scatter path).  Each runs its
+    kernel twice and checks the result."""
+    import torch
+    from bitsparse_b200 import TensorBuffer
+    from bitsparse_b200.src.functions import dense_to_tilesparse
+    from bitsparse_b200.src.operators import (matmul_relu2_grad, matmul_relu_mask,
+                                              relu2_grad_sparse_, unpack_batch_)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    if which == "fp8":
+        from bitsparse_b200.fp8 import gemm_fp8
+        n = 8192
+        a = torch.randn(n, n, generator=g, device=dev).to(torch.float8_e4m3fn)
+        bt = torch.randn(n, n, generator=g, device=dev).to(torch.float8_e4m3fn)
+        s1 = torch.tensor(1.0, device=dev)
+        for _ in range(2):
+            out = gemm_fp8(a, bt, s1, s1)
+        ref = a[:256].float() @ bt.float().T
+        if (out[:256].float() - ref).abs().max() > 1e-2 * ref.abs().max():
+            raise RuntimeError("fp8 gemm case mismatch")
+        import torch.nn.functional as F
+
+        def ev(fn, k=20):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(k):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / k * 1e3
+
+        ours = ev(lambda: gemm_fp8(a, bt, s1, s1))
+        cub = ev(lambda: F.scaled_mm(a, bt.T, scale_a=s1, scale_b=s1, output_dtype=torch.bfloat16,
+                                     scale_recipe_a=F.ScalingType.TensorWise,
+                                     scale_recipe_b=F.ScalingType.TensorWise))
+        fl = 2.0 * n ** 3
+        print(f"fp8 {n}^3: tcgen05 {ours:.1f} us ({fl / ours / 1e6:.0f} TFLOP/s), "
+              f"cuBLASLt scaled_mm {cub:.1f} us ({fl / cub / 1e6:.0f} TFLOP/s)")
+    elif which == "relu2":
+        M, N, K = 8192, 3072, 768
+        a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        b = torch.randn(K, N, generator=g, device=dev).to(torch.bfloat16)
+        h = (torch.randn(M, N, generator=g, device=dev) - 1.0).relu().to(torch.bfloat16)
+        sp = dense_to_tilesparse(h, None)
+        for _ in range(2):
+            out = matmul_relu2_grad(a, b, sp)
+        if not torch.equal(out, relu2_grad_sparse_(matmul_relu_mask(a, b), sp)):
+            raise RuntimeError("relu2 gemm case mismatch")
+    else:
+        M = N = 8192
+        x = make_relu_bf16(M, N, -2.3263, 0, dev)
+        buf = TensorBuffer(M * N * 2, device=dev, dtype=torch.bfloat16)
+        sp = dense_to_tilesparse(x, None, buf)
+        out = torch.empty_like(x)
+        for _ in range(2):
+            unpack_batch_(sp, out, 0, sp.grid_n, N, M, sp.grid_m * sp.grid_n)
+        if not torch.equal(out, x):
+            raise RuntimeError("sparse reconstruct case mismatch")
+    torch.cuda.synchronize()
+    print(which, "case ok")
+
+
 def profile_case():
     """Small case for ncu captures: compress + reconstruct of one [8192, 8192]
     bf16 relu(N(0,1)) tensor (134 MB, above L2) into a TensorBuffer, 3 times."""
@@ -852,6 +923,8 @@ def main():
                     help="run only the sparse-MLP fwd+bwd comparison (configs 2 and 4)")
     ap.add_argument("--gemm-case", action="store_true",
                     help="run only the small ncu capture case of the masked tcgen05 GEMM")
+    ap.add_argument("--kernel-case", choices=["fp8", "relu2", "sparse_recon"],
+                    help="run only a small ncu capture case of that kernel and exit")
     ap.add_argument("--profile-case", action="store_true",
                     help="run only the small ncu capture case and exit")
     args = ap.parse_args()
@@ -860,6 +933,9 @@ def main():
         return
     if args.profile_case:
         profile_case()
+        return
+    if args.kernel_case:
+        kernel_cases(args.kernel_case)
         return
     if args.mlp_only:
         import torch

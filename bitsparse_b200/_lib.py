@@ -15,6 +15,7 @@ BS_OK, BS_ERR_SHAPE, BS_ERR_DTYPE, BS_ERR_ALIGN, BS_ERR_CAPACITY = 0, 1, 2, 3, 4
 BS_ERR_LAUNCH, BS_ERR_ARG, BS_ERR_WORKSPACE, BS_ERR_TOO_LARGE = 5, 6, 7, 8
 BS_STATUS_CAPACITY, BS_STATUS_TIMEOUT = 1, 2
 BS_BF16, BS_E4M3, BS_E5M2, BS_F32 = 0, 1, 2, 3
+BS_FP8_COMPILED = 0x100
 
 _ERRORS = {
     BS_ERR_SHAPE: "bad shape",
@@ -39,8 +40,9 @@ _SIGS = {
                                    _i32, _vp, _vp, _vp, _vp, _vp]),
     "bs_compress_noalloc_max_tiles": (_sz, []),
     "bs_compress_bias_relu_fp8": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
-                                         _vp, _i64, _i32, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
-    "bs_fp8_scales_bias_relu": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+                                         _vp, _i64, _i32, _vp, _vp, _vp, _vp, _sz, _i32, _vp,
+                                         _vp]),
+    "bs_fp8_scales_bias_relu": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i32, _vp]),
     "bs_compress_bias_relu": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _i64,
                                      _i32, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     "bs_transpose_b8": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
@@ -59,9 +61,10 @@ _SIGS = {
                          _i64, _i32, _vp, _vp]),
     "bs_mask_with_bitmask": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp]),
     "bs_unpack_status": (_i32, [_vp, _i32]),
-    "bs_quantize_e4m3_2d": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp]),
+    "bs_quantize_e4m3_2d": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _i32,
+                                   _vp]),
     "bs_unpack_relu2_fp8t": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _vp, C.c_float, _vp,
-                                    _vp, _vp, _i64, _vp]),
+                                    _vp, _vp, _i64, _i32, _vp]),
     "bs_relu2_grad": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i32, _i32, _vp,
                              _vp]),
     "bs_fp8_scale": (_i32, [_vp, _i32, _i64, _vp, _vp, _vp]),

@@ -223,6 +223,34 @@ __device__ __forceinline__ void div_e4m3x8(const uint32_t (&w)[4], float s, floa
 
 // torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;
 // -0 and NaN unchanged.
+// 1/448 rounded to fp32: the compiled to_fp8 computes amax / 448 as
+// amax * (1/448), the reciprocal of the constant taken once.
+constexpr float kRcp448 = 1.0f / 448.0f;
+
+// The fp32 division of Triton's `/` operator (PTX div.full.f32, an
+// approximate full-range division): the quotient the reference's compiled
+// to_fp8 computes.
+__device__ __forceinline__ float div_full(float x, float s) {
+  float q;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(q) : "f"(x), "f"(s));
+  return q;
+}
+
+// to_fp8's quantiser as the reference runs it on a GPU: its to_fp8 is
+// @torch.compile'd (lib_sparse/fp8.py:123-129), and the generated Triton
+// code divides the fp32 value by the scale with Triton's division and casts
+// the quotient to e4m3 -- no rounding of the quotient to bf16 as eager
+// PyTorch does.  Eight bf16 values (four words, low half first) -> two
+// words of codes.
+__device__ __forceinline__ void full_e4m3x8(const uint32_t (&w)[4], float s, uint32_t (&o)[2]) {
+  o[0] = o[1] = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float x = __uint_as_float((w[e >> 1] >> (16 * (e & 1))) << 16);
+    o[e >> 2] |= f32_to_e4m3_bits(div_full(x, s)) << (8 * (e & 3));
+  }
+}
+
 __device__ __forceinline__ uint32_t relu_bf16x2(uint32_t w) {
   const uint32_t v = w & 0x7FFF7FFFu;
   const uint32_t nz = v + 0x7FFF7FFFu;   // bit 15 of a half set iff v != 0

@@ -72,6 +72,7 @@ struct CompressParams {
   const uint8_t *dense;
   int64_t M, N, ld;
   const float *qscale;
+  int qcompiled;  // quantise as the reference's compiled to_fp8 (BS_FP8_COMPILED)
   uint8_t *qout;
   uint8_t *bitmask;
   uint32_t *prefix;
@@ -206,14 +207,16 @@ __device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64
       for (int g = 0; g < C::VEC / 8; ++g) {
         const uint32_t w4[4] = {raw[4 * g], raw[4 * g + 1], raw[4 * g + 2], raw[4 * g + 3]};
         uint32_t o2[2];
-        div_e4m3x8(w4, qs, r, o2);
+        if (P.qcompiled) full_e4m3x8(w4, qs, o2);
+        else div_e4m3x8(w4, qs, r, o2);
         sv[2 * g] = o2[0];
         sv[2 * g + 1] = o2[1];
       }
     } else {
 #pragma unroll
       for (int e = 0; e < C::VEC; ++e) {
-        const float y = __fdiv_rn(__uint_as_float(raw[e]), qs);
+        const float y = P.qcompiled ? div_full(__uint_as_float(raw[e]), qs)
+                                    : __fdiv_rn(__uint_as_float(raw[e]), qs);
         sv[e >> 2] |= f32_to_e4m3_bits(y) << (8 * (e & 3));
       }
     }
@@ -924,7 +927,10 @@ __global__ void __launch_bounds__(NW * 32, MINB)
           }
           if constexpr (QUANT) {
             uint32_t qw[2] = {0, 0}, side[2];
-            if constexpr (BIAS) {
+            if (P.qcompiled) {
+              const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
+              full_e4m3x8(h4, qs, qw);
+            } else if constexpr (BIAS) {
               const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
               div_e4m3x8(h4, qs, qr, qw);
             } else {
@@ -947,7 +953,8 @@ __global__ void __launch_bounds__(NW * 32, MINB)
                   const float h1 = bf16_bits_to_f32(v[s4][i] >> 16);
                   sq[i] = bf16x2_from_f32(h0 * h0, h1 * h1);  // h.square_()
                 }
-                div_e4m3x8(sq, qs2, qr2, side);
+                if (P.qcompiled) full_e4m3x8(sq, qs2, side);
+                else div_e4m3x8(sq, qs2, qr2, side);
               }
             }
             v[s4][0] = qw[0]; v[s4][1] = qw[1];
@@ -1315,6 +1322,7 @@ static int setup_compress(CompressParams &P, const void *dense, int in_dtype, in
   if (reinterpret_cast<uintptr_t>(workspace) & 15) return BS_ERR_ALIGN;
   P.qscale = quant_scale;
   P.qout = quant_out;
+  P.qcompiled = 0;
   P.qout_vec = quant_out && ((reinterpret_cast<uintptr_t>(quant_out) & 15) == 0) &&
                (N % 16 == 0);
   P.bitmask = bitmask;
@@ -1340,11 +1348,14 @@ extern "C" int bs_compress(const void *dense, int in_dtype, int64_t M, int64_t N
                            int64_t *arena_offset, int64_t *vals_offset_out, int64_t *nnz_out,
                            void *workspace, size_t workspace_bytes, int32_t *status,
                            void *stream) {
+  const int qcompiled = (in_dtype & BS_FP8_COMPILED) != 0;
+  in_dtype &= ~BS_FP8_COMPILED;
   CompressParams P{};
   const int rc = setup_compress(P, dense, in_dtype, M, N, ld, quant_scale, quant_out, bitmask,
                                 prefix, vals, vals_capacity, pack_sbit, arena_offset,
                                 vals_offset_out, nnz_out, workspace, workspace_bytes, status);
   if (rc) return rc;
+  P.qcompiled = qcompiled;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (P.num_tiles == 0) {
     // Empty tensor: prefix = [0]; arena offset, vals_offset_out, nnz_out untouched.
@@ -1394,8 +1405,8 @@ extern "C" int bs_compress_bias_relu_fp8(const void *z, int64_t M, int64_t N, in
                                          int64_t vals_capacity, int pack_sbit,
                                          int64_t *arena_offset, int64_t *vals_offset_out,
                                          int64_t *nnz_out, void *workspace,
-                                         size_t workspace_bytes, int32_t *status,
-                                         void *stream) {
+                                         size_t workspace_bytes, int fp8_flags,
+                                         int32_t *status, void *stream) {
   CompressParams P{};
   if (!scale_h) return BS_ERR_ARG;
   int rc = setup_compress(P, z, BS_BF16, M, N, ld, scale_h, side_out, bitmask, prefix, vals,
@@ -1406,6 +1417,7 @@ extern "C" int bs_compress_bias_relu_fp8(const void *z, int64_t M, int64_t N, in
   if (reinterpret_cast<uintptr_t>(bias) & 15) return BS_ERR_ALIGN;
   P.bias = static_cast<const uint8_t *>(bias);
   P.qscale2 = scale_side;
+  P.qcompiled = (fp8_flags & BS_FP8_COMPILED) != 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (P.num_tiles == 0) {
     if (cudaMemsetAsync(prefix, 0, sizeof(uint32_t), st) != cudaSuccess) return BS_ERR_LAUNCH;
@@ -1505,6 +1517,8 @@ extern "C" int bs_compress_noalloc(const void *dense, int in_dtype, int64_t M, i
                                    int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
                                    int64_t *vals_offset_out, int64_t *nnz_out, int32_t *status,
                                    void *stream) {
+  const int qcompiled = (in_dtype & BS_FP8_COMPILED) != 0;
+  in_dtype &= ~BS_FP8_COMPILED;
   if (M < 0 || N < 0) return BS_ERR_SHAPE;
   const int64_t gm = (M + kTileM - 1) / kTileM, gn = (N + kTileN - 1) / kTileN;
   // bound the factors one at a time: their product could wrap
@@ -1519,6 +1533,7 @@ extern "C" int bs_compress_noalloc(const void *dense, int in_dtype, int64_t M, i
                       vals_capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out, scratch,
                       kNoAllocScratchBytes, status);
   if (rc) return rc;
+  P.qcompiled = qcompiled;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (P.num_tiles == 0) {
     if (cudaMemsetAsync(prefix, 0, sizeof(uint32_t), st) != cudaSuccess) return BS_ERR_LAUNCH;

@@ -1,8 +1,10 @@
 // to_fp8 on the GPU: per-tensor amax -> scale, and the e4m3 quantiser
-// (lib_sparse/fp8.py:123-129).  Both follow eager PyTorch's arithmetic for a
-// bf16 / fp32 tensor: scale = max(amax / 448, 1e-9) with the quotient
-// rounded to the input dtype, q = e4m3(x / scale) with the quotient rounded
-// to the input dtype first.
+// (lib_sparse/fp8.py:123-129), in either of two arithmetics: eager
+// PyTorch's for a bf16 / fp32 tensor (scale = max(amax / 448, 1e-9) with the
+// quotient rounded to the input dtype, q = e4m3(x / scale) with the quotient
+// rounded to the input dtype first), or -- `compiled` -- that of the
+// reference's @torch.compile'd to_fp8 on a GPU (scale = max(amax * (1/448),
+// 1e-9) in fp32, q = e4m3(x / scale) with Triton's fp32 division).
 #include "common.cuh"
 
 namespace bs {
@@ -52,10 +54,12 @@ amax_kernel(const uint8_t *x, int64_t n, uint32_t *amax_ws) {
 
 // Finalise the scale and reset the scratch word for the next call.
 template <int DT>
-__global__ void scale_kernel(uint32_t *amax_ws, float *scale_out) {
+__global__ void scale_kernel(uint32_t *amax_ws, float *scale_out, int compiled) {
   const float amax = __uint_as_float(*amax_ws);
-  float s = __fdiv_rn(amax, 448.0f);
-  if constexpr (DT == BS_BF16) s = bf16_bits_to_f32(f32_to_bf16_bits(s));
+  // eager divides by 448; the compiled function multiplies by 1/448 rounded
+  // to fp32 (Inductor's rewrite of a division by a constant)
+  float s = compiled ? amax * kRcp448 : __fdiv_rn(amax, 448.0f);
+  if (DT == BS_BF16 && !compiled) s = bf16_bits_to_f32(f32_to_bf16_bits(s));
   *scale_out = fmaxf(s, 1e-9f);  // clamp(min=1e-9)
   *amax_ws = 0u;
 }
@@ -117,13 +121,16 @@ amax_bias_relu_kernel(const uint8_t *z, int64_t M, int64_t N, int64_t ld, const 
 // a non-decreasing function of h >= 0 and rounding is monotonic, so
 // amax(h2) = bf16(amax(h)^2) exactly; both scales follow scale_kernel's
 // bf16 rule.  Resets the scratch word.
-__global__ void scales_relu2_kernel(uint32_t *amax_ws, float *scale_h, float *scale_h2) {
+__global__ void scales_relu2_kernel(uint32_t *amax_ws, float *scale_h, float *scale_h2,
+                                    int compiled) {
   const float amax = __uint_as_float(*amax_ws);
-  float s = bf16_bits_to_f32(f32_to_bf16_bits(__fdiv_rn(amax, 448.0f)));
+  float s = compiled ? amax * kRcp448 : __fdiv_rn(amax, 448.0f);
+  if (!compiled) s = bf16_bits_to_f32(f32_to_bf16_bits(s));
   *scale_h = fmaxf(s, 1e-9f);
   if (scale_h2) {
     const float a2 = bf16_bits_to_f32(f32_to_bf16_bits(amax * amax));
-    s = bf16_bits_to_f32(f32_to_bf16_bits(__fdiv_rn(a2, 448.0f)));
+    s = compiled ? a2 * kRcp448 : __fdiv_rn(a2, 448.0f);
+    if (!compiled) s = bf16_bits_to_f32(f32_to_bf16_bits(s));
     *scale_h2 = fmaxf(s, 1e-9f);
   }
   *amax_ws = 0u;
@@ -132,7 +139,7 @@ __global__ void scales_relu2_kernel(uint32_t *amax_ws, float *scale_h, float *sc
 // q = e4m3(x / scale) over a flat tensor (the quantise half of to_fp8).
 template <int DT>
 __global__ void __launch_bounds__(kThreads)
-quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q) {
+quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q, int compiled) {
   const float s = *scale;
   const float r = __frcp_rn(s);
   const int64_t stride = (int64_t)gridDim.x * kThreads;
@@ -166,11 +173,12 @@ quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q) {
       // fast e4m3 conversion applies (NaN stays NaN).
       const uint32_t w4[4] = {b[0] | b[1] << 16, b[2] | b[3] << 16, b[4] | b[5] << 16,
                               b[6] | b[7] << 16};
-      div_e4m3x8(w4, s, r, o);
+      if (compiled) full_e4m3x8(w4, s, o);
+      else div_e4m3x8(w4, s, r, o);
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float y = __fdiv_rn(__uint_as_float(b[e]), s);
+        const float y = compiled ? div_full(__uint_as_float(b[e]), s) : __fdiv_rn(__uint_as_float(b[e]), s);
         o[e >> 2] |= f32_to_e4m3_bits(y) << (8 * (e & 3));
       }
     }
@@ -191,7 +199,8 @@ quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q) {
 // shared memory.
 __global__ void __launch_bounds__(kThreads)
 quant2d_kernel(const uint8_t *x, int64_t R, int64_t C, int64_t ld, const float *scale,
-               uint8_t *q, int64_t ldq, uint8_t *qT, int64_t ldqT, int vx, int vq, int vqT) {
+               uint8_t *q, int64_t ldq, uint8_t *qT, int64_t ldqT, int vx, int vq, int vqT,
+               int compiled) {
   __shared__ uint8_t t[64][64 + 4];
   const float s = *scale;
   const float rc = __frcp_rn(s);
@@ -218,9 +227,11 @@ quant2d_kernel(const uint8_t *x, int64_t R, int64_t C, int64_t ld, const float *
     {
       const uint32_t lo[4] = {w[0], w[1], w[2], w[3]}, hi[4] = {w[4], w[5], w[6], w[7]};
       uint32_t o2[2];
-      div_e4m3x8(lo, s, rc, o2);
+      if (compiled) full_e4m3x8(lo, s, o2);
+      else div_e4m3x8(lo, s, rc, o2);
       o[0] = o2[0]; o[1] = o2[1];
-      div_e4m3x8(hi, s, rc, o2);
+      if (compiled) full_e4m3x8(hi, s, o2);
+      else div_e4m3x8(hi, s, rc, o2);
       o[2] = o2[0]; o[3] = o2[1];
     }
     if (q != nullptr && gr < R) {
@@ -308,6 +319,8 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 extern "C" int bs_fp8_scale(const void *x, int dtype, int64_t numel, uint32_t *amax_ws,
                             float *scale_out, void *stream) {
+  const int compiled = (dtype & BS_FP8_COMPILED) != 0;
+  dtype &= ~BS_FP8_COMPILED;
   if (dtype != BS_BF16 && dtype != BS_F32) return BS_ERR_DTYPE;
   if (numel < 0) return BS_ERR_SHAPE;
   if (!amax_ws || !scale_out || (numel > 0 && !x)) return BS_ERR_ARG;
@@ -320,17 +333,17 @@ extern "C" int bs_fp8_scale(const void *x, int dtype, int64_t numel, uint32_t *a
   const uint8_t *xb = static_cast<const uint8_t *>(x);
   if (dtype == BS_BF16) {
     amax_kernel<BS_BF16><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, amax_ws);
-    scale_kernel<BS_BF16><<<1, 1, 0, st>>>(amax_ws, scale_out);
+    scale_kernel<BS_BF16><<<1, 1, 0, st>>>(amax_ws, scale_out, compiled);
   } else {
     amax_kernel<BS_F32><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, amax_ws);
-    scale_kernel<BS_F32><<<1, 1, 0, st>>>(amax_ws, scale_out);
+    scale_kernel<BS_F32><<<1, 1, 0, st>>>(amax_ws, scale_out, compiled);
   }
   return launch_err();
 }
 
 extern "C" int bs_fp8_scales_bias_relu(const void *z, int64_t M, int64_t N, int64_t ld,
                                        const void *bias, uint32_t *amax_ws, float *scale_h,
-                                       float *scale_h2, void *stream) {
+                                       float *scale_h2, int fp8_flags, void *stream) {
   if (M < 0 || N < 0 || ld < N) return BS_ERR_SHAPE;
   if (!amax_ws || !scale_h || !bias || (M > 0 && N > 0 && !z)) return BS_ERR_ARG;
   if (!aligned16(z) || !aligned16(bias)) return BS_ERR_ALIGN;
@@ -340,12 +353,15 @@ extern "C" int bs_fp8_scales_bias_relu(const void *z, int64_t M, int64_t N, int6
   if (blocks < 1) blocks = 1;
   amax_bias_relu_kernel<<<(unsigned)blocks, kThreads, 0, st>>>(
       static_cast<const uint8_t *>(z), M, N, ld, static_cast<const uint8_t *>(bias), amax_ws);
-  scales_relu2_kernel<<<1, 1, 0, st>>>(amax_ws, scale_h, scale_h2);
+  scales_relu2_kernel<<<1, 1, 0, st>>>(amax_ws, scale_h, scale_h2,
+                                       (fp8_flags & BS_FP8_COMPILED) != 0);
   return launch_err();
 }
 
 extern "C" int bs_quantize_e4m3(const void *x, int dtype, int64_t numel, const float *scale,
                                 uint8_t *q, void *stream) {
+  const int compiled = (dtype & BS_FP8_COMPILED) != 0;
+  dtype &= ~BS_FP8_COMPILED;
   if (dtype != BS_BF16 && dtype != BS_F32) return BS_ERR_DTYPE;
   if (numel < 0) return BS_ERR_SHAPE;
   if (numel == 0) return BS_OK;
@@ -355,8 +371,10 @@ extern "C" int bs_quantize_e4m3(const void *x, int dtype, int64_t numel, const f
   if (blocks > 148 * 16) blocks = 148 * 16;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint8_t *xb = static_cast<const uint8_t *>(x);
-  if (dtype == BS_BF16) quant_kernel<BS_BF16><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, scale, q);
-  else quant_kernel<BS_F32><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, scale, q);
+  if (dtype == BS_BF16)
+    quant_kernel<BS_BF16><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, scale, q, compiled);
+  else
+    quant_kernel<BS_F32><<<(unsigned)blocks, kThreads, 0, st>>>(xb, numel, scale, q, compiled);
   return launch_err();
 }
 
@@ -378,7 +396,7 @@ extern "C" const char *bs_version(void) { return "bitsparse_b200 0.1 sm_100a"; }
 
 extern "C" int bs_quantize_e4m3_2d(const void *x, int64_t R, int64_t C, int64_t ld,
                                    const float *scale, uint8_t *q, int64_t ldq, uint8_t *qT,
-                                   int64_t ldqT, void *stream) {
+                                   int64_t ldqT, int fp8_flags, void *stream) {
   if (R < 0 || C < 0 || ld < C || (q && ldq < C) || (qT && ldqT < R)) return BS_ERR_SHAPE;
   if (R == 0 || C == 0 || (!q && !qT)) return BS_OK;
   if (!x || !scale) return BS_ERR_ARG;
@@ -388,6 +406,7 @@ extern "C" int bs_quantize_e4m3_2d(const void *x, int64_t R, int64_t C, int64_t 
   const int vq = q && aligned16(q) && ldq % 16 == 0;
   const int vqT = qT && aligned16(qT) && ldqT % 16 == 0;
   quant2d_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t *>(x), R, C, ld, scale, q, ldq, qT, ldqT, vx, vq, vqT);
+      static_cast<const uint8_t *>(x), R, C, ld, scale, q, ldq, qT, ldqT, vx, vq, vqT,
+      (fp8_flags & BS_FP8_COMPILED) != 0);
   return launch_err();
 }

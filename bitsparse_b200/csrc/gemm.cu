@@ -524,7 +524,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           const uint32_t first = rfirst[c], excl = rexcl[c];
           const uint16_t *sv = reinterpret_cast<const uint16_t *>(vs);
           const uint8_t *sv8 = vs;
-          const float hs = (EPI == kEpiFp8Relu2 && P.hscale) ? *P.hscale : 1.f;
+          // grad.mul_(scale) multiplies a bf16 tensor by the 0-dim fp32 scale,
+          // which torch first casts to the tensor's dtype: bf16(scale)
+          const float hs = (EPI == kEpiFp8Relu2 && P.hscale)
+                               ? __uint_as_float(bf16x2_rn(__float_as_uint(*P.hscale), 0u) << 16)
+                               : 1.f;
           uint32_t rk = first + excl;
           // k = 1 (the reference's RELU2_SCALE): 2r is exact in bf16 and the
           // fp32 product of two bf16 values is exact, so bf16(g * 2r) is one

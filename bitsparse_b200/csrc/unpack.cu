@@ -42,6 +42,7 @@ struct UnpackParams {
   const float *scale;
   float k;       // RELU2_SCALE
   const float *qscale;  // OUT 2: to_fp8 scale of the ReLU^2 reconstruction
+  int qcompiled;  // OUT 2: to_fp8 as the reference's compiled version (BS_FP8_COMPILED)
   int vals_v16;  // vals base 16-byte aligned
   int out_v32;   // out base + row stride allow 32-byte accesses
 };
@@ -220,9 +221,10 @@ __device__ __forceinline__ uint32_t relu2_out(const UnpackParams &P, uint32_t v)
     const float s2 = bf16_bits_to_f32(f32_to_bf16_bits(sc * sc));  // scale.square() in bf16
     v = f32_to_bf16_bits(bf16_bits_to_f32(v) * s2);
   }
-  if constexpr (OUT == 2) {  // e4m3(bf16(v / qscale)), as to_fp8 on the bf16 tensor
+  if constexpr (OUT == 2) {  // to_fp8's quantiser on the bf16 tensor (eager or compiled)
     const float qs = *P.qscale;
-    v = div_e4m3x2(bf16_bits_to_f32(v), 0.f, qs, __frcp_rn(qs)) & 0xFFu;
+    v = P.qcompiled ? f32_to_e4m3_bits(div_full(bf16_bits_to_f32(v), qs))
+                    : div_e4m3x2(bf16_bits_to_f32(v), 0.f, qs, __frcp_rn(qs)) & 0xFFu;
   }
   return v;
 }
@@ -932,14 +934,15 @@ code_max_kernel(const uint8_t *vals, const int64_t *vals_offset, const uint32_t 
 // the scratch word.
 template <int SDT>
 __global__ void relu2_qscale_kernel(uint32_t *code_ws, const float *scale, float k,
-                                    float *qscale) {
+                                    float *qscale, int compiled) {
   const float x = store_bits_to_f32<SDT>(*code_ws);
   float v = bf16_bits_to_f32(f32_to_bf16_bits(k * x * x));
   if (scale) {
     const float sc = *scale;
     v = bf16_bits_to_f32(f32_to_bf16_bits(v * bf16_bits_to_f32(f32_to_bf16_bits(sc * sc))));
   }
-  const float s = bf16_bits_to_f32(f32_to_bf16_bits(__fdiv_rn(v, 448.0f)));
+  float s = compiled ? v * kRcp448 : __fdiv_rn(v, 448.0f);
+  if (!compiled) s = bf16_bits_to_f32(f32_to_bf16_bits(s));
   *qscale = fmaxf(s, 1e-9f);
   *code_ws = 0u;
 }
@@ -951,7 +954,8 @@ extern "C" int bs_unpack_relu2_fp8t(const void *vals, const uint8_t *bitmask,
                                     const uint32_t *prefix, const int64_t *vals_offset,
                                     int store_dtype, int64_t M, int64_t N, const float *scale,
                                     float k, uint32_t *code_ws, float *qscale_out, void *outT,
-                                    int64_t out_ld, void *stream) {
+                                    int64_t out_ld, int fp8_flags, void *stream) {
+  const int compiled = (fp8_flags & BS_FP8_COMPILED) != 0;
   if (store_dtype != BS_E4M3 && store_dtype != BS_E5M2) return BS_ERR_DTYPE;
   if (M < 0 || N < 0 || out_ld < M) return BS_ERR_SHAPE;
   const int64_t gm = (M + kTileM - 1) / kTileM, gn = (N + kTileN - 1) / kTileN;
@@ -961,9 +965,9 @@ extern "C" int bs_unpack_relu2_fp8t(const void *vals, const uint8_t *bitmask,
   const uint8_t *v8 = static_cast<const uint8_t *>(vals);
   code_max_kernel<<<148 * 4, kThreads, 0, st>>>(v8, vals_offset, prefix + gm * gn, code_ws);
   if (store_dtype == BS_E4M3)
-    relu2_qscale_kernel<BS_E4M3><<<1, 1, 0, st>>>(code_ws, scale, k, qscale_out);
+    relu2_qscale_kernel<BS_E4M3><<<1, 1, 0, st>>>(code_ws, scale, k, qscale_out, compiled);
   else
-    relu2_qscale_kernel<BS_E5M2><<<1, 1, 0, st>>>(code_ws, scale, k, qscale_out);
+    relu2_qscale_kernel<BS_E5M2><<<1, 1, 0, st>>>(code_ws, scale, k, qscale_out, compiled);
   if (gm * gn == 0) return launch_err();
   UnpackParams P{};
   P.vals = v8;
@@ -980,6 +984,7 @@ extern "C" int bs_unpack_relu2_fp8t(const void *vals, const uint8_t *bitmask,
   P.scale = scale;
   P.k = k;
   P.qscale = qscale_out;
+  P.qcompiled = compiled;
   P.vals_v16 = aligned(vals, 16);
   P.out_v32 = aligned(outT, 16) && (out_ld % 16 == 0);
   const dim3 g(ctas(P.ntiles));

@@ -1,8 +1,9 @@
 """FP8 helpers: per-tensor e4m3 quantiser and the FP8 matmul autograd op.
 
 Mirrors lib_sparse/fp8.py (Maxzhu123/bitsparse).  ``to_fp8`` runs on this
-library's CUDA kernels (amax -> scale, then quantise).  The FP8 GEMMs are
-plain library GEMMs (cuBLASLt through ``F.scaled_mm``), as in the reference.
+library's CUDA kernels (amax -> scale, then quantise) with the arithmetic of
+``FP8_SEMANTICS``.  The FP8 GEMMs are cuBLASLt through ``F.scaled_mm``, as in
+the reference, or this library's tcgen05 kernels (``FP8_GEMM``).
 
 Two deliberate differences from the reference, both bug fixes:
 
@@ -23,6 +24,41 @@ from torch.autograd import Function
 from torch.nn import functional as F
 
 from .config import CACHE_FP8_MATMUl
+
+# to_fp8's arithmetic (lib_sparse/fp8.py:123-129), which decides the FP8
+# bytes: "compiled" -- the reference's @torch.compile'd to_fp8 as it runs on
+# a GPU (scale = amax * (1/448) in fp32, q = e4m3(x / scale) with Triton's
+# fp32 division), the default;
+# "eager" -- eager PyTorch's (bf16 input: the scale and the quotient rounded
+# to bf16), which the reference's CPU golden fixtures hold.
+# BS_FP8_SEMANTICS in the environment overrides the default.
+FP8_SEMANTICS = os.environ.get("BS_FP8_SEMANTICS", "compiled")
+
+
+class fp8_semantics:
+    """Context manager: ``with fp8_semantics("eager"): ...`` runs to_fp8's
+    quantisation with that arithmetic and restores the previous one."""
+
+    def __init__(self, mode: str):
+        self.mode = mode
+
+    def __enter__(self):
+        global FP8_SEMANTICS
+        self.prev, FP8_SEMANTICS = FP8_SEMANTICS, self.mode
+        return self
+
+    def __exit__(self, *a):
+        global FP8_SEMANTICS
+        FP8_SEMANTICS = self.prev
+
+
+def fp8_flags() -> int:
+    """The C ABI flag of the current FP8_SEMANTICS."""
+    from . import _lib
+    if FP8_SEMANTICS not in ("compiled", "eager"):
+        raise ValueError(f"FP8_SEMANTICS must be 'compiled' or 'eager', not {FP8_SEMANTICS!r}")
+    return _lib.BS_FP8_COMPILED if FP8_SEMANTICS == "compiled" else 0
+
 
 _FP8_DTYPES = (torch.float8_e4m3fn, torch.float8_e5m2)
 _FP8_DTYPE = torch.float8_e4m3fn
@@ -55,8 +91,8 @@ def _dense_layout(x: Tensor) -> tuple[Tensor, bool]:
 def fp8_scale(x: Tensor) -> Tensor:
     """Per-tensor scale of to_fp8: max(amax(|x|) / 448, 1e-9), fp32 0-dim.
 
-    For bf16 input amax / 448 is rounded to bf16 first (the eager PyTorch
-    semantics of lib_sparse/fp8.py:126 on a bf16 tensor)."""
+    In eager semantics amax / 448 is rounded to bf16 for bf16 input (eager
+    PyTorch on lib_sparse/fp8.py:126); in compiled semantics it stays fp32."""
     from . import _lib, _runtime as R
 
     R.require_cuda(x, "x")
@@ -64,7 +100,7 @@ def fp8_scale(x: Tensor) -> Tensor:
         raise TypeError("to_fp8 takes bfloat16 or float32 input")
     x, _ = _dense_layout(x)  # the amax does not depend on the layout
     scale = torch.empty((), dtype=torch.float32, device=x.device)
-    _lib.call("bs_fp8_scale", x.data_ptr(), R.dtype_code(x.dtype), x.numel(),
+    _lib.call("bs_fp8_scale", x.data_ptr(), R.dtype_code(x.dtype) | fp8_flags(), x.numel(),
               R.amax_scratch(x.device).data_ptr(), scale.data_ptr(),
               R.stream_handle(x.device))
     return scale
@@ -72,12 +108,14 @@ def fp8_scale(x: Tensor) -> Tensor:
 
 @torch.no_grad()
 def quantize_e4m3(x: Tensor, scale: Tensor) -> Tensor:
-    """e4m3fn(x / scale), elementwise (bf16 input: quotient rounded to bf16)."""
+    """to_fp8's quantiser, elementwise: e4m3fn(bf16(x / scale)) for bf16 input
+    in eager semantics, e4m3fn(x / scale) with Triton's fp32 division in
+    compiled semantics."""
     from . import _lib, _runtime as R
 
     xc, transposed = _dense_layout(x)
     q = torch.empty(xc.shape, dtype=_FP8_DTYPE, device=x.device)
-    _lib.call("bs_quantize_e4m3", xc.data_ptr(), R.dtype_code(xc.dtype), xc.numel(),
+    _lib.call("bs_quantize_e4m3", xc.data_ptr(), R.dtype_code(xc.dtype) | fp8_flags(), xc.numel(),
               scale.data_ptr(), q.data_ptr(), R.stream_handle(x.device))
     return q.T if transposed else q
 
@@ -111,7 +149,7 @@ def quantize_e4m3_layouts(x: Tensor, scale: Tensor, row: bool = True,
     qT = torch.empty((cols, rows), dtype=_FP8_DTYPE, device=x.device) if want_qT else None
     ld = xc.stride(0) if rows > 1 else cols  # a single row's stride is arbitrary
     _lib.call("bs_quantize_e4m3_2d", xc.data_ptr(), rows, cols, ld, scale.data_ptr(),
-              R.ptr(q), cols, R.ptr(qT), rows, R.stream_handle(x.device))
+              R.ptr(q), cols, R.ptr(qT), rows, fp8_flags(), R.stream_handle(x.device))
     if transposed:  # x = xc.T: x's row-major form is qT, its column-major form q.T
         return (qT if row else None), (q.T if col else None)
     return (q if row else None), (qT.T if col else None)

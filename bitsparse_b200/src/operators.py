@@ -123,6 +123,10 @@ def compress(dense: Tensor, scale: Tensor | None = None, sparse_data=None,
     status = R.status_word(dev)
     qs = R.ptr(quant_scale)
     qo = R.ptr(quant_out)
+    dcode = R.dtype_code(dense.dtype)
+    if quant_scale is not None:  # to_fp8's arithmetic: eager or compiled
+        from ..fp8 import fp8_flags
+        dcode |= fp8_flags()
     if quant_out is not None and (quant_out.dtype != torch.float8_e4m3fn
                                   or not quant_out.is_contiguous()
                                   or tuple(quant_out.shape) != (M, N)):
@@ -144,7 +148,7 @@ def compress(dense: Tensor, scale: Tensor | None = None, sparse_data=None,
                 tmp = torch.empty(M * N, device=dev, dtype=stored)
                 cap = M * N
             nnz_t = torch.empty((), device=dev, dtype=torch.int64)
-            _lib.call("bs_compress", dense.data_ptr(), R.dtype_code(dense.dtype), M, N, ld,
+            _lib.call("bs_compress", dense.data_ptr(), dcode, M, N, ld,
                       qs, qo, bitmask.data_ptr(), prefix.data_ptr(), tmp.data_ptr(), cap,
                       int(pack_sbit), None, None, nnz_t.data_ptr(), ws.data_ptr(),
                       ws.numel(), status.data_ptr(), st)
@@ -166,7 +170,7 @@ def compress(dense: Tensor, scale: Tensor | None = None, sparse_data=None,
             off = sparse_data.offset
             vals_offset.copy_((off + 7) // 8 * 8 if pack_sbit else off)
         else:
-            _lib.call("bs_compress", dense.data_ptr(), R.dtype_code(dense.dtype), M, N, ld,
+            _lib.call("bs_compress", dense.data_ptr(), dcode, M, N, ld,
                       qs, qo, bitmask.data_ptr(), prefix.data_ptr(), vals.data_ptr(), cap,
                       int(pack_sbit), sparse_data.offset.data_ptr(), vals_offset.data_ptr(),
                       None, ws.data_ptr(), ws.numel(), status.data_ptr(), st)
@@ -357,7 +361,8 @@ def matmul_fp8_relu2_grad(a: Tensor, bt: Tensor, a_scale: Tensor, b_scale: Tenso
 
 
 def _fused_compress(fn, name: str, head: tuple, dev, stream: int, stored, M: int, N: int,
-                    T: int, bitmask: Tensor, prefix: Tensor, sparse_data, pack_sbit: bool):
+                    T: int, bitmask: Tensor, prefix: Tensor, sparse_data, pack_sbit: bool,
+                    flags: tuple = ()):
     """Run a fused compress entry point ``fn(*head, bitmask, prefix, vals,
     capacity, pack_sbit, arena_offset, vals_offset_out, nnz_out, workspace,
     workspace_bytes, status, stream)`` (``head``: its leading arguments,
@@ -375,7 +380,7 @@ def _fused_compress(fn, name: str, head: tuple, dev, stream: int, stored, M: int
         nnz_t = torch.empty((), device=dev, dtype=torch.int64)
         rc = fn(*head, bitmask.data_ptr(), prefix.data_ptr(), tmp.data_ptr(), tmp.numel(),
                 int(pack_sbit), None, None, nnz_t.data_ptr(), ws.data_ptr(), ws.numel(),
-                status.data_ptr(), stream)
+                *flags, status.data_ptr(), stream)
         if rc == _lib.BS_ERR_ALIGN:
             return None
         _lib.check(rc, name)
@@ -390,7 +395,7 @@ def _fused_compress(fn, name: str, head: tuple, dev, stream: int, stored, M: int
     vals_offset = torch.empty(1, device=dev, dtype=torch.int64)
     rc = fn(*head, bitmask.data_ptr(), prefix.data_ptr(), vals.data_ptr(), vals.numel(),
             int(pack_sbit), sparse_data.offset.data_ptr(), vals_offset.data_ptr(), None,
-            ws.data_ptr(), ws.numel(), status.data_ptr(), stream)
+            ws.data_ptr(), ws.numel(), *flags, status.data_ptr(), stream)
     if rc == _lib.BS_ERR_ALIGN:
         return None
     _lib.check(rc, name)
@@ -451,6 +456,7 @@ def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit:
     ``None`` when the one-pass kernel cannot read the tensors.
     """
     from ..config import RELU2_SCALE
+    from ..fp8 import fp8_flags
     if z.dtype != torch.bfloat16 or bias.dtype != torch.bfloat16:
         return None
     if square and RELU2_SCALE != 1:
@@ -470,14 +476,16 @@ def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit:
     scale_s = torch.empty((), device=dev, dtype=torch.float32) if square else None
     _lib.check(lib.bs_fp8_scales_bias_relu(z.data_ptr(), M, N, ld, bias.data_ptr(),
                                            R.amax_scratch(dev).data_ptr(), scale_h.data_ptr(),
-                                           R.ptr(scale_s), st), "bs_fp8_scales_bias_relu")
+                                           R.ptr(scale_s), fp8_flags(), st),
+               "bs_fp8_scales_bias_relu")
     side = torch.empty((M, N), device=dev, dtype=torch.float8_e4m3fn)
     bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
     prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
     out = _fused_compress(lib.bs_compress_bias_relu_fp8, "bs_compress_bias_relu_fp8",
                           (z.data_ptr(), M, N, ld, bias.data_ptr(), scale_h.data_ptr(),
                            R.ptr(scale_s), side.data_ptr()), dev, st,
-                          torch.float8_e4m3fn, M, N, T, bitmask, prefix, sparse_data, pack_sbit)
+                          torch.float8_e4m3fn, M, N, T, bitmask, prefix, sparse_data, pack_sbit,
+                          flags=(fp8_flags(),))
     if out is None:
         return None
     vals, vals_offset = out

@@ -67,6 +67,7 @@ def _relu2_fp8_colmajor(sp: BitsparseTensor) -> tuple[Tensor, Tensor]:
     in one pass over the compressed tensor (bs_unpack_relu2_fp8t)."""
     from .. import _lib, _runtime as R
     from ..config import RELU2_SCALE
+    from ..fp8 import fp8_flags
     M, N = sp.shape
     dev = sp.bitmask.device
     bT = torch.empty(N, M, device=dev, dtype=torch.float8_e4m3fn)
@@ -75,7 +76,7 @@ def _relu2_fp8_colmajor(sp: BitsparseTensor) -> tuple[Tensor, Tensor]:
     _lib.call("bs_unpack_relu2_fp8t", sp.vals.data_ptr(), sp.bitmask.data_ptr(),
               sp.prefix.data_ptr(), sp.vals_offset.data_ptr(), R.dtype_code(sp.dtype), M, N,
               R.ptr(scale), float(RELU2_SCALE), R.amax_scratch(dev).data_ptr(), qs.data_ptr(),
-              bT.data_ptr(), M, R.stream_handle(dev))
+              bT.data_ptr(), M, fp8_flags(), R.stream_handle(dev))
     return bT, qs
 
 

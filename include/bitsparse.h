@@ -62,6 +62,17 @@ enum {
   BS_F32 = 3
 };
 
+/* FP8 quantiser semantics, OR-ed into the dtype argument of bs_fp8_scale,
+ * bs_quantize_e4m3 and (with quant_scale) bs_compress, and passed as the
+ * fp8_flags argument of the fused FFN entry points.  0 (default): eager
+ * PyTorch's to_fp8 arithmetic (bf16 input: scale = bf16(amax / 448), q =
+ * e4m3(bf16(x / scale))), which the CPU golden fixtures of the reference
+ * hold.  BS_FP8_COMPILED: the arithmetic of the reference's
+ * @torch.compile'd to_fp8 on a GPU (lib_sparse/fp8.py:123-129): scale =
+ * amax * (1/448) in fp32, q = e4m3(x / scale) with the fp32
+ * division of Triton's `/` (PTX div.full.f32) and no intermediate rounding. */
+#define BS_FP8_COMPILED 0x100
+
 /* Tile geometry (lib_sparse/config.py:5-6, lib_sparse/bitsparse.py:120-127). */
 #define BS_BLOCK_M 64
 #define BS_BLOCK_N 64
@@ -155,7 +166,8 @@ int bs_compress_bias_relu_fp8(const void *z, int64_t M, int64_t N, int64_t ld,
                               uint8_t *bitmask, uint32_t *prefix, void *vals,
                               int64_t vals_capacity, int pack_sbit, int64_t *arena_offset,
                               int64_t *vals_offset_out, int64_t *nnz_out, void *workspace,
-                              size_t workspace_bytes, int32_t *status, void *stream);
+                              size_t workspace_bytes, int fp8_flags, int32_t *status,
+                              void *stream);
 
 /* to_fp8 scales for the fused FFN forward without materialising h =
  * relu(bf16(z + bias)): *scale_h = max(bf16(amax(h) / 448), 1e-9) and,
@@ -164,7 +176,7 @@ int bs_compress_bias_relu_fp8(const void *z, int64_t M, int64_t N, int64_t ld,
  * amax_ws as in bs_fp8_scale. */
 int bs_fp8_scales_bias_relu(const void *z, int64_t M, int64_t N, int64_t ld,
                             const void *bias, uint32_t *amax_ws, float *scale_h,
-                            float *scale_h2, void *stream);
+                            float *scale_h2, int fp8_flags, void *stream);
 
 /* bs_compress without any device allocation, for callers that cannot call
  * cudaMalloc (code running inside an allocator or a hook where allocating is
@@ -224,7 +236,8 @@ int bs_unpack(const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
  * of an operand (lib_sparse/fp8.py:15-17), in one read of x.  Either
  * output may be NULL. */
 int bs_quantize_e4m3_2d(const void *x, int64_t R, int64_t C, int64_t ld, const float *scale,
-                        uint8_t *q, int64_t ldq, uint8_t *qT, int64_t ldqT, void *stream);
+                        uint8_t *q, int64_t ldq, uint8_t *qT, int64_t ldqT, int fp8_flags,
+                        void *stream);
 
 /* Status of the reconstruct kernels of the current device (bs_unpack has
  * no status argument): *status_out = BS_STATUS_* bits OR-ed since the last
@@ -250,7 +263,7 @@ int bs_mask_with_bitmask(void *grad, int grad_dtype, int64_t M, int64_t N,
 int bs_unpack_relu2_fp8t(const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
                          const int64_t *vals_offset, int store_dtype, int64_t M, int64_t N,
                          const float *scale, float k, uint32_t *code_ws, float *qscale_out,
-                         void *outT, int64_t out_ld, void *stream);
+                         void *outT, int64_t out_ld, int fp8_flags, void *stream);
 
 /* In place grad <- bit ? grad * (2 * k * r) : 0, r gathered from the stored
  * values, then (scale != NULL) grad *= scale.  Replaces relu2_grad_sparse_

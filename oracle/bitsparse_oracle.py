@@ -181,7 +181,10 @@ def to_fp8(x: np.ndarray, in_dtype: str):
     ``in_dtype`` is ``"float32"`` (x is float32) or ``"bfloat16"`` (x is
     bf16 bits).  Eager PyTorch semantics: for bf16 input ``amax / 448`` is
     rounded to bf16 before ``.to(float32)`` and ``x / scale`` is rounded to
-    bf16 before the fp8 cast; for fp32 both stay fp32.  Returns
+    bf16 before the fp8 cast; for fp32 both stay fp32.  (The reference's
+    ``@torch.compile``d to_fp8 on a GPU divides with an approximate
+    hardware division, which a CPU cannot restate bit for bit; the tests
+    check that semantics against the compiled function itself.)  Returns
     ``(q_bits uint8, scale float32)``.
     """
     if in_dtype == "bfloat16":

@@ -49,3 +49,25 @@ def payload(vals: np.ndarray, start: int, nnz: int, nbits: int) -> np.ndarray:
     idx = np.arange(sb.size)
     sb &= ((idx >= start * nbits) & (idx < (start + nnz) * nbits)).astype(np.uint8)
     return np.packbits(sb, bitorder="little")
+
+
+_COMPILED = None
+
+
+def reference_to_fp8(x: torch.Tensor, compiled: bool = True):
+    """The reference's to_fp8 (lib_sparse/fp8.py:123-129), its three lines
+    restated here, run on the GPU as the reference runs it: compiled by
+    torch.compile (Inductor / Triton), or eagerly."""
+    global _COMPILED
+
+    @torch.no_grad()
+    def to_fp8(t):
+        scale = (t.detach().abs().max() / torch.finfo(torch.float8_e4m3fn).max).to(torch.float32)
+        scale = scale.clamp(min=1e-9)
+        return (t / scale).to(torch.float8_e4m3fn), scale
+
+    if not compiled:
+        return to_fp8(x)
+    if _COMPILED is None:
+        _COMPILED = torch.compile(to_fp8)
+    return _COMPILED(x)

@@ -8,10 +8,9 @@ values are compared with the oracle byte for byte.  A packed stream is
 checked by decoding every value at its logical index (the oracle's decoder,
 pinned on the golden fixtures) against the oracle's raw values, and every
 bit outside the payload must be zero: together these fix the whole stream
-bit for bit.  The FP8 bytes of config 4 are compared with PyTorch's own
-eager quantiser on the same GPU (the reference's to_fp8 arithmetic,
-lib_sparse/fp8.py:123-129; the oracle's restatement of it is pinned to the
-same torch semantics in test_to_fp8_many_values_and_scales)."""
+bit for bit.  The FP8 bytes of config 4 are compared with the reference's
+to_fp8 (lib_sparse/fp8.py:123-129) run on the same GPU, eagerly and
+torch.compile'd."""
 import numpy as np
 import pytest
 import torch
@@ -22,7 +21,7 @@ from bitsparse_b200.src.functions import dense_to_tilesparse, relu_to_tilesparse
 from bitsparse_b200.src.operators import unpack_batch_
 from bench import make_relu_bf16
 from oracle import bitsparse_oracle as O
-from tests.gpu_util import bits
+from tests.gpu_util import bits, reference_to_fp8
 
 pytestmark = pytest.mark.gpu
 
@@ -72,19 +71,21 @@ def test_config3_full_size(variant, target, mu, pack):
 
 
 @pytest.mark.parametrize("pack", [False, True])
-def test_config4_fp8_full_size(pack):
+@pytest.mark.parametrize("semantics", ["compiled", "eager"])
+def test_config4_fp8_full_size(pack, semantics):
     """16384 x 16384 relu(N(0,1)) quantised + compressed in one pass:
-    T = 65536 tiles (one whole _PACK_CHUNK_TILES chunk of the reference)."""
+    T = 65536 tiles (one whole _PACK_CHUNK_TILES chunk of the reference).
+    The FP8 bytes are compared with the reference's to_fp8 run on the same
+    GPU, eagerly or torch.compile'd."""
+    from bitsparse_b200.fp8 import fp8_semantics
     M = N = 16384
     g = torch.Generator().manual_seed(23)
     x = torch.randn(M, N, generator=g).relu_().to(torch.bfloat16)
     xd = x.cuda()
     del x
-    # the reference's to_fp8, eager, on the same GPU
-    scale = (xd.abs().max() / torch.finfo(torch.float8_e4m3fn).max).to(torch.float32)
-    scale = scale.clamp(min=1e-9)
-    q_ref = (xd / scale).to(torch.float8_e4m3fn)
-    q, sp = relu_to_tilesparse_fp8(xd, None, pack)
+    q_ref, scale = reference_to_fp8(xd, compiled=semantics == "compiled")
+    with fp8_semantics(semantics):
+        q, sp = relu_to_tilesparse_fp8(xd, None, pack)
     assert sp.grid_m * sp.grid_n == 65536
     assert sp.scale.item() == scale.item()
     assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8))

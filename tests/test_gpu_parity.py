@@ -14,7 +14,7 @@ import torch
 
 import bitsparse_b200 as B
 from bitsparse_b200 import TensorBuffer, bits_per_value
-from bitsparse_b200.fp8 import to_fp8
+from bitsparse_b200.fp8 import fp8_semantics, to_fp8
 from bitsparse_b200.src.functions import (_prepare_tiles, dense_to_tilesparse,
                                           relu_to_tilesparse_fp8)
 from bitsparse_b200.src.operators import (compact_vals, mask_with_bitmask_,
@@ -24,7 +24,7 @@ from oracle import bitsparse_oracle as O
 from tests.conftest import golden_cases, parse_case
 from tests.golden.fixtures import arena_inputs, case_inputs, check, digest, has
 from tests.golden.make_golden import SHAPES_FULL, SPARSITIES
-from tests.gpu_util import TORCH_DT, bits, oracle_sparse, payload, to_dev
+from tests.gpu_util import TORCH_DT, bits, oracle_sparse, payload, reference_to_fp8, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -95,12 +95,20 @@ def test_golden_shared_arena(golden):
 
 
 def test_config1_fp8_and_bf16(golden):
-    """Config 1: x ~ N(0,1) [1024, 3072] fp32 seed 0, to_fp8(relu(x))."""
+    """Config 1: x ~ N(0,1) [1024, 3072] fp32 seed 0, to_fp8(relu(x)), against
+    the reference's own CPU run (eager to_fp8); in compiled semantics the
+    scale and bytes equal those of the compiled to_fp8 run on this GPU."""
     g = torch.Generator().manual_seed(0)
     x = torch.randn(1024, 3072, generator=g, dtype=torch.float32)
     assert digest(x.numpy()) == str(golden["c1/x_sha"])
     h = torch.relu(x).cuda()
-    q, scale = to_fp8(h)
+    with fp8_semantics("compiled"):
+        qc, sc = to_fp8(h)
+    qr, sr = reference_to_fp8(h)
+    assert sc.item() == sr.item()
+    assert torch.equal(qc.view(torch.uint8), qr.view(torch.uint8))
+    with fp8_semantics("eager"):
+        q, scale = to_fp8(h)
     assert scale.item() == float(golden["c1/scale"])
     assert digest(bits(q)) == str(golden["c1/q_sha"])
     for name, dense in (("fp8", q), ("bf16", h.to(torch.bfloat16))):
@@ -118,16 +126,24 @@ def test_config1_fp8_and_bf16(golden):
             assert digest(bits(_reconstruct(sp))) == str(golden[k + "recon_sha"])
 
 
-def test_fused_quantise_matches_to_fp8_then_compress():
+@pytest.mark.parametrize("semantics", ["eager", "compiled"])
+def test_fused_quantise_matches_to_fp8_then_compress(semantics):
     """relu_to_tilesparse_fp8 (one amax pass + one fused pass) equals the
-    reference's to_fp8 then dense_to_tilesparse, bit for bit (oracle)."""
+    reference's to_fp8 then dense_to_tilesparse, bit for bit (the oracle's
+    compress; to_fp8 from the oracle in eager semantics, from the compiled
+    function on this GPU in compiled semantics)."""
     g = torch.Generator().manual_seed(11)
     for (M, N) in ((1024, 3072), (129, 131), (64, 64), (1, 8)):
         z = (torch.randn(M, N, generator=g) * 2.5).to(torch.bfloat16)
         h = torch.relu(z).cuda()
         for pack in (False, True):
-            h_fp8, sp = relu_to_tilesparse_fp8(h.clone(), None, pack)
-            q_o, s_o = O.to_fp8(bits(h), "bfloat16")
+            with fp8_semantics(semantics):
+                h_fp8, sp = relu_to_tilesparse_fp8(h.clone(), None, pack)
+            if semantics == "eager":
+                q_o, s_o = O.to_fp8(bits(h), "bfloat16")
+            else:
+                qr, sr = reference_to_fp8(h)
+                q_o, s_o = bits(qr), np.float32(sr.item())
             assert sp.scale.item() == s_o
             np.testing.assert_array_equal(bits(h_fp8).reshape(-1), q_o.reshape(-1))
             osp = O.dense_to_tilesparse(q_o.reshape(M, N), O.DT_E4M3, None, pack)
@@ -311,16 +327,24 @@ def test_deterministic():
         assert torch.equal(a.vals, b.vals) and torch.equal(a.prefix, b.prefix)
 
 
-def test_to_fp8_many_values_and_scales():
-    """The bf16 quantiser (reciprocal + residual-corrected quotient, exact
-    division near bf16 rounding midpoints, hardware e4m3 cast) equals the
-    oracle's eager-PyTorch to_fp8 on random data over many magnitudes."""
+@pytest.mark.parametrize("semantics", ["eager", "compiled"])
+def test_to_fp8_many_values_and_scales(semantics):
+    """The bf16 quantiser (eager: reciprocal + residual-corrected quotient,
+    exact division near bf16 rounding midpoints, hardware e4m3 cast;
+    compiled: Triton's division) equals the reference's to_fp8 -- the
+    oracle's eager restatement, or the compiled function on this GPU -- on
+    random data over many magnitudes."""
     g = torch.Generator().manual_seed(17)
     for mag in (1e-6, 1e-3, 0.37, 1.0, 3.3, 250.0, 1e4):
         x = (torch.randn(1 << 20, generator=g) * mag).to(torch.bfloat16)
         x[:7] = torch.tensor([0.0, -0.0, mag, -mag, 1e-30, mag * 1e-4, -mag * 3])
-        q, s = to_fp8(x.cuda())
-        qo, so = O.to_fp8(bits(x), "bfloat16")
+        with fp8_semantics(semantics):
+            q, s = to_fp8(x.cuda())
+        if semantics == "eager":
+            qo, so = O.to_fp8(bits(x), "bfloat16")
+        else:
+            qr, sr = reference_to_fp8(x.cuda())
+            qo, so = bits(qr), np.float32(sr.item())
         assert s.item() == so
         np.testing.assert_array_equal(bits(q), qo)
 
@@ -424,7 +448,13 @@ def test_compress_bias_relu_equals_separate_steps(M, N, pack):
 @pytest.mark.gpu
 @pytest.mark.parametrize("M, N", [(64, 64), (300, 200), (1000, 3072), (129, 4097), (1, 17)])
 @pytest.mark.parametrize("zero", [False, True])
-def test_relu2_fp8_colmajor_equals_to_fp8_of_reconstruction(M, N, zero):
+@pytest.mark.parametrize("semantics", ["compiled", "eager"])
+def test_relu2_fp8_colmajor_equals_to_fp8_of_reconstruction(M, N, zero, semantics):
+    with fp8_semantics(semantics):
+        _check_relu2_fp8_colmajor_equals_to_fp8_of_reconstruction(M, N, zero)
+
+
+def _check_relu2_fp8_colmajor_equals_to_fp8_of_reconstruction(M, N, zero):
     """bs_unpack_relu2_fp8t == to_fp8(ReLU^2 reconstruction) transposed, bit
     for bit (the dW operand of the fp8 Relu2Linear backward)."""
     from bitsparse_b200.src.sparse_matmul import _relu2_fp8_colmajor
@@ -447,7 +477,13 @@ def test_relu2_fp8_colmajor_equals_to_fp8_of_reconstruction(M, N, zero):
 @pytest.mark.gpu
 @pytest.mark.parametrize("M, N", [(512, 1024), (300, 200), (1, 40), (130, 8), (2048, 3072)])
 @pytest.mark.parametrize("square", [False, True])
-def test_compress_bias_relu_fp8_equals_separate_steps(M, N, square):
+@pytest.mark.parametrize("semantics", ["compiled", "eager"])
+def test_compress_bias_relu_fp8_equals_separate_steps(M, N, square, semantics):
+    with fp8_semantics(semantics):
+        _check_compress_bias_relu_fp8_equals_separate_steps(M, N, square)
+
+
+def _check_compress_bias_relu_fp8_equals_separate_steps(M, N, square):
     """Fused fp8 bias + ReLU (+ square) + quantise + compress == torch's
     z + b, relu, to_fp8, compress; the side operand == to_fp8(h) or
     to_fp8(h * h), bit for bit, scales included."""
@@ -504,7 +540,13 @@ def test_plain_reconstruct_both_kernels(monkeypatch, per_cta, dtype, pack):
 @pytest.mark.gpu
 @pytest.mark.parametrize("R, C", [(64, 64), (300, 200), (1, 17), (4096, 768), (129, 4097)])
 @pytest.mark.parametrize("view", ["plain", "transposed", "strided"])
-def test_quantize_layouts_equal_to_fp8_copies(R, C, view):
+@pytest.mark.parametrize("semantics", ["compiled", "eager"])
+def test_quantize_layouts_equal_to_fp8_copies(R, C, view, semantics):
+    with fp8_semantics(semantics):
+        _check_quantize_layouts_equal_to_fp8_copies(R, C, view)
+
+
+def _check_quantize_layouts_equal_to_fp8_copies(R, C, view):
     """bs_quantize_e4m3_2d: both layouts == to_fp8's codes and their
     transposed copy, bit for bit, for plain, transposed (W.T) and row-strided
     inputs."""

@@ -12,8 +12,9 @@
    this library's kernels, bit for bit, over every positive bf16 pattern and
    every positive e4m3 code.
 2. The reference's ``to_fp8`` is ``@torch.compile``d (lib_sparse/fp8.py:
-   123-129).  The same three lines compiled by Inductor on this GPU are
-   compared with this library's scale and quantiser at several magnitudes.
+   123-129).  The same three lines compiled by Inductor on this GPU, and
+   run eagerly, are compared bit for bit with this library's scale and
+   quantiser in its compiled and eager semantics at several magnitudes.
 """
 import numpy as np
 import pytest
@@ -137,22 +138,20 @@ def _to_fp8_eager(x):
 
 
 @pytest.mark.parametrize("mag", [1e-6, 1e-3, 0.1, 1.0, 7.0, 300.0, 1e4])
-def test_to_fp8_compiled_vs_library(mag):
-    """The reference's to_fp8 as it runs there (torch.compile'd) against this
-    library's fp8_scale + quantize_e4m3 (which follow eager PyTorch), on bf16
-    input.  The result of each comparison is part of the test's output."""
+def test_to_fp8_compiled_and_eager(mag):
+    """The reference's to_fp8 as it runs there (torch.compile'd on this GPU)
+    equals this library's fp8_scale + quantize_e4m3 in compiled semantics,
+    bit for bit, scale included; the same function run eagerly equals them
+    in eager semantics.  (The two arithmetics differ in about 1-3% of the
+    codes of bf16 input, and in the scale.)"""
+    from bitsparse_b200.fp8 import fp8_semantics
     compiled = torch.compile(_to_fp8_eager)
     g = torch.Generator().manual_seed(int(mag * 1000) % 9973)
     x = (torch.randn(2048, 4096, generator=g) * mag).to(torch.bfloat16).cuda()
-    qc, sc = compiled(x)
-    qe, se = _to_fp8_eager(x)
-    s = fp8_scale(x)
-    q = quantize_e4m3(x, s)
-    assert s.item() == se.item()
-    assert torch.equal(q.view(torch.uint8), qe.view(torch.uint8))
-    same_scale = sc.item() == s.item()
-    diff = (qc.view(torch.uint8) != q.view(torch.uint8)).sum().item()
-    print(f"mag {mag}: compiled scale {'==' if same_scale else '!='} library scale "
-          f"({sc.item()!r} vs {s.item()!r}); fp8 codes differing: {diff} of {x.numel()}")
-    if same_scale:
-        assert diff == 0
+    for mode, fn in (("compiled", compiled), ("eager", _to_fp8_eager)):
+        qr, sr = fn(x)
+        with fp8_semantics(mode):
+            s = fp8_scale(x)
+            q = quantize_e4m3(x, s)
+        assert s.item() == sr.item(), mode
+        assert torch.equal(q.view(torch.uint8), qr.view(torch.uint8)), mode
