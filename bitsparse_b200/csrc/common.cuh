@@ -221,8 +221,6 @@ __device__ __forceinline__ void div_e4m3x8(const uint32_t (&w)[4], float s, floa
   }
 }
 
-// torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;
-// -0 and NaN unchanged.
 // 1/448 rounded to fp32: the compiled to_fp8 computes amax / 448 as
 // amax * (1/448), the reciprocal of the constant taken once.
 constexpr float kRcp448 = 1.0f / 448.0f;
@@ -240,17 +238,59 @@ __device__ __forceinline__ float div_full(float x, float s) {
 // @torch.compile'd (lib_sparse/fp8.py:123-129), and the generated Triton
 // code divides the fp32 value by the scale with Triton's division and casts
 // the quotient to e4m3 -- no rounding of the quotient to bf16 as eager
-// PyTorch does.  Eight bf16 values (four words, low half first) -> two
-// words of codes.
-__device__ __forceinline__ void full_e4m3x8(const uint32_t (&w)[4], float s, uint32_t (&o)[2]) {
-  o[0] = o[1] = 0;
+// PyTorch does.  The e4m3 code only depends on which side of the e4m3
+// rounding midpoints the quotient lies: the estimate x * r (r = 1/s rounded
+// to fp32) is within a few fp32 ulps of the division's result, so when it
+// lies in the normal e4m3 range (>= 2^-6) and more than 64 ulps from a
+// midpoint (fp32 mantissa bits 19..0 = 0x80000) both give the same code;
+// only the others take the division itself.
+__device__ __forceinline__ bool e4m3_code_settled(float q0) {
+  const uint32_t b = __float_as_uint(q0);
+  const uint32_t low = b & 0xFFFFFu, d = low > 0x80000u ? low - 0x80000u : 0x80000u - low;
+  // a zero estimate is final too: 0*r and 0/s are the same signed zero (and
+  // the same NaN when s is 0 or NaN), and an estimate that underflowed to 0
+  // is below e4m3's smallest subnormal either way
+  return (((b >> 23) & 0xFFu) >= 127u - 6u && d > 64u) || (b << 1) == 0u;
+}
+// (The fp32 -> e4m3 casts are the hardware conversion, saturating to 448,
+// which is what Triton's cast compiles to.)
+__device__ __forceinline__ uint32_t e4m3_compiled(float x, float s, float r) {
+  const float q0 = x * r;
+  return e4m3x2_bits(e4m3_code_settled(q0) ? q0 : div_full(x, s), 0.f) & 0xFFu;
+}
+// The rare case of full_e4m3x8 (some estimate unsettled): all eight by the
+// division, out of line so that the unrolled callers stay small.
+static __device__ __noinline__ uint2 full_e4m3x8_div(uint32_t w0, uint32_t w1, uint32_t w2,
+                                                    uint32_t w3, float s) {
+  const uint32_t w[4] = {w0, w1, w2, w3};
+  float q[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) q[e] = div_full(__uint_as_float((w[e >> 1] >> (16 * (e & 1))) << 16), s);
+  return make_uint2(e4m3x2_bits(q[0], q[1]) | e4m3x2_bits(q[2], q[3]) << 16,
+                    e4m3x2_bits(q[4], q[5]) | e4m3x2_bits(q[6], q[7]) << 16);
+}
+// Eight bf16 values (four words, low half first) -> two words of codes.
+__device__ __forceinline__ void full_e4m3x8(const uint32_t (&w)[4], float s, float r,
+                                            uint32_t (&o)[2]) {
+  float q[8];
+  bool all = true;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    const float x = __uint_as_float((w[e >> 1] >> (16 * (e & 1))) << 16);
-    o[e >> 2] |= f32_to_e4m3_bits(div_full(x, s)) << (8 * (e & 3));
+    q[e] = __uint_as_float((w[e >> 1] >> (16 * (e & 1))) << 16) * r;
+    all &= e4m3_code_settled(q[e]);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    o[i] = e4m3x2_bits(q[4 * i], q[4 * i + 1]) | e4m3x2_bits(q[4 * i + 2], q[4 * i + 3]) << 16;
+  if (!all) {
+    const uint2 d = full_e4m3x8_div(w[0], w[1], w[2], w[3], s);
+    o[0] = d.x;
+    o[1] = d.y;
   }
 }
 
+// torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;
+// -0 and NaN unchanged.
 __device__ __forceinline__ uint32_t relu_bf16x2(uint32_t w) {
   const uint32_t v = w & 0x7FFF7FFFu;
   const uint32_t nz = v + 0x7FFF7FFFu;   // bit 15 of a half set iff v != 0

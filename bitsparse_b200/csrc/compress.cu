@@ -207,7 +207,7 @@ __device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64
       for (int g = 0; g < C::VEC / 8; ++g) {
         const uint32_t w4[4] = {raw[4 * g], raw[4 * g + 1], raw[4 * g + 2], raw[4 * g + 3]};
         uint32_t o2[2];
-        if (P.qcompiled) full_e4m3x8(w4, qs, o2);
+        if (P.qcompiled) full_e4m3x8(w4, qs, r, o2);
         else div_e4m3x8(w4, qs, r, o2);
         sv[2 * g] = o2[0];
         sv[2 * g + 1] = o2[1];
@@ -215,8 +215,11 @@ __device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64
     } else {
 #pragma unroll
       for (int e = 0; e < C::VEC; ++e) {
-        const float y = P.qcompiled ? div_full(__uint_as_float(raw[e]), qs)
-                                    : __fdiv_rn(__uint_as_float(raw[e]), qs);
+        if (P.qcompiled) {
+          sv[e >> 2] |= e4m3_compiled(__uint_as_float(raw[e]), qs, __frcp_rn(qs)) << (8 * (e & 3));
+          continue;
+        }
+        const float y = __fdiv_rn(__uint_as_float(raw[e]), qs);
         sv[e >> 2] |= f32_to_e4m3_bits(y) << (8 * (e & 3));
       }
     }
@@ -770,7 +773,7 @@ __device__ __forceinline__ void place8(uint32_t &a, uint32_t m, uint32_t bit, ui
 }
 
 template <int DT_IN, bool QUANT, bool PACK, int TPP_, int NW, int D, int A, int MINB,
-          bool BIAS = false>
+          bool BIAS = false, bool QC = false>
 __global__ void __launch_bounds__(NW * 32, MINB)
     onepass_kernel(const __grid_constant__ CUtensorMap tmap, const CompressParams P) {
   using O = Onepass<DT_IN, QUANT, TPP_, NW, D, A>;
@@ -927,9 +930,9 @@ __global__ void __launch_bounds__(NW * 32, MINB)
           }
           if constexpr (QUANT) {
             uint32_t qw[2] = {0, 0}, side[2];
-            if (P.qcompiled) {
+            if constexpr (QC) {  // quantise as the compiled to_fp8
               const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
-              full_e4m3x8(h4, qs, qw);
+              full_e4m3x8(h4, qs, qr, qw);
             } else if constexpr (BIAS) {
               const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
               div_e4m3x8(h4, qs, qr, qw);
@@ -953,7 +956,7 @@ __global__ void __launch_bounds__(NW * 32, MINB)
                   const float h1 = bf16_bits_to_f32(v[s4][i] >> 16);
                   sq[i] = bf16x2_from_f32(h0 * h0, h1 * h1);  // h.square_()
                 }
-                if (P.qcompiled) full_e4m3x8(sq, qs2, side);
+                if constexpr (QC) full_e4m3x8(sq, qs2, qr2, side);
                 else div_e4m3x8(sq, qs2, qr2, side);
               }
             }
@@ -1180,7 +1183,10 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return kNotApplicable;
-  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS>;
+  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS, false>;
+  if constexpr (QUANT) {  // the compiled to_fp8's quantiser: its own instantiation
+    if (P.qcompiled) kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS, true>;
+  }
   int resident = resident_ctas(reinterpret_cast<const void *>(kernel), O::SMEM, NW * 32);
   if (resident <= 0) return BS_ERR_LAUNCH;
   // a flush reads the counts of G - 1 partitions, at most CV per thread

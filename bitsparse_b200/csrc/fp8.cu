@@ -173,12 +173,16 @@ quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q, int co
       // fast e4m3 conversion applies (NaN stays NaN).
       const uint32_t w4[4] = {b[0] | b[1] << 16, b[2] | b[3] << 16, b[4] | b[5] << 16,
                               b[6] | b[7] << 16};
-      if (compiled) full_e4m3x8(w4, s, o);
+      if (compiled) full_e4m3x8(w4, s, r, o);
       else div_e4m3x8(w4, s, r, o);
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float y = compiled ? div_full(__uint_as_float(b[e]), s) : __fdiv_rn(__uint_as_float(b[e]), s);
+        if (compiled) {
+          o[e >> 2] |= e4m3_compiled(__uint_as_float(b[e]), s, r) << (8 * (e & 3));
+          continue;
+        }
+        const float y = __fdiv_rn(__uint_as_float(b[e]), s);
         o[e >> 2] |= f32_to_e4m3_bits(y) << (8 * (e & 3));
       }
     }
@@ -227,10 +231,10 @@ quant2d_kernel(const uint8_t *x, int64_t R, int64_t C, int64_t ld, const float *
     {
       const uint32_t lo[4] = {w[0], w[1], w[2], w[3]}, hi[4] = {w[4], w[5], w[6], w[7]};
       uint32_t o2[2];
-      if (compiled) full_e4m3x8(lo, s, o2);
+      if (compiled) full_e4m3x8(lo, s, rc, o2);
       else div_e4m3x8(lo, s, rc, o2);
       o[0] = o2[0]; o[1] = o2[1];
-      if (compiled) full_e4m3x8(hi, s, o2);
+      if (compiled) full_e4m3x8(hi, s, rc, o2);
       else div_e4m3x8(hi, s, rc, o2);
       o[2] = o2[0]; o[3] = o2[1];
     }
