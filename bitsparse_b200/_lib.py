@@ -68,6 +68,7 @@ _SIGS = {
     "bs_relu2_grad": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i32, _i32, _vp,
                              _vp]),
     "bs_fp8_scale": (_i32, [_vp, _i32, _i64, _vp, _vp, _vp]),
+    "bs_fp8_estimate_exact": (_i32, [_vp, _i32, _vp, _vp]),
     "bs_quantize_e4m3": (_i32, [_vp, _i32, _i64, _vp, _vp, _vp]),
 }
 

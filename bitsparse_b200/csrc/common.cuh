@@ -155,6 +155,14 @@ __device__ __forceinline__ uint32_t e4m3x2_bits(float a, float b) {
   return r;
 }
 
+// 1/s rounded to fp32, the quantisers' reciprocal, or 0 where it would not
+// be an accurate normal number (s zero, subnormal, at or above 2^126, inf or
+// NaN): every quantiser then takes its division for all values.
+__device__ __forceinline__ float quant_rcp(float s) {
+  const uint32_t e = (__float_as_uint(s) >> 23) & 0xFFu;
+  return (e >= 1u && e <= 252u) ? __frcp_rn(s) : 0.f;
+}
+
 // x / s in fp32, close enough that rounding it to bf16 gives bf16(x / s) of
 // the exact IEEE quotient: y1 = x*r corrected by one FMA residual step is
 // within 1 fp32 ulp of the true quotient, so its bf16 rounding can only
@@ -167,7 +175,7 @@ __device__ __forceinline__ float quotient_fp32(float x, float s, float r) {
   const float y1 = fmaf(e, r, y0);
   const uint32_t lo = __float_as_uint(y1) & 0xFFFFu;
   // the quotient has x's sign (keeps -0, which the residual loses)
-  return (lo - 0x7FFCu <= 8u) ? __fdiv_rn(x, s) : copysignf(y1, x);
+  return (r == 0.f || lo - 0x7FFCu <= 8u) ? __fdiv_rn(x, s) : copysignf(y1, x);
 }
 
 // to_fp8's quantiser on two bf16 values (as fp32): e4m3(bf16(x / s)).
@@ -186,18 +194,23 @@ __device__ __forceinline__ uint32_t div_e4m3x2(float x0, float x1, float s, floa
 static __device__ __noinline__ uint2 div_e4m3x8_exact(uint32_t w0, uint32_t w1, uint32_t w2,
                                                uint32_t w3, float s, float r) {
   const uint32_t w[4] = {w0, w1, w2, w3};
+  uint32_t b[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    b[i] = bf16x2_from_f32(__fdiv_rn(__uint_as_float(w[i] << 16), s),
+                           __fdiv_rn(__uint_as_float(w[i] & 0xFFFF0000u), s));
   uint32_t o[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i)
-    o[i] = div_e4m3x2(bf16_bits_to_f32(w[2 * i] & 0xFFFFu), bf16_bits_to_f32(w[2 * i] >> 16), s, r) |
-           div_e4m3x2(bf16_bits_to_f32(w[2 * i + 1] & 0xFFFFu),
-                      bf16_bits_to_f32(w[2 * i + 1] >> 16), s, r) << 16;
+    o[i] = e4m3x2_bits(__uint_as_float(b[2 * i] << 16), __uint_as_float(b[2 * i] & 0xFFFF0000u)) |
+           e4m3x2_bits(__uint_as_float(b[2 * i + 1] << 16),
+                       __uint_as_float(b[2 * i + 1] & 0xFFFF0000u)) << 16;
   return make_uint2(o[0], o[1]);
 }
 
 __device__ __forceinline__ void div_e4m3x8(const uint32_t (&w)[4], float s, float r,
                                            uint32_t (&o)[2]) {
-  uint32_t near = 0;
+  uint32_t near = r == 0.f;  // no usable reciprocal: divide all
   float y[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
@@ -256,7 +269,7 @@ __device__ __forceinline__ bool e4m3_code_settled(float q0) {
 // which is what Triton's cast compiles to.)
 __device__ __forceinline__ uint32_t e4m3_compiled(float x, float s, float r) {
   const float q0 = x * r;
-  return e4m3x2_bits(e4m3_code_settled(q0) ? q0 : div_full(x, s), 0.f) & 0xFFu;
+  return e4m3x2_bits(r != 0.f && e4m3_code_settled(q0) ? q0 : div_full(x, s), 0.f) & 0xFFu;
 }
 // The rare case of full_e4m3x8 (some estimate unsettled): all eight by the
 // division, out of line so that the unrolled callers stay small.
@@ -273,7 +286,7 @@ static __device__ __noinline__ uint2 full_e4m3x8_div(uint32_t w0, uint32_t w1, u
 __device__ __forceinline__ void full_e4m3x8(const uint32_t (&w)[4], float s, float r,
                                             uint32_t (&o)[2]) {
   float q[8];
-  bool all = true;
+  bool all = r != 0.f;  // no usable reciprocal: divide all
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     q[e] = __uint_as_float((w[e >> 1] >> (16 * (e & 1))) << 16) * r;
@@ -287,6 +300,81 @@ __device__ __forceinline__ void full_e4m3x8(const uint32_t (&w)[4], float s, flo
     o[0] = d.x;
     o[1] = d.y;
   }
+}
+
+// Whether the plain estimate x * r (r = 1/s rounded to fp32) gives the
+// quantiser's e4m3 code for EVERY bf16 x at this scale -- compiled:
+// e4m3(div_full(x, s)); eager: e4m3(bf16(x / s)) -- so that a kernel may
+// quantise with the estimate alone (est_e4m3x8).  Proved by exhaustion over
+// the bf16 codes that can reach a rounding boundary: with e_s the biased
+// exponent of s, a bf16 x of biased exponent E below e_s - 13 has
+// |x / s| < 2^-13 (both forms give a signed zero code) and one above
+// e_s + 11 has |x / s| > 2^11 (both saturate to +-448), so the 25 binades
+// E = e_s - 13 .. e_s + 11, both signs, and E = 255 (inf / NaN) are tested,
+// 6656 codes.  A scale whose window leaves bf16's normal exponents (or a
+// non-positive, non-finite scale) answers false.  Every thread of the block
+// must call it; the answer is uniform over the block.
+static __device__ __noinline__ bool e4m3_estimate_exact(float s, float r, bool compiled) {
+  const uint32_t es = (__float_as_uint(s) >> 23) & 0xFFu;
+  bool ok = s > 0.f && es >= 14u && es <= 243u;
+  if (ok) {  // same s in every thread: uniform
+    constexpr uint32_t kBinades = 25, kCodes = (kBinades + 1) * 256;
+    for (uint32_t i = threadIdx.x; i < kCodes; i += blockDim.x) {
+      const uint32_t g = i >> 8, e = g < kBinades ? es - 13u + g : 255u;
+      const float x = __uint_as_float((((i & 1u) << 15) | (e << 7) | ((i >> 1) & 127u)) << 16);
+      const float q = x * r;
+      uint32_t a, b;
+      if (compiled) {
+        a = e4m3x2_bits(q, 0.f);
+        b = e4m3x2_bits(div_full(x, s), 0.f);
+      } else {
+        const uint32_t h = bf16x2_from_f32(q, __fdiv_rn(x, s));
+        a = e4m3x2_bits(bf16_bits_to_f32(h & 0xFFFFu), 0.f);
+        b = e4m3x2_bits(bf16_bits_to_f32(h >> 16), 0.f);
+      }
+      ok &= a == b;
+    }
+  }
+  return __syncthreads_and(ok) != 0;
+}
+
+// The quantiser by the estimate alone, on eight bf16 values (four words,
+// low half first) -> two words of codes: e4m3(x * r) (compiled) or
+// e4m3(bf16(x * r)) (eager).  Exact where e4m3_estimate_exact(s, r, COMPILED)
+// holds.
+template <bool COMPILED>
+__device__ __forceinline__ void est_e4m3x8(const uint32_t (&w)[4], float r, uint32_t (&o)[2]) {
+  float q[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    q[2 * i] = __uint_as_float(w[i] << 16) * r;
+    q[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u) * r;
+    if constexpr (!COMPILED) {
+      const uint32_t h = bf16x2_from_f32(q[2 * i], q[2 * i + 1]);
+      q[2 * i] = __uint_as_float(h << 16);
+      q[2 * i + 1] = __uint_as_float(h & 0xFFFF0000u);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    o[i] = e4m3x2_bits(q[4 * i], q[4 * i + 1]) | e4m3x2_bits(q[4 * i + 2], q[4 * i + 3]) << 16;
+}
+
+// Elementwise bf16x2 sum / product, rounded to nearest even.  Equal to
+// torch's bf16 arithmetic (the fp32 result rounded to bf16): fp32 carries
+// more than 2 * 8 + 2 significant bits, so rounding first to fp32 and then
+// to bf16 gives the correctly rounded sum; a product of two bf16 values is
+// exact in fp32 wherever it is normal, and in fp32's subnormal range the
+// two roundings agree as well.
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
 
 // torch.relu on two bf16: strictly negative values (incl. -inf) -> +0;

@@ -201,7 +201,7 @@ __device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64
     for (int i = 0; i < C::SW; ++i) sv[i] = 0;
     if constexpr (DT_IN == BS_BF16) {
       // |x / scale| <= 448 * (1 + 2^-8): the fast paths are exact here
-      const float r = __frcp_rn(qs);
+      const float r = quant_rcp(qs);
       static_assert(C::VEC % 8 == 0, "groups of eight values");
 #pragma unroll
       for (int g = 0; g < C::VEC / 8; ++g) {
@@ -216,7 +216,7 @@ __device__ __forceinline__ uint32_t process_chunk(const CompressParams &P, int64
 #pragma unroll
       for (int e = 0; e < C::VEC; ++e) {
         if (P.qcompiled) {
-          sv[e >> 2] |= e4m3_compiled(__uint_as_float(raw[e]), qs, __frcp_rn(qs)) << (8 * (e & 3));
+          sv[e >> 2] |= e4m3_compiled(__uint_as_float(raw[e]), qs, quant_rcp(qs)) << (8 * (e & 3));
           continue;
         }
         const float y = __fdiv_rn(__uint_as_float(raw[e]), qs);
@@ -825,9 +825,16 @@ __global__ void __launch_bounds__(NW * 32, MINB)
       if (i * G + b < nparts) fetch(i * G + b, i);
 
   const float qs = QUANT ? *P.qscale : 1.f;
-  const float qr = QUANT ? __frcp_rn(qs) : 1.f;
+  const float qr = QUANT ? quant_rcp(qs) : 1.f;
   const float qs2 = (QUANT && BIAS && P.qscale2 != nullptr) ? *P.qscale2 : 1.f;
-  const float qr2 = __frcp_rn(qs2);
+  const float qr2 = quant_rcp(qs2);
+  // the estimate alone quantises exactly at these scales (checked per CTA,
+  // while the first partitions are in flight)
+  bool qfast = false, qfast2 = false;
+  if constexpr (QUANT) {
+    qfast = e4m3_estimate_exact(qs, qr, QC);
+    if constexpr (BIAS) qfast2 = P.qscale2 != nullptr && e4m3_estimate_exact(qs2, qr2, QC);
+  }
   const uint32_t epoch = s_epoch;
   long long known_end = 0, known = -1;  // end (count) through this CTA's last flushed partition
   for (long long r = 0;; ++r) {
@@ -912,11 +919,7 @@ __global__ void __launch_bounds__(NW * 32, MINB)
             // rows past M (TMA zero fill) stay 0: the bias must not reach them
             const uint32_t live = grow < P.M ? 0xFFFFFFFFu : 0u;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float lo = bf16_bits_to_f32(v[s4][i] & 0xFFFFu) + bf16_bits_to_f32(bw[i] & 0xFFFFu);
-              const float hi = bf16_bits_to_f32(v[s4][i] >> 16) + bf16_bits_to_f32(bw[i] >> 16);
-              v[s4][i] = relu_bf16x2(bf16x2_from_f32(lo, hi)) & live;
-            }
+            for (int i = 0; i < 4; ++i) v[s4][i] = relu_bf16x2(bf16x2_add(v[s4][i], bw[i])) & live;
             if (P.relu_out != nullptr && grow < P.M) {
               uint8_t *dst = P.relu_out + (grow * P.relu_ld + bcol) * 2;
               if (bcol + 8 <= P.N) {
@@ -930,7 +933,10 @@ __global__ void __launch_bounds__(NW * 32, MINB)
           }
           if constexpr (QUANT) {
             uint32_t qw[2] = {0, 0}, side[2];
-            if constexpr (QC) {  // quantise as the compiled to_fp8
+            if (qfast) {
+              const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
+              est_e4m3x8<QC>(h4, qr, qw);
+            } else if constexpr (QC) {  // quantise as the compiled to_fp8
               const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
               full_e4m3x8(h4, qs, qr, qw);
             } else if constexpr (BIAS) {
@@ -951,12 +957,9 @@ __global__ void __launch_bounds__(NW * 32, MINB)
                 // side output: e4m3(bf16(h * h) / scale2) (h.square_() then to_fp8)
                 uint32_t sq[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float h0 = bf16_bits_to_f32(v[s4][i] & 0xFFFFu);
-                  const float h1 = bf16_bits_to_f32(v[s4][i] >> 16);
-                  sq[i] = bf16x2_from_f32(h0 * h0, h1 * h1);  // h.square_()
-                }
-                if constexpr (QC) full_e4m3x8(sq, qs2, qr2, side);
+                for (int i = 0; i < 4; ++i) sq[i] = bf16x2_mul(v[s4][i], v[s4][i]);  // h.square_()
+                if (qfast2) est_e4m3x8<QC>(sq, qr2, side);
+                else if constexpr (QC) full_e4m3x8(sq, qs2, qr2, side);
                 else div_e4m3x8(sq, qs2, qr2, side);
               }
             }

@@ -141,8 +141,13 @@ template <int DT>
 __global__ void __launch_bounds__(kThreads)
 quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q, int compiled) {
   const float s = *scale;
-  const float r = __frcp_rn(s);
+  const float r = quant_rcp(s);
   const int64_t stride = (int64_t)gridDim.x * kThreads;
+  // with 16+ groups per thread the once-per-block exactness check of the
+  // plain estimate pays for itself (the condition is uniform over the grid)
+  bool fast = false;
+  if constexpr (DT == BS_BF16)
+    if ((n + 7) / 8 >= 16 * stride) fast = e4m3_estimate_exact(s, r, compiled != 0);
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i * 8 < n; i += stride) {
     uint32_t o[2] = {0, 0};
     const int64_t e0 = i * 8;
@@ -173,8 +178,14 @@ quant_kernel(const uint8_t *x, int64_t n, const float *scale, uint8_t *q, int co
       // fast e4m3 conversion applies (NaN stays NaN).
       const uint32_t w4[4] = {b[0] | b[1] << 16, b[2] | b[3] << 16, b[4] | b[5] << 16,
                               b[6] | b[7] << 16};
-      if (compiled) full_e4m3x8(w4, s, r, o);
-      else div_e4m3x8(w4, s, r, o);
+      if (fast) {
+        if (compiled) est_e4m3x8<true>(w4, r, o);
+        else est_e4m3x8<false>(w4, r, o);
+      } else if (compiled) {
+        full_e4m3x8(w4, s, r, o);
+      } else {
+        div_e4m3x8(w4, s, r, o);
+      }
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -207,7 +218,7 @@ quant2d_kernel(const uint8_t *x, int64_t R, int64_t C, int64_t ld, const float *
                int compiled) {
   __shared__ uint8_t t[64][64 + 4];
   const float s = *scale;
-  const float rc = __frcp_rn(s);
+  const float rc = quant_rcp(s);
   const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
   const int tid = threadIdx.x;
   {  // row tid/4, 16 values at column (tid%4)*16
@@ -412,5 +423,18 @@ extern "C" int bs_quantize_e4m3_2d(const void *x, int64_t R, int64_t C, int64_t 
   quant2d_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t *>(x), R, C, ld, scale, q, ldq, qT, ldqT, vx, vq, vqT,
       (fp8_flags & BS_FP8_COMPILED) != 0);
+  return launch_err();
+}
+
+__global__ void estimate_exact_kernel(const float *scale, int compiled, int *out) {
+  const float s = *scale;
+  const bool ok = e4m3_estimate_exact(s, quant_rcp(s), compiled != 0);
+  if (threadIdx.x == 0) *out = ok ? 1 : 0;
+}
+
+extern "C" int bs_fp8_estimate_exact(const float *scale, int fp8_flags, int *out, void *stream) {
+  if (!scale || !out) return BS_ERR_ARG;
+  estimate_exact_kernel<<<1, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      scale, (fp8_flags & BS_FP8_COMPILED) != 0, out);
   return launch_err();
 }

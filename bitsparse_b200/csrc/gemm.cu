@@ -172,13 +172,6 @@ __device__ __forceinline__ uint32_t bf16x2_rn(uint32_t lo, uint32_t hi) {
   return r;
 }
 
-// Elementwise bf16x2 product, rounded to nearest even.
-__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
 // 32 consecutive fp32 columns of this thread's TMEM lane (no wait).
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t *r) {
   asm volatile(

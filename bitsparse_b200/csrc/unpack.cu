@@ -223,8 +223,8 @@ __device__ __forceinline__ uint32_t relu2_out(const UnpackParams &P, uint32_t v)
   }
   if constexpr (OUT == 2) {  // to_fp8's quantiser on the bf16 tensor (eager or compiled)
     const float qs = *P.qscale;
-    v = P.qcompiled ? e4m3_compiled(bf16_bits_to_f32(v), qs, __frcp_rn(qs))
-                    : div_e4m3x2(bf16_bits_to_f32(v), 0.f, qs, __frcp_rn(qs)) & 0xFFu;
+    v = P.qcompiled ? e4m3_compiled(bf16_bits_to_f32(v), qs, quant_rcp(qs))
+                    : div_e4m3x2(bf16_bits_to_f32(v), 0.f, qs, quant_rcp(qs)) & 0xFFu;
   }
   return v;
 }

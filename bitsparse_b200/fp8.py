@@ -120,6 +120,20 @@ def quantize_e4m3(x: Tensor, scale: Tensor) -> Tensor:
     return q.T if transposed else q
 
 
+def estimate_exact(scale: Tensor) -> bool:
+    """Whether the quantisers take the plain estimate x * (1/scale) at this
+    scale in the current semantics (an exhaustive check over the bf16 codes
+    that can reach an e4m3 rounding boundary; bs_fp8_estimate_exact).  They
+    divide where it is False; the codes are the same either way."""
+    from . import _lib, _runtime as R
+
+    R.require_cuda(scale, "scale")
+    out = torch.empty(1, dtype=torch.int32, device=scale.device)
+    _lib.call("bs_fp8_estimate_exact", scale.data_ptr(), fp8_flags(), out.data_ptr(),
+              R.stream_handle(scale.device))
+    return bool(out.item())
+
+
 @torch.no_grad()
 def to_fp8(x: Tensor) -> tuple[Tensor, Tensor]:
     """(x_fp8, scale): per-tensor e4m3fn quantisation (lib_sparse/fp8.py:123-129)."""

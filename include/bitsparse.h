@@ -239,6 +239,15 @@ int bs_quantize_e4m3_2d(const void *x, int64_t R, int64_t C, int64_t ld, const f
                         uint8_t *q, int64_t ldq, uint8_t *qT, int64_t ldqT, int fp8_flags,
                         void *stream);
 
+/* Whether the quantisers may take the plain estimate x * (1 / *scale) for
+ * every bf16 x at this scale (fp8_flags: BS_FP8_COMPILED or 0): *out = 1 if
+ * an exhaustive check over the bf16 codes that can reach an e4m3 rounding
+ * boundary finds the estimate's code equal to the definition's for each,
+ * else 0.  The compress and quantise kernels run the same check per CTA and
+ * divide where it answers 0; this entry point reports the answer (tests,
+ * diagnostics).  out: one device int. */
+int bs_fp8_estimate_exact(const float *scale, int fp8_flags, int *out, void *stream);
+
 /* Status of the reconstruct kernels of the current device (bs_unpack has
  * no status argument): *status_out = BS_STATUS_* bits OR-ed since the last
  * reset (BS_STATUS_TIMEOUT: a bounded wait on the bulk copies of the
@@ -338,9 +347,15 @@ int bs_fp8_scale(const void *x, int dtype, int64_t numel, uint32_t *amax_ws,
                  float *scale_out, void *stream);
 
 /* q = e4m3fn(x / *scale) elementwise over `numel` elements of a bf16 or
- * fp32 tensor (bf16: the quotient is rounded to bf16 first) -- the quantise
- * step of to_fp8 (lib_sparse/fp8.py:127).  x 16-byte aligned, q 8-byte
- * aligned. */
+ * fp32 tensor -- the quantise step of to_fp8 (lib_sparse/fp8.py:127).
+ * Eager semantics round a bf16 input's quotient to bf16 first; with
+ * BS_FP8_COMPILED in dtype the quotient is Triton's fp32 division, as the
+ * reference's compiled to_fp8 computes it.  Quotients beyond +-464 (never
+ * produced by to_fp8's own scales, |x / scale| <= 448 * (1 + 2^-8))
+ * saturate to +-448 for bf16 input, as Triton's cast does.  The kernel
+ * quantises by the estimate x * (1 / scale) where bs_fp8_estimate_exact
+ * holds at the scale and divides otherwise: same codes.  x 16-byte aligned,
+ * q 8-byte aligned. */
 int bs_quantize_e4m3(const void *x, int dtype, int64_t numel, const float *scale,
                      uint8_t *q, void *stream);
 

@@ -155,3 +155,70 @@ def test_to_fp8_compiled_and_eager(mag):
             q = quantize_e4m3(x, s)
         assert s.item() == sr.item(), mode
         assert torch.equal(q.view(torch.uint8), qr.view(torch.uint8)), mode
+
+
+@pytest.mark.parametrize("mode", ["compiled", "eager"])
+@pytest.mark.parametrize("mag", [1.0, 5e37])
+def test_estimate_path_and_division_path(mode, mag):
+    """The quantisers use the plain estimate x * (1/s) wherever a per-block
+    exhaustive check over the bf16 codes proves it gives the definition's
+    codes at that scale, and the checked division otherwise.  Magnitude 1
+    takes the estimate; 5e37 gives a scale above 2^116, outside the check's
+    window, so the division path runs.  Both must equal the reference's
+    to_fp8 bit for bit: the flat quantiser (8192 x 10240 gives every thread
+    the 16+ groups its check needs), the fused quantise + compress, and the
+    fused bias + ReLU (+ square) compress."""
+    from bitsparse_b200.fp8 import estimate_exact, fp8_semantics, to_fp8
+    from bitsparse_b200.src.functions import relu_to_tilesparse_fp8
+    from bitsparse_b200.src.operators import compress_bias_relu_fp8
+    from tests.gpu_util import reference_to_fp8
+    compiled = mode == "compiled"
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = (torch.randn(8192, 10240, generator=g, device="cuda") * mag).to(torch.bfloat16)
+    b = (torch.randn(10240, generator=g, device="cuda") * (0.25 * mag)).to(torch.bfloat16)
+    qr, sr = reference_to_fp8(x, compiled)
+    with fp8_semantics(mode):
+        q, s = to_fp8(x)
+        assert estimate_exact(s) == (mag == 1.0)
+    assert s.item() == sr.item()
+    assert torch.equal(q.view(torch.uint8), qr.view(torch.uint8))
+    h = torch.relu(x)
+    qr, sr = reference_to_fp8(h, compiled)
+    with fp8_semantics(mode):
+        q, sp = relu_to_tilesparse_fp8(h)
+    assert sp.scale.item() == sr.item()
+    assert torch.equal(q.view(torch.uint8), qr.view(torch.uint8))
+    h = torch.relu(x + b)
+    square = mag == 1.0  # h * h of the large case would overflow bf16
+    qr, sr = reference_to_fp8(h * h if square else h, compiled)
+    with fp8_semantics(mode):
+        side, side_scale, sp = compress_bias_relu_fp8(x, b, None, False, square=square)
+    assert side_scale.item() == sr.item()
+    assert torch.equal(side.view(torch.uint8), qr.view(torch.uint8))
+    B.check_status()
+
+
+@pytest.mark.parametrize("mode", ["compiled", "eager"])
+def test_quantise_at_scales_outside_the_check(mode):
+    """quantize_e4m3 with a caller's scale that the exactness check refuses
+    (2^-133, fp32-subnormal, whose reciprocal overflows): the division path
+    gives the definition's codes, e4m3(x / s) by Triton's division
+    (compiled) or e4m3(bf16(x / s)) (eager).  The scale is a bf16 value, as
+    to_fp8's eager scales are (torch's eager division rounds an fp32 scale
+    to the bf16 operand's type first), and |x / s| stays within e4m3's
+    range, where torch's eager cast and the saturating hardware conversion
+    agree."""
+    from bitsparse_b200.fp8 import estimate_exact, fp8_semantics
+    g = torch.Generator(device="cuda").manual_seed(6)
+    x = (torch.randn(8192, 10240, generator=g, device="cuda") * 1e-39).to(torch.bfloat16)
+    s = torch.tensor(2.0 ** -133, device="cuda", dtype=torch.float32)
+    with fp8_semantics(mode):
+        assert not estimate_exact(s)
+
+    def ref(t, sc):
+        return (t / sc).to(torch.float8_e4m3fn)
+
+    qr = (torch.compile(ref) if mode == "compiled" else ref)(x, s)
+    with fp8_semantics(mode):
+        q = quantize_e4m3(x, s)
+    assert torch.equal(q.view(torch.uint8), qr.view(torch.uint8))
