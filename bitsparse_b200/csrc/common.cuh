@@ -360,6 +360,18 @@ __device__ __forceinline__ void est_e4m3x8(const uint32_t (&w)[4], float r, uint
     o[i] = e4m3x2_bits(q[4 * i], q[4 * i + 1]) | e4m3x2_bits(q[4 * i + 2], q[4 * i + 3]) << 16;
 }
 
+// The quantiser where the estimate alone is not known exact, out of line
+// (the rare path of kernels that check e4m3_estimate_exact): eight bf16
+// values -> two words of codes, compiled or eager semantics.
+static __device__ __noinline__ uint2 quant8_checked(uint32_t w0, uint32_t w1, uint32_t w2,
+                                                    uint32_t w3, float s, float r, bool compiled) {
+  const uint32_t w[4] = {w0, w1, w2, w3};
+  uint32_t o[2];
+  if (compiled) full_e4m3x8(w, s, r, o);
+  else div_e4m3x8(w, s, r, o);
+  return make_uint2(o[0], o[1]);
+}
+
 // Elementwise bf16x2 sum / product, rounded to nearest even.  Equal to
 // torch's bf16 arithmetic (the fp32 result rounded to bf16): fp32 carries
 // more than 2 * 8 + 2 significant bits, so rounding first to fp32 and then

@@ -933,22 +933,15 @@ __global__ void __launch_bounds__(NW * 32, MINB)
           }
           if constexpr (QUANT) {
             uint32_t qw[2] = {0, 0}, side[2];
-            if (qfast) {
+            {
               const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
-              est_e4m3x8<QC>(h4, qr, qw);
-            } else if constexpr (QC) {  // quantise as the compiled to_fp8
-              const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
-              full_e4m3x8(h4, qs, qr, qw);
-            } else if constexpr (BIAS) {
-              const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
-              div_e4m3x8(h4, qs, qr, qw);
-            } else {
-              // (the per-value form measures faster here; the codes are the same)
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                qw[i >> 1] |= div_e4m3x2(bf16_bits_to_f32(v[s4][i] & 0xFFFFu),
-                                         bf16_bits_to_f32(v[s4][i] >> 16), qs, qr)
-                              << (16 * (i & 1));
+              if (qfast) {
+                est_e4m3x8<QC>(h4, qr, qw);
+              } else {
+                const uint2 c = quant8_checked(h4[0], h4[1], h4[2], h4[3], qs, qr, QC);
+                qw[0] = c.x;
+                qw[1] = c.y;
+              }
             }
             side[0] = qw[0];
             side[1] = qw[1];
@@ -958,9 +951,13 @@ __global__ void __launch_bounds__(NW * 32, MINB)
                 uint32_t sq[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) sq[i] = bf16x2_mul(v[s4][i], v[s4][i]);  // h.square_()
-                if (qfast2) est_e4m3x8<QC>(sq, qr2, side);
-                else if constexpr (QC) full_e4m3x8(sq, qs2, qr2, side);
-                else div_e4m3x8(sq, qs2, qr2, side);
+                if (qfast2) {
+                  est_e4m3x8<QC>(sq, qr2, side);
+                } else {
+                  const uint2 c = quant8_checked(sq[0], sq[1], sq[2], sq[3], qs2, qr2, QC);
+                  side[0] = c.x;
+                  side[1] = c.y;
+                }
               }
             }
             v[s4][0] = qw[0]; v[s4][1] = qw[1];

@@ -630,6 +630,458 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// K5 -- the weight-gradient GEMM with the reconstruct fused into its B
+// producer (AspB / AspRelu2B, lib_sparse/src/sparse_matmul.py:9-47, :91-132):
+//
+//   C[D, H] = g^T[D, T] . h[T, H]      h = unpack(stored)  or  k * unpack(stored)^2
+//
+// g is row-major [T, D] (grad_output), so A = g^T is MN-major; h is a bf16
+// bitsparse tensor [T, H].  The contraction runs over tokens, and a 64-token
+// x 64-column box of h is exactly one compressed tile: the B operand of a
+// stage is expanded straight from the compressed form into the 128-byte
+// swizzled MN-major layout tcgen05.mma reads, so the dense h never exists in
+// HBM.  CTA pairs (cta_group::2) share 256 x 256 tiles of C; per 64-token K
+// block a CTA loads its 128 rows of A (two 64 x 64 TMA boxes of g) and
+// expands its 128 columns of B (two tiles of h).
+//   warp 0      producer: A by TMA into the stage; the two tiles' bitmasks and
+//               value run (one contiguous 16-byte aligned superset) by 1-D
+//               bulk copies into a compressed-data slot, the tile prefixes
+//               read ahead through a cp.async ring;
+//   warp 1      MMA issuer (leader CTA), as in K3 with both operands MN-major;
+//   warps 2..5  epilogue (as K3 without a mask);
+//   warps 6..13 expanders: warp 6 + 4j + q expands rows 16q .. 16q + 15 of
+//               tile j -- lane = (row, 8-column chunk): the chunk's mask byte,
+//               its first rank from a scan of the row counts, the ranks of
+//               its 8 positions from one nibble-packed prefix sum, the set
+//               values read from the staged run (independent loads), one
+//               16-byte swizzled store -- then fence.proxy.async and an
+//               arrive on the leader's "full" barrier (which also counts the
+//               leader's A bytes).
+// All waits are bounded (BS_STATUS_TIMEOUT); copies in flight are waited for
+// before the CTA exits; TMEM is always freed.
+constexpr int kThreadsD = 448;  // 14 warps
+struct DwCfg {
+  static constexpr int BM = 2 * kBM;          // rows of C per pair tile
+  static constexpr int ABYTES = 2 * 8192;     // this CTA's 128 rows of A: two 64 x 64 atoms
+  static constexpr int BBYTES = 2 * 8192;     // this CTA's 128 columns of B: two tiles
+  static constexpr int STAGE = ABYTES + BBYTES;
+  static constexpr int NST = 4;
+  static constexpr int RS = 3;                // compressed-data slots
+  static constexpr int RMETA = 16, RMASK = 2 * kTileBytes, RVALS = 2 * 8192 + 32;
+  static constexpr int RSLOT = RMETA + RMASK + RVALS;
+  static constexpr int LA = 8;                // prefix read-ahead (steps)
+  static constexpr size_t SMEM = 1024 + (size_t)NST * STAGE + (size_t)RS * RSLOT + kEpiBytes +
+                                 LA * 16 + 512;
+  // fp32 accumulator, bf16 A and B, both MN-major, N = 256, M = 256
+  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) |
+                                    (1u << 16) | ((uint32_t)(kBN >> 3) << 17) |
+                                    ((uint32_t)(BM >> 4) << 24);
+};
+static_assert(DwCfg::RSLOT % 16 == 0, "bulk-copy destinations stay 16-byte aligned");
+static_assert(DwCfg::STAGE % 1024 == 0 && kEpiBytes % 1024 == 0,
+              "stages and staging boxes stay on 1024-byte boundaries");
+
+struct DwParams {
+  uint8_t *C;
+  int64_t M, N, K, ldc;      // D, H, T
+  const uint8_t *vals;       // stored values (bf16), 16-byte aligned base
+  const uint8_t *bitmask;    // [grid_m * grid_n] tiles of 512 bytes
+  const uint32_t *prefix;    // [grid_m * grid_n + 1]
+  const int64_t *vals_offset;
+  int64_t grid_n;            // tile columns of h: ceil(H / 64)
+  int c_tma;
+  int32_t *status;
+};
+
+__device__ __forceinline__ void mbar_arrive_local(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+// Bounded wait with cluster-scope acquire (the barrier counts arrivals
+// released by the peer CTA of the pair).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity,
+                                                  int32_t *status) {
+  for (uint32_t n = 0; n < kMaxPolls; ++n) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(saddr(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  status_or(status, BS_STATUS_TIMEOUT);
+  return false;
+}
+// Explicit shared-space accesses (the aligned dynamic shared-memory base is
+// formed through an integer, which hides the state space from the compiler).
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint64_t lds_u64(uint32_t a) {
+  uint64_t v;
+  asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(saddr(dst)), "l"(src) : "memory");
+}
+
+template <bool RELU2>
+__global__ void __launch_bounds__(kThreadsD, 1)
+    dw_unpack_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmC, const DwParams P) {
+  using G = DwCfg;
+  constexpr int CG = 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  // stages and the epilogue's swizzled staging boxes on 1024-byte
+  // boundaries (the 128-byte swizzle atoms), then the compressed-data slots
+  uint8_t *epi = smem + (size_t)G::NST * G::STAGE;   // epilogue staging boxes
+  uint8_t *raw = epi + kEpiBytes;                     // compressed-data slots
+  uint32_t *pref = reinterpret_cast<uint32_t *>(raw + (size_t)G::RS * G::RSLOT);  // prefix ring
+  uint64_t *full = reinterpret_cast<uint64_t *>(pref + 4 * G::LA);
+  uint64_t *empty = full + G::NST;
+  uint64_t *rfull = empty + G::NST;
+  uint64_t *rempty = rfull + G::RS;
+  uint64_t *acc_full = rempty + G::RS;
+  uint64_t *acc_empty = acc_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int64_t cid = (int64_t)blockIdx.x / CG, ncl = (int64_t)gridDim.x / CG;
+  const int nk = (int)((P.K + kBK - 1) / kBK);
+  const int64_t mt = (P.M + G::BM - 1) / G::BM, nt = (P.N + kBN - 1) / kBN;
+  const int64_t ntiles = mt * nt;
+
+  if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    for (int s = 0; s < G::NST; ++s) {
+      mbar_init(&full[s], 1 + 8 * CG);  // leader's A arrival + every expander warp of the pair
+      mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < G::RS; ++r) {
+      mbar_init(&rfull[r], 1);
+      mbar_init(&rempty[r], 8);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4 * CG);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(tmem_slot)),
+                 "r"(2 * kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // steps of this CTA: (its tile i = step / nk, K block step % nk)
+  const int64_t my_tiles = cid < ntiles ? (ntiles - cid + ncl - 1) / ncl : 0;
+  const int64_t nsteps = my_tiles * nk;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int64_t voff = *P.vals_offset;
+      // A step cursor: this CTA's tile t (its m / n block), K block kb, the
+      // tile index of its first tile column of h and how many of its two
+      // tiles exist (0 past the right edge of h).  Advanced without divisions.
+      struct Cursor {
+        int64_t t, mb, nb, c0;
+        int kb, ntl;
+      };
+      auto at_tile = [&](Cursor &c, int64_t t) {
+        c.t = t;
+        c.kb = 0;
+        if (t < ntiles) {
+          tile_coords(t, mt, nt, c.mb, c.nb);
+          c.c0 = c.nb * 4 + 2 * (int64_t)rank;
+          c.ntl = c.c0 < P.grid_n ? (c.c0 + 1 < P.grid_n ? 2 : 1) : 0;
+        }
+      };
+      auto advance = [&](Cursor &c) {
+        if (++c.kb == nk) at_tile(c, c.t + ncl);
+      };
+      // read ahead: ring entry i holds prefix[tfirst], [+1], [+ntl] of the
+      // step LA steps after the one that last used it
+      Cursor ahead;
+      at_tile(ahead, cid);
+      int ring_in = 0;
+      auto issue_prefix = [&]() {
+        if (ahead.t < ntiles) {
+          const int64_t tf = (int64_t)ahead.kb * P.grid_n + ahead.c0;
+          uint32_t *e = pref + 4 * ring_in;
+          if (ahead.ntl) {
+            cp_async4(e, P.prefix + tf);
+            cp_async4(e + 1, P.prefix + tf + 1);
+            cp_async4(e + 2, P.prefix + tf + ahead.ntl);
+          }
+          advance(ahead);
+        }
+        cp_async_commit();  // (possibly empty) group: one per step
+        if (++ring_in == G::LA) ring_in = 0;
+      };
+      for (int i = 0; i < G::LA; ++i) issue_prefix();
+      Cursor cur;
+      at_tile(cur, cid);
+      int s = 0, rs = 0, ring = 0;
+      uint32_t sph = 0, rph = 0;  // use parity of stage s / slot rs
+      bool ok = true;
+      int64_t j = 0;
+      for (; j < nsteps && ok; ++j) {
+        // A: this CTA's 128 rows (columns of g) for tokens kb*64 ..
+        if (j >= G::NST && !mbar_wait(&empty[s], sph ^ 1u, P.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t *a = smem + (size_t)s * G::STAGE;
+        if (leader) mbar_expect_tx(&full[s], 2 * G::ABYTES);
+        const uint32_t bar = map_rank(saddr(&full[s]), 0);
+        const int ax = (int)(cur.mb * G::BM + rank * kBM);
+        tma_load_2d_pair(a, &tmA, ax, cur.kb * kBK, bar);
+        tma_load_2d_pair(a + 8192, &tmA, ax + 64, cur.kb * kBK, bar);
+        // the compressed tiles of B
+        if (j >= G::RS && !mbar_wait(&rempty[rs], rph ^ 1u, P.status)) {
+          ok = false;
+          break;
+        }
+        const int ntl = cur.ntl;
+        const int64_t tfirst = (int64_t)cur.kb * P.grid_n + cur.c0;
+        cp_async_wait<G::LA - 1>();  // step j's prefixes are in
+        const uint32_t *e = pref + 4 * ring;
+        uint8_t *slot = raw + (size_t)rs * G::RSLOT;
+        uint32_t mbytes = 0, vbytes = 0;
+        int64_t a0 = 0;
+        uint32_t *meta = reinterpret_cast<uint32_t *>(slot);
+        if (ntl) {
+          const uint32_t p0 = e[0], p1 = e[1], p2 = e[2];
+          const int64_t b0 = (voff + p0) * 2, b1 = (voff + p2) * 2;
+          a0 = b0 & ~(int64_t)15;
+          const int64_t a1 = (b1 + 15) & ~(int64_t)15;
+          vbytes = p2 > p0 ? (uint32_t)(a1 - a0) : 0u;  // no values: no copy
+          mbytes = (uint32_t)ntl * kTileBytes;
+          meta[0] = (uint32_t)((b0 - a0) >> 1);  // first value's position in the slot
+          meta[1] = p1 - p0;                      // values of the first tile
+        }
+        meta[2] = (uint32_t)ntl;
+        issue_prefix();  // the ring entry just read is reused for step j + LA
+        mbar_expect_tx(&rfull[rs], mbytes + vbytes);  // also releases the meta words
+        if (mbytes) bulk_load(slot + G::RMETA, P.bitmask + tfirst * kTileBytes, mbytes, &rfull[rs]);
+        if (vbytes) bulk_load(slot + G::RMETA + G::RMASK, P.vals + a0, vbytes, &rfull[rs]);
+        advance(cur);
+        if (++ring == G::LA) ring = 0;
+        if (++s == G::NST) { s = 0; sph ^= 1u; }
+        if (++rs == G::RS) { rs = 0; rph ^= 1u; }
+      }
+      cp_async_wait<0>();
+      // every copy landed before the CTA may exit
+      for (int64_t i = j - G::RS < 0 ? 0 : j - G::RS; i < j; ++i)
+        mbar_wait(&rfull[i % G::RS], (uint32_t)((i / G::RS) & 1), P.status);
+      if (leader)
+        for (int64_t i = j - G::NST < 0 ? 0 : j - G::NST; i < j; ++i)
+          mbar_wait_cluster(&full[i % G::NST], (uint32_t)((i / G::NST) & 1), P.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      int64_t it = 0;
+      int jt = 0;
+      bool ok = true;
+      for (int64_t t = cid; t < ntiles && ok; t += ncl, ++jt) {
+        const int buf = jt & 1;
+        if (jt >= 2 && !mbar_wait(&acc_empty[buf], (uint32_t)(((jt >> 1) - 1) & 1), P.status))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * kTmemCols);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % G::NST);
+          if (!mbar_wait_cluster(&full[s], (uint32_t)((it / G::NST) & 1), P.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = saddr(smem + (size_t)s * G::STAGE);
+          const uint32_t b = a + G::ABYTES;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // both MN-major: 64-element atoms 8 KB apart (LBO), 8-row K
+            // groups 1024 B apart (SBO); +2048 B per K = 16
+            const uint64_t ad = smem_desc(a + 2048 * k, 8192, 1024);
+            const uint64_t bd = smem_desc(b + 2048 * k, 8192, 1024);
+            mma_bf16<CG>(d, ad, bd, G::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit_to<CG>(saddr(&empty[s]));
+          mma_commit_to<CG>(map_rank(saddr(&empty[s]), 1));
+        }
+        mma_commit_to<CG>(saddr(&acc_full[buf]));
+        mma_commit_to<CG>(map_rank(saddr(&acc_full[buf]), 1));
+      }
+    }
+  } else if (warp < 6) {
+    // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (this CTA's rows)
+    const int q = warp & 3;
+    const uint32_t acc_empty_leader = map_rank(saddr(acc_empty), 0);
+    int jt = 0;
+    for (int64_t t = cid; t < ntiles; t += ncl, ++jt) {
+      int64_t mb, nb;
+      tile_coords(t, mt, nt, mb, nb);
+      const int64_t row0 = mb * G::BM + rank * kBM + 32 * q;
+      const int64_t m = row0 + lane, n0 = nb * kBN;
+      const int buf = jt & 1;
+      const bool ok = mbar_wait(&acc_full[buf], (uint32_t)((jt >> 1) & 1), P.status);
+      tc_fence_after();
+      const uint32_t zero_guard = ok ? 0xFFFFFFFFu : 0u;
+      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTmemCols);
+#pragma unroll
+      for (int c = 0; c < kBN / 64; ++c) {
+        uint32_t r[64];
+        tmem_ld32_nowait(tbase + (uint32_t)(64 * c), r);
+        tmem_ld32_nowait(tbase + (uint32_t)(64 * c + 32), r + 32);
+        tmem_wait_ld();
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = bf16x2_rn(r[2 * i], r[2 * i + 1]) & zero_guard;
+        const int64_t n = n0 + 64 * c;
+        if (P.c_tma) {
+          uint8_t *box = epi + (size_t)(q * 2 + (c & 1)) * kEpiBox;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint4 *>(box + lane * 128 + ((i ^ (lane & 7)) * 16)) =
+                make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0 && n < P.N && row0 < P.M) {
+            asm volatile(
+                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                    reinterpret_cast<uint64_t>(&tmC)),
+                "r"((int)n), "r"((int)row0), "r"(saddr(box))
+                : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        } else if (m < P.M) {
+          for (int i = 0; i < 64 && n + i < P.N; ++i)
+            reinterpret_cast<uint16_t *>(P.C + (m * P.ldc + n) * 2)[i] =
+                (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader + (uint32_t)(8 * buf));
+    }
+  } else {
+    // expanders: warp 6 + 4 * tj + qq -> rows 16 qq .. + 15 of this CTA's tile tj
+    const int e = warp - 6, tj = e >> 2, qq = e & 3;
+    const int r0 = 16 * qq;
+    const uint32_t full_leader = map_rank(saddr(full), 0);
+    int s = 0, rs = 0;
+    uint32_t sph = 0, rph = 0;
+    for (int64_t j = 0; j < nsteps; ++j) {
+      if (!mbar_wait(&rfull[rs], rph, P.status)) break;
+      if (j >= G::NST && !mbar_wait(&empty[s], sph ^ 1u, P.status)) break;
+      const uint32_t slot = saddr(raw + (size_t)rs * G::RSLOT);
+      const uint32_t box = saddr(smem + (size_t)s * G::STAGE + G::ABYTES + tj * 8192);
+      const uint32_t ntl = lds_u32(slot + 8);
+      if (tj < (int)ntl) {
+        const uint32_t mw = slot + G::RMETA + tj * kTileBytes;  // the tile's 64 row words
+        const uint32_t sv = slot + G::RMETA + G::RMASK;          // staged values (bf16)
+        // values of the tile's rows before this warp's 16
+        uint32_t before = 0;
+        if (qq) {
+          const uint64_t wa = lds_u64(mw + 8 * lane), wb = lds_u64(mw + 8 * (32 + lane));
+          before = (lane < r0 ? (uint32_t)__popcll(wa) : 0u) +
+                   (lane + 32 < r0 ? (uint32_t)__popcll(wb) : 0u);
+          before = __reduce_add_sync(0xFFFFFFFFu, before);
+        }
+        // lanes l and l + 16 hold row r0 + l: its word and first value's slot position
+        const uint64_t my = lds_u64(mw + 8 * (r0 + (lane & 15)));
+        const uint32_t cnt = (uint32_t)__popcll(my);
+        uint32_t inc = cnt;
+#pragma unroll
+        for (int d = 1; d < 16; d <<= 1) {
+          const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, d, 16);
+          if ((lane & 15) >= d) inc += v;
+        }
+        const uint32_t rowbase =
+            lds_u32(slot) + (tj ? lds_u32(slot + 4) : 0u) + before + inc - cnt;
+        const uint32_t mlo = (uint32_t)my, mhi = (uint32_t)(my >> 32);
+        const int c = lane & 7;
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+          const int rl = 4 * st + (lane >> 3);  // row within this warp's 16
+          const uint32_t wlo = __shfl_sync(0xFFFFFFFFu, mlo, rl);
+          const uint32_t whi = __shfl_sync(0xFFFFFFFFu, mhi, rl);
+          uint32_t p = __shfl_sync(0xFFFFFFFFu, rowbase, rl);
+          const uint64_t wr = ((uint64_t)whi << 32) | wlo;
+          const uint32_t mbyte = (uint32_t)(wr >> (8 * c)) & 0xFFu;
+          p += (uint32_t)__popcll(wr & ((1ull << (8 * c)) - 1ull));
+          uint32_t o[4] = {0, 0, 0, 0};
+          if (mbyte) {
+            // bit i -> nibble i, then nibble i of x * 0x11111111 - x = set
+            // bits below position i (at most 7: no carries between nibbles)
+            uint32_t x = (mbyte | (mbyte << 12)) & 0x000F000Fu;
+            x = (x | (x << 6)) & 0x03030303u;
+            x = (x | (x << 3)) & 0x11111111u;
+            const uint32_t rk = x * 0x11111111u - x;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint32_t v =
+                  ((mbyte >> i) & 1u) ? lds_u16(sv + 2 * (p + ((rk >> (4 * i)) & 0xFu))) : 0u;
+              o[i >> 1] |= v << (16 * (i & 1));
+            }
+            if constexpr (RELU2) {  // k * v * v with k = 1: one bf16 product
+#pragma unroll
+              for (int i = 0; i < 4; ++i) o[i] = bf16x2_mul(o[i], o[i]);
+            }
+          }
+          const int row = r0 + rl;
+          sts_v4(box + row * 128 + ((c ^ (row & 7)) * 16), o[0], o[1], o[2], o[3]);
+        }
+      } else {  // no tile here (right edge of h): zero columns
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sts_v4(box + r0 * 128 + (i * 32 + lane) * 16, 0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();  // B writes (and slot reads) before the async proxy's use
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_local(&rempty[rs]);
+        mbar_arrive_cluster(full_leader + (uint32_t)(8 * s));
+      }
+      if (++s == G::NST) { s = 0; sph ^= 1u; }
+      if (++rs == G::RS) { rs = 0; rph ^= 1u; }
+    }
+  }
+  if (warp >= 2 && warp < 6 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * kTmemCols)
+                 : "memory");
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                    const cuuint32_t *, CUtensorMapInterleave,
@@ -835,4 +1287,90 @@ extern "C" int bs_gemm_fp8_relu2(const void *A, int64_t lda, const void *Bt, int
   P.status = status;
   return gemm_run(A, lda, Bt, ldb, C, ldc, M, N, K, kEpiFp8Relu2, P,
                   static_cast<cudaStream_t>(stream));
+}
+
+namespace bs {
+namespace {
+template <bool RELU2>
+int launch_dw(const CUtensorMap &ta, const CUtensorMap &tc, const DwParams &P, cudaStream_t st) {
+  using G = DwCfg;
+  static_assert(G::SMEM <= 227 * 1024, "shared memory of one CTA");
+  auto kernel = dw_unpack_kernel<RELU2>;
+  constexpr int kMaxDev = 64;
+  static std::mutex mu;
+  static int sms_of[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return BS_ERR_LAUNCH;
+  int sms;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!sms_of[dev]) {
+      int n = 0;
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)G::SMEM) != cudaSuccess ||
+          cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return BS_ERR_LAUNCH;
+      sms_of[dev] = n;
+    }
+    sms = sms_of[dev];
+  }
+  const int64_t tiles = ((P.M + G::BM - 1) / G::BM) * ((P.N + kBN - 1) / kBN);
+  const int64_t slots = sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * (tiles < slots ? tiles : slots)));
+  cfg.blockDim = dim3(kThreadsD);
+  cfg.dynamicSmemBytes = G::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tc, P) != cudaSuccess) return BS_ERR_LAUNCH;
+  return BS_OK;
+}
+}  // namespace
+}  // namespace bs
+
+extern "C" int bs_gemm_unpack_dw(const void *g, int64_t ldg, int64_t T, int64_t D,
+                                 const void *vals, const uint8_t *bitmask,
+                                 const uint32_t *prefix, const int64_t *vals_offset, int64_t H,
+                                 int relu2, float k, void *C, int64_t ldc, int32_t *status,
+                                 void *stream) {
+  if (T < 0 || D < 0 || H < 0) return BS_ERR_SHAPE;
+  if (D == 0 || H == 0) return BS_OK;
+  // (vals may be null when the tensor holds no values)
+  if (!g || !C || !bitmask || !prefix || !vals_offset) return BS_ERR_ARG;
+  if (ldg < D || ldc < H) return BS_ERR_SHAPE;
+  if (relu2 && k != 1.0f) return BS_ERR_ARG;  // the fused square assumes k = 1
+  if (T >= ((int64_t)1 << 31) || D >= ((int64_t)1 << 31) || H >= ((int64_t)1 << 31))
+    return BS_ERR_TOO_LARGE;
+  if ((reinterpret_cast<uintptr_t>(g) & 15) || ((ldg * 2) & 15) ||
+      (reinterpret_cast<uintptr_t>(vals) & 15) || (reinterpret_cast<uintptr_t>(bitmask) & 15))
+    return BS_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0) {  // empty reduction: C = 0
+    for (int64_t r = 0; r < D; ++r)
+      if (cudaMemsetAsync(static_cast<uint8_t *>(C) + r * ldc * 2, 0, (size_t)H * 2, st) !=
+          cudaSuccess)
+        return BS_ERR_LAUNCH;
+    return BS_OK;
+  }
+  DwParams P{};
+  P.C = static_cast<uint8_t *>(C);
+  P.M = D; P.N = H; P.K = T; P.ldc = ldc;
+  P.vals = static_cast<const uint8_t *>(vals);
+  P.bitmask = bitmask;
+  P.prefix = prefix;
+  P.vals_offset = vals_offset;
+  P.grid_n = (H + kTileN - 1) / kTileN;
+  P.status = status;
+  P.c_tma = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((ldc * 2) % 16 == 0);
+  CUtensorMap ta, tc;
+  if (!make_map(&ta, g, T, D, ldg, 64, 64)) return BS_ERR_ALIGN;
+  if (P.c_tma && !make_map(&tc, C, D, H, ldc, 64, 32)) P.c_tma = 0;
+  if (!P.c_tma) tc = ta;  // unused
+  return relu2 ? launch_dw<true>(ta, tc, P, st) : launch_dw<false>(ta, tc, P, st);
 }

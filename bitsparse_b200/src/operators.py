@@ -321,6 +321,40 @@ def matmul_relu2_grad(a: Tensor, b: Tensor, sparse: BitsparseTensor) -> Tensor |
     return out
 
 
+def matmul_unpack_dw(a: Tensor, sparse: BitsparseTensor, relu2: bool = False) -> Tensor | None:
+    """``a @ unpack(sparse)`` (AspB) or ``a @ (k * unpack(sparse)^2)``
+    (AspRelu2B) in one tcgen05 GEMM that expands each compressed tile of
+    ``sparse`` straight into its shared-memory operand
+    (lib_sparse/src/sparse_matmul.py:9-47, :91-132): the FFN's weight
+    gradient ``grad_output.T @ h`` without the dense h.  ``a`` [D, T] must
+    be the transpose of a row-major bf16 [T, D] (the layers pass
+    ``grad_output.T``).  Returns ``None`` when the path does not apply (FP8
+    or packed storage, a scaled tensor, k != 1 for ReLU^2, D < 256, layouts
+    TMA cannot read), and the caller unpacks and multiplies."""
+    if (sparse.dtype != torch.bfloat16 or sparse.pack_sbit or sparse.scale is not None
+            or a.dtype != torch.bfloat16 or a.dim() != 2 or not a.is_cuda):
+        return None
+    if relu2 and RELU2_SCALE != 1:
+        return None
+    D, T = a.shape
+    if tuple(sparse.shape)[0] != T or (sparse.BLOCK_M, sparse.BLOCK_N) != (_BM, _BN):
+        return None
+    if D < 256 or a.stride(0) != 1 or a.stride(1) < D or a.data_ptr() % 16 or (a.stride(1) * 2) % 16:
+        return None
+    if sparse.vals.data_ptr() % 16 or sparse.bitmask.data_ptr() % 16:
+        return None
+    H = sparse.shape[1]
+    out = torch.empty((D, H), device=a.device, dtype=torch.bfloat16)
+    rc = _lib.load().bs_gemm_unpack_dw(
+        a.data_ptr(), a.stride(1), T, D, sparse.vals.data_ptr(), sparse.bitmask.data_ptr(),
+        sparse.prefix.data_ptr(), sparse.vals_offset.data_ptr(), H, int(relu2),
+        float(RELU2_SCALE), out.data_ptr(), H, R.status_word(a.device).data_ptr(), _stream(a))
+    if rc == _lib.BS_ERR_ALIGN:
+        return None
+    _lib.check(rc, "bs_gemm_unpack_dw")
+    return out
+
+
 def matmul_fp8_relu2_grad(a: Tensor, bt: Tensor, a_scale: Tensor, b_scale: Tensor,
                           sparse: BitsparseTensor) -> Tensor | None:
     """``relu2_grad_sparse_(scaled_mm(a, bt.T), sparse)`` for e4m3 storage in

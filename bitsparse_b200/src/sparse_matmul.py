@@ -1,18 +1,30 @@
 """Dense x BitsparseTensor GEMMs (lib_sparse/src/sparse_matmul.py).
 
 ``AspB`` / ``AspRelu2B`` compute ``A @ B`` / ``A @ (k * B^2)`` with B stored
-sparse: B is reconstructed by the CUDA unpack kernel, then multiplied.
+sparse: B is reconstructed by the CUDA unpack kernel, then multiplied; or,
+with ``FUSED_DW`` (bf16 raw storage, A the transpose of a row-major operand
+as the layers' ``grad_output.T``), one tcgen05 GEMM expands B's compressed
+tiles straight into its shared-memory operand (``matmul_unpack_dw``).
 ``row_batch > 0`` unpacks tile-aligned row batches and accumulates, trading
 time for peak memory, as in the reference.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 from torch import Tensor
 
 from ..bitsparse import BitsparseTensor
 from ..fp8 import matmul
-from .operators import unpack_batch_, unpack_relu2_batch_
+from .operators import matmul_unpack_dw, unpack_batch_, unpack_relu2_batch_
+
+
+# The fused reconstruct + tcgen05 weight-gradient GEMM (matmul_unpack_dw) is
+# opt-in: it never writes the dense activation, but on B200 its per-tile
+# expansion on the CUDA cores cannot keep pace with the tensor cores, and
+# unpack + cuBLAS is faster at every measured shape.  BS_DW_FUSED=1 selects it.
+FUSED_DW = os.environ.get("BS_DW_FUSED", "0") == "1"
 
 
 def _row_batches(grid_m: int, BLOCK_M: int, N: int, row_batch: int):
@@ -32,6 +44,10 @@ def AspB(A: Tensor, B_sparse: BitsparseTensor, A_scale: Tensor | None = None,
     N, K = B_sparse.shape
     M = A.shape[0]
     if row_batch <= 0:
+        if FUSED_DW and not B_sparse.fp8:  # reconstruct fused into the tcgen05 GEMM
+            out = matmul_unpack_dw(A, B_sparse)
+            if out is not None:
+                return out
         dense = torch.empty(N, K, device=A.device, dtype=B_sparse.dtype)
         unpack_batch_(B_sparse, dense, 0, grid_n, K, N, grid_m * grid_n)
         return matmul(A, dense, B_sparse.fp8, a_scale=A_scale, b_scale=B_sparse.scale)
@@ -99,6 +115,10 @@ def AspRelu2B(A: Tensor, B_sparse: BitsparseTensor, A_scale: Tensor | None = Non
             bT, b_scale = _relu2_fp8_colmajor(B_sparse)
             return _scaled_mm(_row_major_fp8(A), bT.T, A_scale, b_scale,
                               output_dtype=torch.bfloat16)
+        if FUSED_DW and not B_sparse.fp8:
+            out = matmul_unpack_dw(A, B_sparse, relu2=True)
+            if out is not None:
+                return out
         dense = torch.empty(N, K, device=A.device, dtype=torch.bfloat16)
         unpack_relu2_batch_(B_sparse, dense, 0, grid_n, K, N, grid_m * grid_n)
         return matmul(A, dense, B_sparse.fp8, a_scale=A_scale)

@@ -339,6 +339,25 @@ int bs_gemm_fp8_relu2(const void *A, int64_t lda, const void *Bt, int64_t ldb, v
                       const uint32_t *prefix, const int64_t *vals_offset, float k,
                       const float *hscale, int32_t *status, void *stream);
 
+/* The weight gradient of the FFN's second linear with the reconstruct fused
+ * into the GEMM (AspB / AspRelu2B, lib_sparse/src/sparse_matmul.py:9-47 and
+ * :91-132, called from lib_sparse/layers.py:58 and :142):
+ *   C[D, H] = g^T . h        (relu2 = 0)
+ *   C[D, H] = g^T . (k h^2)  (relu2 = 1; k must be 1, the reference's RELU2_SCALE)
+ * g: bf16 [T, D] row-major (row stride ldg elements, 16-byte aligned base
+ * and row stride); h: the bf16 bitsparse tensor [T, H] (vals 16-byte
+ * aligned, bitmask, prefix, vals_offset as bs_compress wrote them, raw
+ * storage, 64 x 64 tiles); C: bf16 [D, H] (row stride ldc).  Each 64 x 64
+ * tile of h is expanded from its compressed form straight into the tensor
+ * cores' shared-memory operand; the dense h is never written.  fp32
+ * accumulation, C rounded to bf16 once.  status: as bs_compress (bounded
+ * waits).  BS_ERR_ALIGN when g, vals or bitmask cannot be read by TMA /
+ * bulk copies. */
+int bs_gemm_unpack_dw(const void *g, int64_t ldg, int64_t T, int64_t D, const void *vals,
+                      const uint8_t *bitmask, const uint32_t *prefix,
+                      const int64_t *vals_offset, int64_t H, int relu2, float k, void *C,
+                      int64_t ldc, int32_t *status, void *stream);
+
 /* Per-tensor fp8 scale of to_fp8 (lib_sparse/fp8.py:123-129):
  * *scale_out = max(amax(|x|) / 448, 1e-9), with the amax / 448 rounded to
  * bf16 for bf16 input (eager PyTorch semantics).  `amax_ws` is a device

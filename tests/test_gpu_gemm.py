@@ -155,3 +155,62 @@ def test_fp8_relu2_epilogue_equals_two_steps(M, N, K, scaled):
     assert torch.equal(out, two)
     assert torch.all(out[hq.float() == 0] == 0)
     B.check_status()
+
+
+def _dw_case(T, D, H, seed, mu=0.0, arena=False):
+    from bitsparse_b200.bitsparse import TensorBuffer
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    go = torch.randn(T, D, generator=g, device="cuda").to(torch.bfloat16)
+    h = (torch.randn(T, H, generator=g, device="cuda") + mu).relu().to(torch.bfloat16)
+    buf = None
+    if arena:  # a shared arena at an odd value offset: runs start unaligned
+        buf = TensorBuffer(2 * T * H + 64, device="cuda", dtype=torch.bfloat16)
+        buf.offset.fill_(3)
+    return go, h, dense_to_tilesparse(h, None, buf)
+
+
+@pytest.mark.parametrize("T, D, H", [(64, 256, 64), (1000, 384, 200), (130, 512, 72),
+                                     (4096, 768, 3072), (8192, 1024, 4096)])
+@pytest.mark.parametrize("relu2", [False, True])
+@pytest.mark.parametrize("arena", [False, True])
+def test_fused_dw_matches_fp32_reference(T, D, H, relu2, arena):
+    """K5: go^T @ h (AspB) / go^T @ (h * h) (AspRelu2B, k = 1) with h
+    expanded from its compressed tiles inside the tcgen05 GEMM, against the
+    fp32 product of the same bf16 operands (h * h rounded to bf16 as the
+    reference's ReLU^2 reconstruct does)."""
+    from bitsparse_b200.src.operators import matmul_unpack_dw
+    go, h, sp = _dw_case(T, D, H, T + D + H, arena=arena)
+    dense = (h * h) if relu2 else h
+    ref = go.float().T @ dense.float()
+    out = matmul_unpack_dw(go.T, sp, relu2)
+    assert out is not None and out.shape == (D, H)
+    err = (out.float() - ref).abs().max().item()
+    assert err <= RTOL * ref.abs().max().item(), (err, ref.abs().max().item())
+    B.check_status()
+
+
+@pytest.mark.parametrize("mu", [-1.5, -3.0, -50.0])
+def test_fused_dw_sparse_and_empty(mu):
+    """High sparsity (empty 8-value chunks, empty tiles) and an all-zero h."""
+    from bitsparse_b200.src.operators import matmul_unpack_dw
+    go, h, sp = _dw_case(2048, 512, 1024, 17, mu=mu)
+    ref = go.float().T @ h.float()
+    out = matmul_unpack_dw(go.T, sp)
+    if mu == -50.0:
+        assert torch.count_nonzero(out) == 0
+    else:
+        err = (out.float() - ref).abs().max().item()
+        assert err <= RTOL * ref.abs().max().item()
+    B.check_status()
+
+
+def test_fused_dw_equals_dense_tcgen05_gemm():
+    """The fused expansion feeds the tensor cores exactly the dense tile: the
+    result equals the tcgen05 GEMM of the dense operands (K3, same K-block
+    order) bit for bit."""
+    from bitsparse_b200.src.operators import matmul_unpack_dw
+    go, h, sp = _dw_case(4096, 512, 2048, 5)
+    out = matmul_unpack_dw(go.T, sp)
+    ref = matmul_relu_mask(go.T.contiguous(), h)
+    assert torch.equal(out, ref)
+    B.check_status()

@@ -11,6 +11,7 @@ import torch
 
 import bitsparse_b200 as B
 from bitsparse_b200 import TensorBuffer
+import bitsparse_b200.src.sparse_matmul as SM
 from bitsparse_b200.layers import FFNRelu, FFNRelu2
 from tests.golden.fixtures import has
 
@@ -94,9 +95,9 @@ class _DenseTwin(torch.autograd.Function):
     compression is lossless, so only the storage differs."""
 
     @staticmethod
-    def forward(ctx, z, W, relu2, fp8):
+    def forward(ctx, z, W, relu2, fp8, fused_dw=False):
         from bitsparse_b200.fp8 import matmul, to_fp8
-        ctx.relu2, ctx.fp8 = relu2, fp8
+        ctx.relu2, ctx.fp8, ctx.fused_dw = relu2, fp8, fused_dw
         ctx.save_for_backward(W)
         h = z.relu_()
         if fp8:
@@ -123,7 +124,8 @@ class _DenseTwin(torch.autograd.Function):
             dense = (r * r).to(torch.bfloat16)
             if scale is not None:
                 dense.mul_(scale.square())
-            gW = matmul(go.T, dense, fp8, a_scale=gscale)
+            gW = _twin_dw(go, dense, ctx.fused_dw) if not fp8 else \
+                matmul(go.T, dense, fp8, a_scale=gscale)
             if fp8:
                 gh = matmul(go, W, fp8=fp8, a_scale=gscale)
             else:  # the layer's grad_h comes from the tcgen05 GEMM (ReLU^2 epilogue)
@@ -138,19 +140,29 @@ class _DenseTwin(torch.autograd.Function):
             # taken from the dense activation kept here
             from bitsparse_b200.layers import _relu_grad
             from bitsparse_b200.src.functions import dense_to_tilesparse
-            gW = matmul(go.T, h, fp8, a_scale=gscale, b_scale=scale)
+            gW = _twin_dw(go, h, ctx.fused_dw)
             gz = _relu_grad(go, W, dense_to_tilesparse(h.contiguous(), None))
         else:
             gW = matmul(go.T, h, fp8, a_scale=gscale, b_scale=scale)
             gh = matmul(go, W, fp8=fp8, a_scale=gscale)
             gz = torch.where(mask, gh, torch.zeros((), dtype=gh.dtype, device=gh.device))
-        return gz, gW, None, None
+        return gz, gW, None, None, None
 
 
-def _twin_ffn(x, W1, W2, b1, b2, relu2, fp8):
+def _twin_dw(go, dense, fused_dw):
+    """The twin's dW2 = go^T @ dense: where the layer's GEMM expands the
+    compressed activation inside a tcgen05 GEMM (raw bf16 storage), the same
+    tensor-core accumulation on the dense operand (K3 on go^T); else cuBLAS."""
+    from bitsparse_b200.src.operators import matmul_relu_mask
+    if fused_dw:
+        return matmul_relu_mask(go.T.contiguous(), dense.contiguous())
+    return go.T @ dense
+
+
+def _twin_ffn(x, W1, W2, b1, b2, relu2, fp8, fused_dw=False):
     from bitsparse_b200.fp8 import matmul
     z = matmul(x, W1.T, fp8) + b1
-    return _DenseTwin.apply(z, W2, relu2, fp8) + b2
+    return _DenseTwin.apply(z, W2, relu2, fp8, fused_dw) + b2
 
 
 @pytest.mark.parametrize("relu2", [False, True])
@@ -165,7 +177,25 @@ def test_ffn_bit_exact_vs_dense_activation_twin(relu2, fp8, pack):
     kw = {"pack_sbit": pack, ("storage_dtype" if relu2 else "dtype"): dt}
     y, grads = run(layer, (x, W1, W2, b1, b2), gy, **kw)
     ps = [t.detach().clone().requires_grad_() for t in (x, W1, W2, b1, b2)]
-    yt = _twin_ffn(*ps, relu2, fp8)
+    yt = _twin_ffn(*ps, relu2, fp8, fused_dw=SM.FUSED_DW and not fp8 and not pack)
+    yt.backward(gy)
+    assert torch.equal(y, yt.detach())
+    for n, a, p in zip(("x", "W1", "W2", "b1", "b2"), grads, ps):
+        assert torch.equal(a, p.grad), n
+    B.check_status()
+
+
+@pytest.mark.parametrize("relu2", [False, True])
+def test_ffn_fused_dw_bit_exact(monkeypatch, relu2):
+    """With the fused reconstruct + tcgen05 weight-gradient GEMM selected,
+    the bf16 FFN equals its dense-activation twin (whose dW2 is the tcgen05
+    GEMM of the dense operands) bit for bit."""
+    monkeypatch.setattr(SM, "FUSED_DW", True)
+    T, d, H, do = 512, 256, 1024, 256
+    x, W1, W2, b1, b2, gy = make(T, d, H, do, seed=8, bias_shift=-0.01)
+    y, grads = run(FFNRelu2 if relu2 else FFNRelu, (x, W1, W2, b1, b2), gy)
+    ps = [t.detach().clone().requires_grad_() for t in (x, W1, W2, b1, b2)]
+    yt = _twin_ffn(*ps, relu2, False, fused_dw=True)
     yt.backward(gy)
     assert torch.equal(y, yt.detach())
     for n, a, p in zip(("x", "W1", "W2", "b1", "b2"), grads, ps):
@@ -198,7 +228,7 @@ def test_ffn_fused_masked_gemm_path_bit_exact(monkeypatch):
     x, W1, W2, b1, b2, gy = make(T, d, H, do, seed=5, bias_shift=-0.01)
     y, grads = run(FFNRelu, (x, W1, W2, b1, b2), gy)
     ps = [t.detach().clone().requires_grad_() for t in (x, W1, W2, b1, b2)]
-    yt = _twin_ffn(*ps, False, False)
+    yt = _twin_ffn(*ps, False, False, fused_dw=SM.FUSED_DW)
     yt.backward(gy)
     assert torch.equal(y, yt.detach())
     for n, a, p in zip(("x", "W1", "W2", "b1", "b2"), grads, ps):
