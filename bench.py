@@ -818,8 +818,13 @@ def kernel_cases(which: str):
     "relu2" -- the bf16 GEMM with the ReLU^2 gradient in its epilogue at the
     config-2 backward shape (8192 x 768 @ 768 x 3072, h 84% sparse);
     "sparse_recon" -- the persistent reconstruct of an [8192, 8192] bf16
-    tensor at 99% sparsity (the sparse-chunk scatter path).  Each runs its
-    kernel twice and checks the result."""
+    tensor at 99% sparsity (the sparse-chunk scatter path); "dw" -- the
+    fused reconstruct + tcgen05 weight-gradient GEMM at the config-2
+    backward shape (go^T [768 x 8192] @ h [8192 x 3072], h 50% sparse),
+    timed against unpack + cuBLAS; "fp8_compress" -- the one-pass FP8
+    quantise + compress of an [8192, 8192] bf16 tensor, plain and with bias,
+    ReLU and the square side output.  Each runs its kernel twice and checks
+    the result."""
     import torch
     from bitsparse_b200 import TensorBuffer
     from bitsparse_b200.src.functions import dense_to_tilesparse
@@ -869,6 +874,74 @@ def kernel_cases(which: str):
             out = matmul_relu2_grad(a, b, sp)
         if not torch.equal(out, relu2_grad_sparse_(matmul_relu_mask(a, b), sp)):
             raise RuntimeError("relu2 gemm case mismatch")
+        import os
+        if os.environ.get("BS_CASE_TIMING", "1") == "1":
+            def ev(fn, k=50):
+                for _ in range(5):
+                    fn()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(k):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+                return e0.elapsed_time(e1) / k * 1e3
+            fused = ev(lambda: matmul_relu2_grad(a, b, sp))
+            two = ev(lambda: relu2_grad_sparse_(matmul_relu_mask(a, b), sp))
+            cub = ev(lambda: relu2_grad_sparse_(a @ b, sp))
+            print(f"ReLU^2 dX {M}x{K} @ {K}x{N}: fused epilogue {fused:.1f} us, tcgen05 GEMM + "
+                  f"relu2_grad {two:.1f} us, cuBLAS + relu2_grad {cub:.1f} us")
+    elif which == "dw":
+        import os
+        import bitsparse_b200.src.sparse_matmul as SM
+        from bitsparse_b200.src.operators import matmul_unpack_dw
+        T, D, H = 8192, 768, 3072
+        go = torch.randn(T, D, generator=g, device=dev).to(torch.bfloat16)
+        h = torch.randn(T, H, generator=g, device=dev).relu().to(torch.bfloat16)
+        sp = dense_to_tilesparse(h, None)
+        for _ in range(2):
+            out = matmul_unpack_dw(go.T, sp)
+        if not torch.equal(out, matmul_relu_mask(go.T.contiguous(), h)):
+            raise RuntimeError("fused dW case mismatch")
+        if os.environ.get("BS_CASE_TIMING", "1") == "1":
+            def ev(fn, k=20):
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(k):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+                return e0.elapsed_time(e1) / k * 1e3
+            SM.FUSED_DW = False
+            fused = ev(lambda: matmul_unpack_dw(go.T, sp))
+            unf = ev(lambda: SM.AspB(go.T, sp))
+            cub = ev(lambda: go.T @ h)
+            print(f"dW {D}x{T}x{H}: fused {fused:.1f} us, unpack + cuBLAS {unf:.1f} us, "
+                  f"cuBLAS alone {cub:.1f} us")
+    elif which == "fp8_compress":
+        from bitsparse_b200.fp8 import to_fp8
+        from bitsparse_b200.src.functions import relu_to_tilesparse_fp8
+        from bitsparse_b200.src.operators import compress_bias_relu_fp8
+        n = 8192
+        x = torch.randn(n, n, generator=g, device=dev).to(torch.bfloat16)
+        b = (0.1 * torch.randn(n, generator=g, device=dev)).to(torch.bfloat16)
+        h = torch.relu(x + b)
+        buf = TensorBuffer(n * n, device=dev, dtype=torch.float8_e4m3fn)
+        for _ in range(2):
+            buf.offset.zero_()
+            side, ss, sp = compress_bias_relu_fp8(x, b, buf, False, square=True)
+            buf.offset.zero_()
+            q, sp2 = relu_to_tilesparse_fp8(h, sparse_data=buf)
+        if not torch.equal(side.view(torch.uint8), to_fp8(h * h)[0].view(torch.uint8)) or \
+                not torch.equal(q.view(torch.uint8), to_fp8(h)[0].view(torch.uint8)):
+            raise RuntimeError("fp8 compress case mismatch")
+        from bitsparse_b200.fp8 import estimate_exact
+        print("quantiser estimate path (h, h*h, relu case):", estimate_exact(sp.scale.reshape(())),
+              estimate_exact(ss.reshape(())), estimate_exact(sp2.scale.reshape(())))
     else:
         M = N = 8192
         x = make_relu_bf16(M, N, -2.3263, 0, dev)
@@ -923,7 +996,7 @@ def main():
                     help="run only the sparse-MLP fwd+bwd comparison (configs 2 and 4)")
     ap.add_argument("--gemm-case", action="store_true",
                     help="run only the small ncu capture case of the masked tcgen05 GEMM")
-    ap.add_argument("--kernel-case", choices=["fp8", "relu2", "sparse_recon"],
+    ap.add_argument("--kernel-case", choices=["fp8", "relu2", "sparse_recon", "dw", "fp8_compress"],
                     help="run only a small ncu capture case of that kernel and exit")
     ap.add_argument("--profile-case", action="store_true",
                     help="run only the small ncu capture case and exit")
