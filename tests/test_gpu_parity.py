@@ -572,3 +572,24 @@ def _check_quantize_layouts_equal_to_fp8_copies(R, C, view):
             assert torch.equal(c.T.contiguous().view(torch.uint8), ref.T.contiguous())
         else:
             assert c is None
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("pack", [False, True])
+def test_standalone_exact_allocation_equals_one_pass(monkeypatch, pack):
+    """Standalone compress in the reference's order (counts, prefix, sync,
+    exact allocation, compaction; no dense-sized transient) gives the same
+    bitmask, prefix and value bytes as the one-pass form."""
+    import bitsparse_b200.src.operators as OP
+    g = torch.Generator(device="cuda").manual_seed(21)
+    for M, N, mu in ((1000, 3000, 0.0), (130, 70, -1.0), (4096, 1024, -2.0)):
+        x = (torch.randn(M, N, generator=g, device="cuda") + mu).relu().to(torch.bfloat16)
+        monkeypatch.setattr(OP, "EXACT_STANDALONE", False)
+        a = dense_to_tilesparse(x, None, None, pack)
+        monkeypatch.setattr(OP, "EXACT_STANDALONE", True)
+        b = dense_to_tilesparse(x, None, None, pack)
+        assert torch.equal(a.bitmask, b.bitmask)
+        assert torch.equal(a.prefix.view(torch.int32), b.prefix.view(torch.int32))
+        assert a.vals.numel() == b.vals.numel()
+        assert torch.equal(a.vals.view(torch.uint8), b.vals.view(torch.uint8))
+    B.check_status()
