@@ -922,6 +922,57 @@ def kernel_cases(which: str):
             cub = ev(lambda: go.T @ h)
             print(f"dW {D}x{T}x{H}: fused {fused:.1f} us, unpack + cuBLAS {unf:.1f} us, "
                   f"cuBLAS alone {cub:.1f} us")
+    elif which == "tile_scaled":
+        # per-tile FP8 scale mode: one pass (tile amax, quantise, compress)
+        # against the per-tensor path (amax pass + quantise + compress), and
+        # the dequantising reconstruct; fraction of the measured HBM peak
+        from bitsparse_b200.src.functions import relu_to_tilesparse_fp8
+        from bitsparse_b200.src.operators import compress_fp8_tile_scaled, unpack_tile_scaled_
+        n = 8192
+        x = torch.randn(n, n, generator=g, device=dev).relu().to(torch.bfloat16)
+        buf = TensorBuffer(n * n, device=dev, dtype=torch.float8_e4m3fn)
+
+        def ts():
+            buf.offset.zero_()
+            return compress_fp8_tile_scaled(x, buf)
+        sp = ts()
+        out = torch.empty(n, n, device=dev, dtype=torch.bfloat16)
+        unpack_tile_scaled_(sp, out)
+        # half an e4m3 step (2^-4 relative in the normal range, 2^-10 of the
+        # tile's scale in the subnormal range) plus the output's bf16 rounding
+        sfull = sp.tile_scales.view(sp.grid_m, sp.grid_n).repeat_interleave(64, 0) \
+            .repeat_interleave(64, 1)[:n, :n]
+        tol = x.float().abs() * (2.0 ** -4 + 2.0 ** -8) + sfull * 2.0 ** -10 * 1.01
+        if bool(((out.float() - x.float()).abs() > tol).any()):
+            raise RuntimeError("tile-scaled round trip error")
+
+        def ev(fn, k=20):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(k):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / k * 1e3
+        peak = peaks()[0]
+        nnz = int(sp.prefix[-1].item())
+        T = sp.grid_m * sp.grid_n
+        c_bytes = n * n * 2 + n * n / 8 + nnz + 4 * (T + 1) + 4 * T
+        r_bytes = n * n / 8 + nnz + 4 * (T + 1) + 4 * T + n * n * 2
+        t_ts = ev(ts)
+
+        def pt():
+            buf.offset.zero_()
+            relu_to_tilesparse_fp8(x, sparse_data=buf)
+        t_pt = ev(pt)
+        t_un = ev(lambda: unpack_tile_scaled_(sp, out))
+        print(f"tile-scaled compress {t_ts:.1f} us = {c_bytes / t_ts / 1e3:.0f} GB/s "
+              f"({c_bytes / t_ts / 1e3 / peak:.2f} of peak); per-tensor to_fp8 + compress "
+              f"{t_pt:.1f} us; dequantising reconstruct {t_un:.1f} us = "
+              f"{r_bytes / t_un / 1e3:.0f} GB/s ({r_bytes / t_un / 1e3 / peak:.2f})")
     elif which == "fp8_compress":
         from bitsparse_b200.fp8 import to_fp8
         from bitsparse_b200.src.functions import relu_to_tilesparse_fp8
@@ -996,7 +1047,8 @@ def main():
                     help="run only the sparse-MLP fwd+bwd comparison (configs 2 and 4)")
     ap.add_argument("--gemm-case", action="store_true",
                     help="run only the small ncu capture case of the masked tcgen05 GEMM")
-    ap.add_argument("--kernel-case", choices=["fp8", "relu2", "sparse_recon", "dw", "fp8_compress"],
+    ap.add_argument("--kernel-case", choices=["fp8", "relu2", "sparse_recon", "dw", "fp8_compress",
+                                                  "tile_scaled"],
                     help="run only a small ncu capture case of that kernel and exit")
     ap.add_argument("--profile-case", action="store_true",
                     help="run only the small ncu capture case and exit")

@@ -52,6 +52,10 @@ _SIGS = {
                            _vp]),
     "bs_gemm_fp8_relu2": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
                                  _vp, _vp, _vp, _vp, C.c_float, _vp, _vp, _vp]),
+    "bs_compress_fp8_tile_scaled": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32,
+                                           _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
+    "bs_unpack_tile_scaled": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64,
+                                     _i64, _i64, _vp]),
     "bs_gemm_unpack_dw": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, C.c_float,
                                   _vp, _i64, _vp, _vp]),
     "bs_gemm_bf16_relu2": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp,

@@ -39,11 +39,13 @@ class BitsparseTensor:
     vals_offset int64 tensor: logical index of this tensor's first value in
                 ``vals`` (0 unless ``vals`` is a shared TensorBuffer arena).
     scale       fp32 0-dim per-tensor FP8 scale, or None.
+    tile_scales fp32[T] per-tile FP8 scales (the per-tile scale mode, an
+                extension of the reference's per-tensor format), or None.
     """
 
     def __init__(self, vals, bitmask, prefix, shape, dtype,
                  grid_m, grid_n, BLOCK_M, BLOCK_N,
-                 scale=None, vals_offset=None, pack_sbit=False):
+                 scale=None, vals_offset=None, pack_sbit=False, tile_scales=None):
         self.vals = vals
         self.bitmask = bitmask
         self.prefix = prefix
@@ -53,6 +55,7 @@ class BitsparseTensor:
         self.pack_sbit = pack_sbit
         self.dtype = dtype
         self.scale = scale
+        self.tile_scales = tile_scales
         self.grid_m = grid_m
         self.grid_n = grid_n
         self.BLOCK_M = BLOCK_M

@@ -98,6 +98,9 @@ struct CompressParams {
   // with quant_out in bias + ReLU mode: quant_out receives e4m3(bf16(h * h)
   // / *qscale2) (the FFN's squared activation) instead of e4m3(h / scale)
   const float *qscale2;
+  // per-tile scale mode: scale of each tile (amax_t / 448), written by the
+  // one-pass kernel
+  float *tile_scales;
 };
 
 template <int DT_IN, bool QUANT, int TPP>
@@ -773,7 +776,7 @@ __device__ __forceinline__ void place8(uint32_t &a, uint32_t m, uint32_t bit, ui
 }
 
 template <int DT_IN, bool QUANT, bool PACK, int TPP_, int NW, int D, int A, int MINB,
-          bool BIAS = false, bool QC = false>
+          bool BIAS = false, bool QC = false, bool TS = false>
 __global__ void __launch_bounds__(NW * 32, MINB)
     onepass_kernel(const __grid_constant__ CUtensorMap tmap, const CompressParams P) {
   using O = Onepass<DT_IN, QUANT, TPP_, NW, D, A>;
@@ -824,14 +827,16 @@ __global__ void __launch_bounds__(NW * 32, MINB)
     for (int i = 0; i < A; ++i)
       if (i * G + b < nparts) fetch(i * G + b, i);
 
-  const float qs = QUANT ? *P.qscale : 1.f;
-  const float qr = QUANT ? quant_rcp(qs) : 1.f;
+  static_assert(!TS || (QUANT && !BIAS && DT_IN == BS_BF16), "per-tile scales: bf16 input");
+  __shared__ uint32_t s_tam[TS ? NW : 1];  // per-tile scale mode: warp amax (bf16 bits)
+  const float qs = QUANT && !TS ? *P.qscale : 1.f;
+  const float qr = QUANT && !TS ? quant_rcp(qs) : 1.f;
   const float qs2 = (QUANT && BIAS && P.qscale2 != nullptr) ? *P.qscale2 : 1.f;
   const float qr2 = quant_rcp(qs2);
   // the estimate alone quantises exactly at these scales (checked per CTA,
   // while the first partitions are in flight)
   bool qfast = false, qfast2 = false;
-  if constexpr (QUANT) {
+  if constexpr (QUANT && !TS) {
     qfast = e4m3_estimate_exact(qs, qr, QC);
     if constexpr (BIAS) qfast2 = P.qscale2 != nullptr && e4m3_estimate_exact(qs2, qr2, QC);
   }
@@ -910,6 +915,31 @@ __global__ void __launch_bounds__(NW * 32, MINB)
             v[s4][0] = w.x; v[s4][1] = w.y;
           }
         }
+        // per-tile scale mode: amax of the tile (NaN ignored) from its warps'
+        // rows, then scale = amax / 448 and the code is e4m3(x * (448 / amax))
+        // (a zero tile: scale 1, every code 0)
+        float tinv = 0.f;
+        if constexpr (TS) {
+          uint32_t am = 0;
+#pragma unroll
+          for (int s4 = 0; s4 < S; ++s4)
+#pragma unroll
+            for (int i = 0; i < VW; ++i) {
+              uint32_t lo = v[s4][i] & 0x7FFFu, hi = (v[s4][i] >> 16) & 0x7FFFu;
+              lo = lo > 0x7F80u ? 0u : lo;
+              hi = hi > 0x7F80u ? 0u : hi;
+              am = max(am, max(lo, hi));
+            }
+          am = __reduce_max_sync(0xFFFFFFFFu, am);
+          constexpr int WPT = kTileM / RW;  // warps per tile, all valid or all not
+          if (lane == 0) s_tam[warp] = am;
+          asm volatile("bar.sync %0, %1;" ::"r"(1 + j), "r"(WPT * 32) : "memory");
+#pragma unroll
+          for (int k = 0; k < WPT; ++k) am = max(am, s_tam[j * WPT + k]);
+          const float a = __uint_as_float(am << 16);
+          tinv = a > 0.f ? __fdiv_rn(448.f, a) : 0.f;
+          if (lane == 0 && rho0 == j * kTileM) P.tile_scales[tile] = a > 0.f ? __fdiv_rn(a, 448.f) : 1.f;
+        }
 #pragma unroll
         for (int s4 = 0; s4 < S; ++s4) {
           if constexpr (BIAS) {
@@ -935,7 +965,9 @@ __global__ void __launch_bounds__(NW * 32, MINB)
             uint32_t qw[2] = {0, 0}, side[2];
             {
               const uint32_t h4[4] = {v[s4][0], v[s4][1], v[s4][2], v[s4][3]};
-              if (qfast) {
+              if constexpr (TS) {
+                est_e4m3x8<true>(h4, tinv, qw);  // e4m3(x * inv_t), round to nearest even
+              } else if (qfast) {
                 est_e4m3x8<QC>(h4, qr, qw);
               } else {
                 const uint2 c = quant8_checked(h4[0], h4[1], h4[2], h4[3], qs, qr, QC);
@@ -1159,7 +1191,7 @@ constexpr int onepass_tpp() {
 }
 
 template <int DT_IN, bool QUANT, bool PACK, int TPP2, int NW, int D, int A, int MINB = 2,
-          bool BIAS = false>
+          bool BIAS = false, bool TS = false>
 static int launch_onepass(const CompressParams &P, cudaStream_t st) {
   constexpr int TPP = onepass_tpp<DT_IN, TPP2, NW>();
   using O = Onepass<DT_IN, QUANT, TPP, NW, D, A>;
@@ -1183,8 +1215,8 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return kNotApplicable;
-  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS, false>;
-  if constexpr (QUANT) {  // the compiled to_fp8's quantiser: its own instantiation
+  auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS, false, TS>;
+  if constexpr (QUANT && !TS) {  // the compiled to_fp8's quantiser: its own instantiation
     if (P.qcompiled) kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS, true>;
   }
   int resident = resident_ctas(reinterpret_cast<const void *>(kernel), O::SMEM, NW * 32);
@@ -1402,6 +1434,33 @@ extern "C" int bs_compress_bias_relu(const void *z, int64_t M, int64_t N, int64_
   rc = pack_sbit ? launch_onepass<BS_BF16, false, true, 4, 8, 1, 1, 2, true>(P, st)
                  : launch_onepass<BS_BF16, false, false, 4, 8, 1, 1, 2, true>(P, st);
   return rc == kNotApplicable ? BS_ERR_ALIGN : rc;
+}
+
+extern "C" int bs_compress_fp8_tile_scaled(const void *dense, int64_t M, int64_t N, int64_t ld,
+                                           float *tile_scales, uint8_t *bitmask, uint32_t *prefix,
+                                           void *vals, int64_t vals_capacity, int pack_sbit,
+                                           int64_t *arena_offset, int64_t *vals_offset_out,
+                                           int64_t *nnz_out, void *workspace,
+                                           size_t workspace_bytes, int32_t *status,
+                                           void *stream) {
+  if (!tile_scales) return BS_ERR_ARG;
+  CompressParams P{};
+  // (tile_scales stands in for the quantiser's scale: e4m3 storage; the
+  // kernel never reads it as a scale)
+  const int rc = setup_compress(P, dense, BS_BF16, M, N, ld, tile_scales, nullptr, bitmask,
+                                prefix, vals, vals_capacity, pack_sbit, arena_offset,
+                                vals_offset_out, nnz_out, workspace, workspace_bytes, status);
+  if (rc) return rc;
+  P.tile_scales = tile_scales;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (P.num_tiles == 0) {
+    if (cudaMemsetAsync(prefix, 0, sizeof(uint32_t), st) != cudaSuccess) return BS_ERR_LAUNCH;
+    return BS_OK;
+  }
+  // one pass only; BS_ERR_ALIGN when TMA cannot read the input
+  const int r = pack_sbit ? launch_onepass<BS_BF16, true, true, 4, 8, 1, 1, 2, false, true>(P, st)
+                          : launch_onepass<BS_BF16, true, false, 4, 8, 1, 1, 2, false, true>(P, st);
+  return r == kNotApplicable ? BS_ERR_ALIGN : r;
 }
 
 extern "C" int bs_compress_bias_relu_fp8(const void *z, int64_t M, int64_t N, int64_t ld,

@@ -48,6 +48,9 @@ struct UnpackParams {
   // plain reconstruct: a warp scatters only the set values of its chunks
   // when none holds more than this many (else every element reads its rank)
   uint32_t scatter_max;
+  // OUT 3: the per-tile scales of an e4m3 tensor compressed in per-tile
+  // scale mode (one per tile of the whole tensor)
+  const float *tile_scales;
 };
 
 __device__ __forceinline__ void st_v8(void *p, const uint32_t (&w)[8]) {
@@ -235,10 +238,12 @@ __device__ __forceinline__ uint32_t relu2_out(const UnpackParams &P, uint32_t v)
 // OUT: 0 = elements of SDT (plain reconstruct), 1 = bf16 k*r^2 (ReLU^2),
 // 2 = the ReLU^2 reconstruction quantised to e4m3 with *qscale (to_fp8's
 // quantiser) and written transposed (out is [K, batch_rows]) -- the B
-// operand of the fp8 dW GEMM in the column-major order cuBLASLt wants.
+// operand of the fp8 dW GEMM in the column-major order cuBLASLt wants;
+// 3 = bf16(value(code) * scale of its tile), the dequantised tensor of the
+// per-tile scale mode.
 template <int SDT, bool PACK, int OUT, bool SCALE>
 __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) {
-  constexpr int OB = OUT == 1 ? 2 : (OUT == 2 ? 1 : Elt<SDT>::bytes);  // output element bytes
+  constexpr int OB = (OUT == 1 || OUT == 3) ? 2 : (OUT == 2 ? 1 : Elt<SDT>::bytes);  // output bytes
   using G = Chunk<OB>;
   constexpr int kTP = 80;  // OUT 2: pitch of a transposed tile column in smem
   __shared__ __align__(16) uint8_t stage[kStageBytes];
@@ -255,7 +260,10 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
   const int nt = tiles_here(P, pid0);
   const PidPos pp(pid0, P.grid_n);
   const int tid = threadIdx.x;
-  if constexpr (LUT) lut[tid] = relu2_out<SDT, OUT, SCALE>(P, tid);
+  if constexpr (LUT) {
+    if constexpr (OUT == 3) lut[tid] = __float_as_uint(store_bits_to_f32<SDT>((uint32_t)tid));
+    else lut[tid] = relu2_out<SDT, OUT, SCALE>(P, tid);
+  }
   uint32_t m[G::S], cnt[G::S], ex[G::S];
 #pragma unroll
   for (int s = 0; s < G::S; ++s) {  // masks first: independent of the values
@@ -284,6 +292,8 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     const uint32_t mm = m[s];
     uint32_t r = ex[s];
+    // OUT 3: this chunk's tile scale
+    const float tsc = OUT == 3 ? P.tile_scales[P.first_tile + pid0 + j] : 1.f;
     if constexpr ((OUT == 0 || LUT) && !PACK) {
       // Branch-free expand: every element loads the value at its rank (the
       // stage has slack past the last value) and keeps it only if its bit
@@ -293,6 +303,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
         const uint32_t bit = (mm >> e) & 1u;
         uint32_t v = staged_value<SDT, PACK>(stage, first, r);
         if constexpr (LUT) v = lut[v];
+        if constexpr (OUT == 3) v = f32_to_bf16_bits(__uint_as_float(v) * tsc);
         v &= 0u - bit;
         r += bit;
         if constexpr (OB == 1) w[e >> 2] |= v << (8 * (e & 3));
@@ -306,6 +317,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
       uint32_t v = staged_value<SDT, PACK>(stage, first, r++);
       if constexpr (LUT) v = lut[v];
       else if constexpr (OUT >= 1) v = relu2_out<SDT, OUT, SCALE>(P, v);
+      if constexpr (OUT == 3) v = f32_to_bf16_bits(__uint_as_float(v) * tsc);
       if constexpr (OB == 1) w[e >> 2] |= v << (8 * (e & 3));
       else w[e >> 1] |= v << (16 * (e & 1));
     }
@@ -844,6 +856,41 @@ extern "C" int bs_unpack(const void *vals, const uint8_t *bitmask, const uint32_
     case BS_E4M3: return unpack_disp<BS_E4M3>(P, pack_sbit, relu2, scale, st);
     default: return unpack_disp<BS_E5M2>(P, pack_sbit, relu2, scale, st);
   }
+}
+
+extern "C" int bs_unpack_tile_scaled(const void *vals, const uint8_t *bitmask,
+                                     const uint32_t *prefix, const int64_t *vals_offset,
+                                     int pack_sbit, const float *tile_scales, void *out,
+                                     int64_t out_ld, int64_t first_m_tile, int64_t grid_n,
+                                     int64_t K, int64_t batch_rows, int64_t num_tiles_in_batch,
+                                     void *stream) {
+  if (num_tiles_in_batch < 0 || first_m_tile < 0 || grid_n < 0 || K < 0 || batch_rows < 0 ||
+      out_ld < K)
+    return BS_ERR_SHAPE;
+  if (num_tiles_in_batch == 0) return BS_OK;
+  if (grid_n == 0 || num_tiles_in_batch > ((int64_t)1 << 31)) return BS_ERR_SHAPE;
+  if (!bitmask || !prefix || !out || !tile_scales) return BS_ERR_ARG;
+  if (pack_sbit && !aligned(vals, 4)) return BS_ERR_ALIGN;
+  UnpackParams P{};
+  P.vals = static_cast<const uint8_t *>(vals);
+  P.bitmask = bitmask;
+  P.prefix = prefix;
+  P.vals_offset = vals_offset;
+  P.out = static_cast<uint8_t *>(out);
+  P.out_ld = out_ld;
+  P.first_tile = first_m_tile * grid_n;
+  P.ntiles = num_tiles_in_batch;
+  P.grid_n = grid_n;
+  P.K = K;
+  P.batch_rows = batch_rows;
+  P.tile_scales = tile_scales;
+  P.vals_v16 = aligned(vals, 16);
+  P.out_v32 = aligned(out, 32) && ((out_ld * 2) % 32 == 0);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 g(ctas(P.ntiles));
+  if (pack_sbit) unpack_kernel<BS_E4M3, true, 3, false><<<g, kThreads, 0, st>>>(P);
+  else unpack_kernel<BS_E4M3, false, 3, false><<<g, kThreads, 0, st>>>(P);
+  return launch_err();
 }
 
 extern "C" int bs_mask_with_bitmask(void *grad, int grad_dtype, int64_t M, int64_t N,

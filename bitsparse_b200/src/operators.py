@@ -547,3 +547,66 @@ def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit:
     sp = BitsparseTensor(vals, bitmask, prefix, (M, N), torch.float8_e4m3fn, grid_m, grid_n,
                          _BM, _BN, scale=scale_h, vals_offset=vals_offset, pack_sbit=pack_sbit)
     return side, (scale_s if square else scale_h), sp
+
+
+# ---------------------------------------------------------------------------
+# Per-tile FP8 scale mode (an extension: the reference's to_fp8 is per tensor)
+# ---------------------------------------------------------------------------
+def compress_fp8_tile_scaled(dense: Tensor, sparse_data=None,
+                             pack_sbit: bool = False) -> BitsparseTensor:
+    """Compress a bf16 [M, N] tensor to e4m3 with one scale per 64 x 64 tile,
+    in one pass (bs_compress_fp8_tile_scaled): scale_t = amax_t / 448, code =
+    e4m3(x * (448 / amax_t)), the positive codes stored as usual.  The
+    returned tensor's ``tile_scales`` (fp32 [T]) go with it; its ``scale`` is
+    None.  The input must be TMA-readable (16-byte aligned base, row stride
+    a multiple of 8 elements)."""
+    if dense.dtype != torch.bfloat16:
+        raise TypeError("the per-tile scale mode takes bfloat16 input")
+    dense, ld = _row_major(dense, "dense")
+    M, N = dense.shape
+    grid_m, grid_n, T, _, TB = tile_grid(M, N, _BM, _BN)
+    dev = dense.device
+    stored = torch.float8_e4m3fn
+    bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
+    prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
+    tile_scales = torch.empty(T, device=dev, dtype=torch.float32)
+    if T == 0:
+        prefix.zero_()
+        vals = torch.empty(packed_storage_nbytes(0, 7) if pack_sbit else 0, device=dev,
+                           dtype=torch.uint8 if pack_sbit else stored)
+        return BitsparseTensor(vals, bitmask, prefix, (M, N), stored, grid_m, grid_n, _BM, _BN,
+                               pack_sbit=pack_sbit, tile_scales=tile_scales)
+    lib = _lib.load()
+    out = _fused_compress(lib.bs_compress_fp8_tile_scaled, "bs_compress_fp8_tile_scaled",
+                          (dense.data_ptr(), M, N, ld, tile_scales.data_ptr()), dev,
+                          _stream(dense), stored, M, N, T, bitmask, prefix, sparse_data, pack_sbit)
+    if out is None:
+        raise ValueError("the per-tile scale mode needs a 16-byte aligned base and row stride")
+    vals, vals_offset = out
+    return BitsparseTensor(vals, bitmask, prefix, (M, N), stored, grid_m, grid_n, _BM, _BN,
+                           vals_offset=vals_offset, pack_sbit=pack_sbit, tile_scales=tile_scales)
+
+
+def unpack_tile_scaled_(sparse: BitsparseTensor, output: Tensor, first_m_tile: int = 0,
+                        grid_n: int | None = None, K: int | None = None,
+                        batch_rows: int | None = None,
+                        num_tiles_in_batch: int | None = None) -> Tensor:
+    """bf16 ``output`` = the dequantised tensor of a per-tile-scaled e4m3
+    BitsparseTensor: bf16(value(code) * tile_scale), zeros elsewhere
+    (bs_unpack_tile_scaled; whole tensor by default, or a tile-row batch as
+    ``unpack_batch_`` takes it)."""
+    if sparse.tile_scales is None or sparse.dtype != torch.float8_e4m3fn:
+        raise ValueError("not a per-tile-scaled e4m3 BitsparseTensor")
+    if output.dtype != torch.bfloat16:
+        raise TypeError("the dequantised output is bfloat16")
+    M, N = sparse.shape
+    grid_n = sparse.grid_n if grid_n is None else grid_n
+    K = N if K is None else K
+    batch_rows = M if batch_rows is None else batch_rows
+    if num_tiles_in_batch is None:
+        num_tiles_in_batch = sparse.grid_m * sparse.grid_n
+    _lib.call("bs_unpack_tile_scaled", sparse.vals.data_ptr(), sparse.bitmask.data_ptr(),
+              sparse.prefix.data_ptr(), sparse.vals_offset.data_ptr(), int(sparse.pack_sbit),
+              sparse.tile_scales.data_ptr(), output.data_ptr(), output.stride(0), first_m_tile,
+              grid_n, K, batch_rows, num_tiles_in_batch, _stream(output))
+    return output

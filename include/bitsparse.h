@@ -358,6 +358,33 @@ int bs_gemm_unpack_dw(const void *g, int64_t ldg, int64_t T, int64_t D, const vo
                       const int64_t *vals_offset, int64_t H, int relu2, float k, void *C,
                       int64_t ldc, int32_t *status, void *stream);
 
+/* Per-tile FP8 scale mode -- an extension: the reference's to_fp8 uses one
+ * scale per tensor (lib_sparse/fp8.py:123-129).  A bf16 [M, N] tensor (row
+ * stride ld; TMA-readable: 16-byte aligned base and row stride, else
+ * BS_ERR_ALIGN) is quantised to e4m3 with one scale per 64 x 64 tile and
+ * compressed in one pass: for tile t, amax_t = max |x| over its elements
+ * (NaN ignored), tile_scales[t] = amax_t / 448 and each code is
+ * e4m3(x * (448 / amax_t)) -- the quotients and the product correctly
+ * rounded in fp32, the cast rounding to nearest even (an all-zero tile: scale
+ * 1, codes 0).  The positive codes are then stored exactly as bs_compress
+ * stores e4m3 values (bitmask, prefix, values, arena offset, pack_sbit).
+ * tile_scales: float[num_tiles].  Other arguments as bs_compress. */
+int bs_compress_fp8_tile_scaled(const void *dense, int64_t M, int64_t N, int64_t ld,
+                                float *tile_scales, uint8_t *bitmask, uint32_t *prefix,
+                                void *vals, int64_t vals_capacity, int pack_sbit,
+                                int64_t *arena_offset, int64_t *vals_offset_out,
+                                int64_t *nnz_out, void *workspace, size_t workspace_bytes,
+                                int32_t *status, void *stream);
+
+/* Reconstruct of a per-tile-scaled e4m3 tensor into bf16: out =
+ * bf16(value(code) * tile_scales[t]) (fp32 product, round to nearest even),
+ * 0 where the bitmask bit is clear.  Batch arguments as bs_unpack. */
+int bs_unpack_tile_scaled(const void *vals, const uint8_t *bitmask, const uint32_t *prefix,
+                          const int64_t *vals_offset, int pack_sbit, const float *tile_scales,
+                          void *out, int64_t out_ld, int64_t first_m_tile, int64_t grid_n,
+                          int64_t K, int64_t batch_rows, int64_t num_tiles_in_batch,
+                          void *stream);
+
 /* Per-tensor fp8 scale of to_fp8 (lib_sparse/fp8.py:123-129):
  * *scale_out = max(amax(|x|) / 448, 1e-9), with the amax / 448 rounded to
  * bf16 for bf16 input (eager PyTorch semantics).  `amax_ws` is a device

@@ -454,3 +454,45 @@ def reconstruct_relu2(sp: Sparse, rounding: str = "rne") -> np.ndarray:
     M, N = sp.shape
     out = np.zeros((M, N), dtype=np.uint16)
     return unpack_relu2_batch(sp, out, 0, sp.grid_n, N, M, sp.num_tiles, rounding)
+
+
+# ---------------------------------------------------------------------------
+# Per-tile FP8 scale mode.  An EXTENSION with no reference counterpart (the
+# reference's to_fp8 is per tensor, lib_sparse/fp8.py:123-129), so this
+# restatement is the specification the CUDA path is checked against -- its
+# parity is unpinned by any reference output.  Every step is IEEE fp32 with
+# round-to-nearest-even, which NumPy reproduces exactly.
+# ---------------------------------------------------------------------------
+def to_fp8_tile_scaled(bits: np.ndarray):
+    """bf16 [M, N] bits -> (e4m3 codes [M, N], tile scales float32[T]).
+
+    Tile t (grid-row-major): amax_t = max |x| (NaN ignored); scale_t =
+    amax_t / 448, inv_t = 448 / amax_t (fp32 divisions; an all-zero tile has
+    scale 1 and inv 0); code = e4m3(fp32(x * inv_t)), round to nearest even."""
+    M, N = bits.shape
+    gm, gn, T, _, _ = tile_grid(M, N)
+    x = np.zeros((gm * BLOCK_M, gn * BLOCK_N), dtype=np.float32)
+    x[:M, :N] = bf16_to_f32(bits)
+    t = x.reshape(gm, BLOCK_M, gn, BLOCK_N).transpose(0, 2, 1, 3)
+    a = np.abs(t)
+    a = np.where(np.isnan(a), np.float32(0), a)
+    am = a.reshape(gm, gn, -1).max(axis=2).astype(np.float32)
+    pos = am > 0
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        scale = np.where(pos, am / np.float32(448), np.float32(1)).astype(np.float32)
+        inv = np.where(pos, np.float32(448) / am, np.float32(0)).astype(np.float32)
+        q = (t * inv[:, :, None, None]).astype(np.float32)
+    codes = f32_to_fp8(q, DT_E4M3).transpose(0, 2, 1, 3).reshape(gm * BLOCK_M, gn * BLOCK_N)
+    return np.ascontiguousarray(codes[:M, :N]), scale.reshape(-1)
+
+
+def reconstruct_tile_scaled(sp: "Sparse", scales: np.ndarray) -> np.ndarray:
+    """bf16 bits [M, N] of a per-tile-scaled e4m3 tensor: bf16(value(code) *
+    scale_t) where a value is stored, 0 elsewhere."""
+    M, N = sp.shape
+    codes = reconstruct(sp)
+    gm, gn = sp.grid_m, sp.grid_n
+    s = np.repeat(np.repeat(scales.reshape(gm, gn), BLOCK_M, 0), BLOCK_N, 1)[:M, :N]
+    with np.errstate(invalid="ignore", over="ignore"):
+        v = (fp8_to_f32(codes, DT_E4M3) * s).astype(np.float32)
+    return np.where(codes != 0, f32_to_bf16(v), np.uint16(0)).astype(np.uint16)
