@@ -821,7 +821,7 @@ def kernel_cases(which: str):
     tensor at 99% sparsity (the sparse-chunk scatter path); "dw" -- the
     fused reconstruct + tcgen05 weight-gradient GEMM at the config-2
     backward shape (go^T [768 x 8192] @ h [8192 x 3072], h 50% sparse),
-    timed against unpack + cuBLAS; "fp8_compress" -- the one-pass FP8
+    checked against the fp32 product and timed against unpack + cuBLAS; "fp8_compress" -- the one-pass FP8
     quantise + compress of an [8192, 8192] bf16 tensor, plain and with bias,
     ReLU and the square side output.  Each runs its kernel twice and checks
     the result."""
@@ -902,7 +902,8 @@ def kernel_cases(which: str):
         sp = dense_to_tilesparse(h, None)
         for _ in range(2):
             out = matmul_unpack_dw(go.T, sp)
-        if not torch.equal(out, matmul_relu_mask(go.T.contiguous(), h)):
+        ref = go.float().T @ h.float()  # (K is split here: partial sums in another order)
+        if (out.float() - ref).abs().max() > 1e-2 * ref.abs().max():
             raise RuntimeError("fused dW case mismatch")
         if os.environ.get("BS_CASE_TIMING", "1") == "1":
             def ev(fn, k=20):

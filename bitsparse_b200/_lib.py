@@ -57,7 +57,8 @@ _SIGS = {
     "bs_unpack_tile_scaled": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64,
                                      _i64, _i64, _vp]),
     "bs_gemm_unpack_dw": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i32, C.c_float,
-                                  _vp, _i64, _vp, _vp]),
+                                  _vp, _i64, _vp, _sz, _vp, _vp]),
+    "bs_gemm_unpack_dw_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "bs_gemm_bf16_relu2": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
                                   _vp, _vp, C.c_float, _vp, _vp]),
     "bs_tile_pack": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp]),

@@ -637,54 +637,70 @@ __global__ void __launch_bounds__(kThreadsG, 1)
 //   C[D, H] = g^T[D, T] . h[T, H]      h = unpack(stored)  or  k * unpack(stored)^2
 //
 // g is row-major [T, D] (grad_output), so A = g^T is MN-major; h is a bf16
-// bitsparse tensor [T, H].  The contraction runs over tokens, and a 64-token
-// x 64-column box of h is exactly one compressed tile: the B operand of a
-// stage is expanded straight from the compressed form into the 128-byte
-// swizzled MN-major layout tcgen05.mma reads, so the dense h never exists in
-// HBM.  CTA pairs (cta_group::2) share 256 x 256 tiles of C; per 64-token K
-// block a CTA loads its 128 rows of A (two 64 x 64 TMA boxes of g) and
-// expands its 128 columns of B (two tiles of h).
-//   warp 0      producer: A by TMA into the stage; the two tiles' bitmasks and
-//               value run (one contiguous 16-byte aligned superset) by 1-D
-//               bulk copies into a compressed-data slot, the tile prefixes
-//               read ahead through a cp.async ring;
-//   warp 1      MMA issuer (leader CTA), as in K3 with both operands MN-major;
-//   warps 2..5  epilogue (as K3 without a mask);
-//   warps 6..13 expanders: warp 6 + 4j + q expands rows 16q .. 16q + 15 of
-//               tile j -- lane = (row, 8-column chunk): the chunk's mask byte,
-//               its first rank from a scan of the row counts, the ranks of
-//               its 8 positions from one nibble-packed prefix sum, the set
-//               values read from the staged run (independent loads), one
-//               16-byte swizzled store -- then fence.proxy.async and an
-//               arrive on the leader's "full" barrier (which also counts the
-//               leader's A bytes).
+// bitsparse tensor [T, H].  A 64-token x 64-column box of h is exactly one
+// compressed tile, expanded by producer warps straight into the 128-byte
+// swizzled MN-major layout tcgen05.mma reads: the dense h never exists in
+// HBM.  Expansion runs on the CUDA cores, so each expanded tile is made to
+// feed as much tensor-core work as TMEM holds: a CTA pair (cta_group::2) owns
+// an (NMB x 256) x 128 block of C -- NMB m-blocks of 256 rows, one TMEM
+// accumulator of 128 columns each -- and per 64-token K step expands ONE
+// tile per CTA (its 64 of the 128 columns) for NMB MMAs of 256 x 128 x 64.
+// Small outputs split K over KS pair tiles (fp32 partials, summed in order
+// by `dw_reduce_kernel`) so that every SM pair has work.
+//   warp 0      producer: the NMB m-blocks' A boxes by TMA (two 64 x 64 atoms
+//               each); the tile's bitmask and value run (one 16-byte aligned
+//               superset) by 1-D bulk copies into a compressed-data slot, the
+//               tile prefixes read ahead through a cp.async ring;
+//   warp 1      leader CTA: MMA issuer; peer CTA: relay (below);
+//   warps 2..5  epilogue: TMEM -> bf16 -> TMA store, or fp32 partials;
+//   warps 6..13 expanders: warp 6 + e expands rows 8e .. 8e + 7 of the tile
+//               -- lane = (row, 8-column chunk): the chunk's mask byte, its
+//               first rank from a scan of the row counts, the ranks of its 8
+//               positions from one nibble-packed prefix sum, the set values
+//               read from the staged run, one 16-byte swizzled store -- then
+//               fence.proxy.async and a CTA-local arrive.
+// Stage completion: the leader's TMA bytes and its expanders' arrivals land on
+// the leader's barrier; the peer's expanders arrive on a barrier of their own
+// CTA and the peer's warp 1 relays one cluster-scope arrival per stage (a
+// cluster-scope release costs ~0.6 us, too much for every expander warp).
 // All waits are bounded (BS_STATUS_TIMEOUT); copies in flight are waited for
 // before the CTA exits; TMEM is always freed.
 constexpr int kThreadsD = 448;  // 14 warps
+constexpr int kDwBN = 128;      // columns of C per pair tile (64 per CTA: one tile of h)
+constexpr int kDwEpiBytes = 4 * kEpiBox;  // one staging box per epilogue warp
+template <int NMB>
 struct DwCfg {
-  static constexpr int BM = 2 * kBM;          // rows of C per pair tile
-  static constexpr int ABYTES = 2 * 8192;     // this CTA's 128 rows of A: two 64 x 64 atoms
-  static constexpr int BBYTES = 2 * 8192;     // this CTA's 128 columns of B: two tiles
+  static constexpr int BM = 2 * kBM;              // rows of one m-block (pair)
+  static constexpr int MG = NMB * BM;             // rows of C per pair tile
+  static constexpr int ABYTES = NMB * 2 * 8192;   // this CTA's 128 rows of each m-block
+  static constexpr int BBYTES = 8192;             // this CTA's 64 columns: one tile
   static constexpr int STAGE = ABYTES + BBYTES;
-  static constexpr int NST = 4;
-  static constexpr int RS = 3;                // compressed-data slots
-  static constexpr int RMETA = 16, RMASK = 2 * kTileBytes, RVALS = 2 * 8192 + 32;
+  static constexpr int RS = 3;                    // compressed-data slots
+  static constexpr int RMETA = 16, RMASK = kTileBytes, RVALS = 8192 + 32;
   static constexpr int RSLOT = RMETA + RMASK + RVALS;
-  static constexpr int LA = 8;                // prefix read-ahead (steps)
-  static constexpr size_t SMEM = 1024 + (size_t)NST * STAGE + (size_t)RS * RSLOT + kEpiBytes +
-                                 LA * 16 + 512;
-  // fp32 accumulator, bf16 A and B, both MN-major, N = 256, M = 256
+  static constexpr int LA = 8;                    // prefix read-ahead (steps)
+  static constexpr int NAB = NMB <= 2 ? 2 : 1;    // accumulator sets in TMEM (512 columns)
+  static constexpr size_t FIXED = 1024 + kDwEpiBytes + (size_t)RS * RSLOT + LA * 16 + 512;
+  static constexpr int NSTF = (int)((227 * 1024 - FIXED) / STAGE);
+  static constexpr int NST = NSTF > 6 ? 6 : NSTF;
+  static constexpr size_t SMEM = FIXED + (size_t)NST * STAGE;
+  // fp32 accumulator, bf16 A and B, both MN-major, N = 128, M = 256
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) |
-                                    (1u << 16) | ((uint32_t)(kBN >> 3) << 17) |
+                                    (1u << 16) | ((uint32_t)(kDwBN >> 3) << 17) |
                                     ((uint32_t)(BM >> 4) << 24);
+  static_assert(RSLOT % 16 == 0, "bulk-copy destinations stay 16-byte aligned");
+  static_assert(STAGE % 1024 == 0 && kDwEpiBytes % 1024 == 0,
+                "stages and staging boxes stay on 1024-byte boundaries");
+  static_assert(NST >= 2, "a pipeline needs two stages");
+  static_assert(NAB * NMB * kDwBN <= 512, "accumulators fit TMEM");
 };
-static_assert(DwCfg::RSLOT % 16 == 0, "bulk-copy destinations stay 16-byte aligned");
-static_assert(DwCfg::STAGE % 1024 == 0 && kEpiBytes % 1024 == 0,
-              "stages and staging boxes stay on 1024-byte boundaries");
 
 struct DwParams {
   uint8_t *C;
   int64_t M, N, K, ldc;      // D, H, T
+  float *part;               // split K: fp32 partials [ks][M][N], else null
+  int ks, kspan;             // K splits, 64-token blocks per split
+  int64_t mt, nt;            // pair tiles along M (m-groups) and N
   const uint8_t *vals;       // stored values (bf16), 16-byte aligned base
   const uint8_t *bitmask;    // [grid_m * grid_n] tiles of 512 bytes
   const uint32_t *prefix;    // [grid_m * grid_n + 1]
@@ -697,7 +713,7 @@ struct DwParams {
 __device__ __forceinline__ void mbar_arrive_local(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
 }
-// Bounded wait with cluster-scope acquire (the barrier counts arrivals
+// Bounded wait with cluster-scope acquire (the barrier counts an arrival
 // released by the peer CTA of the pair).
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity,
                                                   int32_t *status) {
@@ -739,22 +755,35 @@ __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(saddr(dst)), "l"(src) : "memory");
 }
 
-template <bool RELU2>
+// Pair tile t -> (K split, m-group, n-block): n fastest, so the pairs working
+// at the same time share their A rows (and K range) in L2.
+__device__ __forceinline__ void dw_tile(const DwParams &P, int64_t t, int &split, int64_t &mg,
+                                        int64_t &nb, int &kb0, int &kb1, int nk) {
+  nb = t % P.nt;
+  const int64_t r = t / P.nt;
+  mg = r % P.mt;
+  split = (int)(r / P.mt);
+  kb0 = split * P.kspan;
+  kb1 = kb0 + P.kspan < nk ? kb0 + P.kspan : nk;
+}
+
+template <int NMB, bool RELU2>
 __global__ void __launch_bounds__(kThreadsD, 1)
     dw_unpack_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmC, const DwParams P) {
-  using G = DwCfg;
+  using G = DwCfg<NMB>;
   constexpr int CG = 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   // stages and the epilogue's swizzled staging boxes on 1024-byte
   // boundaries (the 128-byte swizzle atoms), then the compressed-data slots
-  uint8_t *epi = smem + (size_t)G::NST * G::STAGE;   // epilogue staging boxes
-  uint8_t *raw = epi + kEpiBytes;                     // compressed-data slots
-  uint32_t *pref = reinterpret_cast<uint32_t *>(raw + (size_t)G::RS * G::RSLOT);  // prefix ring
+  uint8_t *epi = smem + (size_t)G::NST * G::STAGE;
+  uint8_t *raw = epi + kDwEpiBytes;
+  uint32_t *pref = reinterpret_cast<uint32_t *>(raw + (size_t)G::RS * G::RSLOT);  // [LA][4]
   uint64_t *full = reinterpret_cast<uint64_t *>(pref + 4 * G::LA);
-  uint64_t *empty = full + G::NST;
+  uint64_t *pfull = full + G::NST;  // peer CTA: its expanders' arrivals (relayed)
+  uint64_t *empty = pfull + G::NST;
   uint64_t *rfull = empty + G::NST;
   uint64_t *rempty = rfull + G::RS;
   uint64_t *acc_full = rempty + G::RS;
@@ -766,13 +795,14 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   const bool leader = rank == 0;
   const int64_t cid = (int64_t)blockIdx.x / CG, ncl = (int64_t)gridDim.x / CG;
   const int nk = (int)((P.K + kBK - 1) / kBK);
-  const int64_t mt = (P.M + G::BM - 1) / G::BM, nt = (P.N + kBN - 1) / kBN;
-  const int64_t ntiles = mt * nt;
+  const int64_t ntiles = P.mt * P.nt * P.ks;
 
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     for (int s = 0; s < G::NST; ++s) {
-      mbar_init(&full[s], 1 + 8 * CG);  // leader's A arrival + every expander warp of the pair
+      // leader: its A arrival + its 8 expander warps + the peer's relayed arrival
+      mbar_init(&full[s], 1 + 8 + 1);
+      mbar_init(&pfull[s], 8);
       mbar_init(&empty[s], 1);
     }
     for (int r = 0; r < G::RS; ++r) {
@@ -788,7 +818,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      saddr(tmem_slot)),
-                 "r"(2 * kTmemCols)
+                 "r"(512)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
@@ -796,34 +826,38 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // steps of this CTA: (its tile i = step / nk, K block step % nk)
-  const int64_t my_tiles = cid < ntiles ? (ntiles - cid + ncl - 1) / ncl : 0;
-  const int64_t nsteps = my_tiles * nk;
+  // this CTA pair's steps: the K blocks of its tiles cid, cid + ncl, ...
+  int64_t nsteps = 0;
+  for (int64_t t = cid; t < ntiles; t += ncl) {
+    int split, kb0, kb1;
+    int64_t mg, nb;
+    dw_tile(P, t, split, mg, nb, kb0, kb1, nk);
+    nsteps += kb1 > kb0 ? kb1 - kb0 : 0;
+  }
 
   if (warp == 0) {
     if (lane == 0) {
       const int64_t voff = *P.vals_offset;
-      // A step cursor: this CTA's tile t (its m / n block), K block kb, the
-      // tile index of its first tile column of h and how many of its two
-      // tiles exist (0 past the right edge of h).  Advanced without divisions.
+      // step cursor: tile t, its K range, its tile column of h and whether
+      // that tile exists (0 past the right edge of h)
       struct Cursor {
-        int64_t t, mb, nb, c0;
-        int kb, ntl;
+        int64_t t, mg, nb, c0;
+        int kb, kb1, ntl;
       };
       auto at_tile = [&](Cursor &c, int64_t t) {
-        c.t = t;
-        c.kb = 0;
-        if (t < ntiles) {
-          tile_coords(t, mt, nt, c.mb, c.nb);
-          c.c0 = c.nb * 4 + 2 * (int64_t)rank;
-          c.ntl = c.c0 < P.grid_n ? (c.c0 + 1 < P.grid_n ? 2 : 1) : 0;
+        for (;; t += ncl) {
+          c.t = t;
+          if (t >= ntiles) return;
+          int split;
+          dw_tile(P, t, split, c.mg, c.nb, c.kb, c.kb1, nk);
+          c.c0 = c.nb * 2 + (int64_t)rank;
+          c.ntl = c.c0 < P.grid_n ? 1 : 0;
+          if (c.kb < c.kb1) return;  // (an empty split has no steps)
         }
       };
       auto advance = [&](Cursor &c) {
-        if (++c.kb == nk) at_tile(c, c.t + ncl);
+        if (++c.kb == c.kb1) at_tile(c, c.t + ncl);
       };
-      // read ahead: ring entry i holds prefix[tfirst], [+1], [+ntl] of the
-      // step LA steps after the one that last used it
       Cursor ahead;
       at_tile(ahead, cid);
       int ring_in = 0;
@@ -834,7 +868,6 @@ __global__ void __launch_bounds__(kThreadsD, 1)
           if (ahead.ntl) {
             cp_async4(e, P.prefix + tf);
             cp_async4(e + 1, P.prefix + tf + 1);
-            cp_async4(e + 2, P.prefix + tf + ahead.ntl);
           }
           advance(ahead);
         }
@@ -845,11 +878,10 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       Cursor cur;
       at_tile(cur, cid);
       int s = 0, rs = 0, ring = 0;
-      uint32_t sph = 0, rph = 0;  // use parity of stage s / slot rs
+      uint32_t sph = 0, rph = 0;
       bool ok = true;
       int64_t j = 0;
       for (; j < nsteps && ok; ++j) {
-        // A: this CTA's 128 rows (columns of g) for tokens kb*64 ..
         if (j >= G::NST && !mbar_wait(&empty[s], sph ^ 1u, P.status)) {
           ok = false;
           break;
@@ -857,10 +889,12 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         uint8_t *a = smem + (size_t)s * G::STAGE;
         if (leader) mbar_expect_tx(&full[s], 2 * G::ABYTES);
         const uint32_t bar = map_rank(saddr(&full[s]), 0);
-        const int ax = (int)(cur.mb * G::BM + rank * kBM);
-        tma_load_2d_pair(a, &tmA, ax, cur.kb * kBK, bar);
-        tma_load_2d_pair(a + 8192, &tmA, ax + 64, cur.kb * kBK, bar);
-        // the compressed tiles of B
+#pragma unroll
+        for (int mi = 0; mi < NMB; ++mi) {
+          const int ax = (int)(cur.mg * G::MG + mi * G::BM + rank * kBM);
+          tma_load_2d_pair(a + mi * 16384, &tmA, ax, cur.kb * kBK, bar);
+          tma_load_2d_pair(a + mi * 16384 + 8192, &tmA, ax + 64, cur.kb * kBK, bar);
+        }
         if (j >= G::RS && !mbar_wait(&rempty[rs], rph ^ 1u, P.status)) {
           ok = false;
           break;
@@ -874,14 +908,13 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         int64_t a0 = 0;
         uint32_t *meta = reinterpret_cast<uint32_t *>(slot);
         if (ntl) {
-          const uint32_t p0 = e[0], p1 = e[1], p2 = e[2];
-          const int64_t b0 = (voff + p0) * 2, b1 = (voff + p2) * 2;
+          const uint32_t p0 = e[0], p1 = e[1];
+          const int64_t b0 = (voff + p0) * 2, b1 = (voff + p1) * 2;
           a0 = b0 & ~(int64_t)15;
           const int64_t a1 = (b1 + 15) & ~(int64_t)15;
-          vbytes = p2 > p0 ? (uint32_t)(a1 - a0) : 0u;  // no values: no copy
-          mbytes = (uint32_t)ntl * kTileBytes;
+          vbytes = p1 > p0 ? (uint32_t)(a1 - a0) : 0u;  // no values: no copy
+          mbytes = kTileBytes;
           meta[0] = (uint32_t)((b0 - a0) >> 1);  // first value's position in the slot
-          meta[1] = p1 - p0;                      // values of the first tile
         }
         meta[2] = (uint32_t)ntl;
         issue_prefix();  // the ring entry just read is reused for step j + LA
@@ -906,13 +939,17 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       int64_t it = 0;
       int jt = 0;
       bool ok = true;
-      for (int64_t t = cid; t < ntiles && ok; t += ncl, ++jt) {
-        const int buf = jt & 1;
-        if (jt >= 2 && !mbar_wait(&acc_empty[buf], (uint32_t)(((jt >> 1) - 1) & 1), P.status))
-          break;
+      for (int64_t t = cid; t < ntiles && ok; t += ncl) {
+        int split, kb0, kb1;
+        int64_t mg, nb;
+        dw_tile(P, t, split, mg, nb, kb0, kb1, nk);
+        if (kb1 <= kb0) continue;  // the epilogue skips it too
+        const int buf = jt % G::NAB;
+        const int use = jt / G::NAB;
+        if (use >= 1 && !mbar_wait(&acc_empty[buf], (uint32_t)((use - 1) & 1), P.status)) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * kTmemCols);
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        const uint32_t d0 = tmem + (uint32_t)(buf * NMB * kDwBN);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = (int)(it % G::NST);
           if (!mbar_wait_cluster(&full[s], (uint32_t)((it / G::NST) & 1), P.status)) {
             ok = false;
@@ -922,113 +959,151 @@ __global__ void __launch_bounds__(kThreadsD, 1)
           const uint32_t a = saddr(smem + (size_t)s * G::STAGE);
           const uint32_t b = a + G::ABYTES;
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            // both MN-major: 64-element atoms 8 KB apart (LBO), 8-row K
-            // groups 1024 B apart (SBO); +2048 B per K = 16
-            const uint64_t ad = smem_desc(a + 2048 * k, 8192, 1024);
-            const uint64_t bd = smem_desc(b + 2048 * k, 8192, 1024);
-            mma_bf16<CG>(d, ad, bd, G::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          for (int mi = 0; mi < NMB; ++mi) {
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              // both MN-major: 64-element atoms 8 KB apart (LBO), 8-row K
+              // groups 1024 B apart (SBO); +2048 B per K = 16
+              const uint64_t ad = smem_desc(a + mi * 16384 + 2048 * k, 8192, 1024);
+              const uint64_t bd = smem_desc(b + 2048 * k, 8192, 1024);
+              mma_bf16<CG>(d0 + (uint32_t)(mi * kDwBN), ad, bd, G::IDESC,
+                           (kb > kb0 || k > 0) ? 1u : 0u);
+            }
           }
           mma_commit_to<CG>(saddr(&empty[s]));
           mma_commit_to<CG>(map_rank(saddr(&empty[s]), 1));
         }
         mma_commit_to<CG>(saddr(&acc_full[buf]));
         mma_commit_to<CG>(map_rank(saddr(&acc_full[buf]), 1));
+        ++jt;
+      }
+    } else if (lane == 0) {
+      // peer relay: one cluster-scope arrival on the leader's stage barrier
+      // per stage, once this CTA's expanders have arrived locally
+      const uint32_t full_leader = map_rank(saddr(full), 0);
+      int s = 0;
+      uint32_t sph = 0;
+      for (int64_t j = 0; j < nsteps; ++j) {
+        if (!mbar_wait(&pfull[s], sph, P.status)) break;
+        mbar_arrive_cluster(full_leader + (uint32_t)(8 * s));
+        if (++s == G::NST) { s = 0; sph ^= 1u; }
       }
     }
   } else if (warp < 6) {
     // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (this CTA's rows)
     const int q = warp & 3;
     const uint32_t acc_empty_leader = map_rank(saddr(acc_empty), 0);
+    uint8_t *box = epi + (size_t)q * kEpiBox;
     int jt = 0;
-    for (int64_t t = cid; t < ntiles; t += ncl, ++jt) {
-      int64_t mb, nb;
-      tile_coords(t, mt, nt, mb, nb);
-      const int64_t row0 = mb * G::BM + rank * kBM + 32 * q;
-      const int64_t m = row0 + lane, n0 = nb * kBN;
-      const int buf = jt & 1;
-      const bool ok = mbar_wait(&acc_full[buf], (uint32_t)((jt >> 1) & 1), P.status);
+    for (int64_t t = cid; t < ntiles; t += ncl) {
+      int split, kb0, kb1;
+      int64_t mg, nb;
+      dw_tile(P, t, split, mg, nb, kb0, kb1, nk);
+      if (kb1 <= kb0) continue;
+      const int buf = jt % G::NAB;
+      const bool ok = mbar_wait(&acc_full[buf], (uint32_t)((jt / G::NAB) & 1), P.status);
       tc_fence_after();
       const uint32_t zero_guard = ok ? 0xFFFFFFFFu : 0u;
-      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTmemCols);
+#pragma unroll 1
+      for (int mi = 0; mi < NMB; ++mi) {
+        const int64_t row0 = mg * G::MG + mi * G::BM + rank * kBM + 32 * q;
+        const int64_t m = row0 + lane;
+        const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) +
+                               (uint32_t)((buf * NMB + mi) * kDwBN);
+#pragma unroll 1
+        for (int c = 0; c < kDwBN / 64; ++c) {
+          const int64_t n = nb * kDwBN + 64 * c;
+          uint32_t r[64];
+          tmem_ld32_nowait(tbase + (uint32_t)(64 * c), r);
+          tmem_ld32_nowait(tbase + (uint32_t)(64 * c + 32), r + 32);
+          tmem_wait_ld();
+          if (row0 >= P.M || n >= P.N) continue;  // (warp-uniform)
+          if (P.part) {  // split K: this split's fp32 partial row
+            if (m < P.M) {
+              float *dst = P.part + ((int64_t)split * P.M + m) * P.N + n;
+              if (n + 64 <= P.N && (P.N & 3) == 0) {
 #pragma unroll
-      for (int c = 0; c < kBN / 64; ++c) {
-        uint32_t r[64];
-        tmem_ld32_nowait(tbase + (uint32_t)(64 * c), r);
-        tmem_ld32_nowait(tbase + (uint32_t)(64 * c + 32), r + 32);
-        tmem_wait_ld();
-        uint32_t w[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) w[i] = bf16x2_rn(r[2 * i], r[2 * i + 1]) & zero_guard;
-        const int64_t n = n0 + 64 * c;
-        if (P.c_tma) {
-          uint8_t *box = epi + (size_t)(q * 2 + (c & 1)) * kEpiBox;
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-          __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<uint4 *>(box + lane * 128 + ((i ^ (lane & 7)) * 16)) =
-                make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0 && n < P.N && row0 < P.M) {
-            asm volatile(
-                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                    reinterpret_cast<uint64_t>(&tmC)),
-                "r"((int)n), "r"((int)row0), "r"(saddr(box))
-                : "memory");
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                for (int i = 0; i < 16; ++i)
+                  *reinterpret_cast<uint4 *>(dst + 4 * i) =
+                      make_uint4(r[4 * i] & zero_guard, r[4 * i + 1] & zero_guard,
+                                 r[4 * i + 2] & zero_guard, r[4 * i + 3] & zero_guard);
+              } else {
+                for (int i = 0; i < 64 && n + i < P.N; ++i)
+                  dst[i] = __uint_as_float(r[i] & zero_guard);
+              }
+            }
+            continue;
           }
-        } else if (m < P.M) {
-          for (int i = 0; i < 64 && n + i < P.N; ++i)
-            reinterpret_cast<uint16_t *>(P.C + (m * P.ldc + n) * 2)[i] =
-                (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+          uint32_t w[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = bf16x2_rn(r[2 * i], r[2 * i + 1]) & zero_guard;
+          if (P.c_tma) {
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<uint4 *>(box + lane * 128 + ((i ^ (lane & 7)) * 16)) =
+                  make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              asm volatile(
+                  "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                      reinterpret_cast<uint64_t>(&tmC)),
+                  "r"((int)n), "r"((int)row0), "r"(saddr(box))
+                  : "memory");
+              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
+          } else if (m < P.M) {
+            for (int i = 0; i < 64 && n + i < P.N; ++i)
+              reinterpret_cast<uint16_t *>(P.C + (m * P.ldc + n) * 2)[i] =
+                  (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty_leader + (uint32_t)(8 * buf));
+      ++jt;
     }
   } else {
-    // expanders: warp 6 + 4 * tj + qq -> rows 16 qq .. + 15 of this CTA's tile tj
-    const int e = warp - 6, tj = e >> 2, qq = e & 3;
-    const int r0 = 16 * qq;
-    const uint32_t full_leader = map_rank(saddr(full), 0);
+    // expanders: warp 6 + e -> rows 8e .. 8e + 7 of this CTA's tile
+    const int e = warp - 6;
+    const int r0 = 8 * e;
     int s = 0, rs = 0;
     uint32_t sph = 0, rph = 0;
     for (int64_t j = 0; j < nsteps; ++j) {
       if (!mbar_wait(&rfull[rs], rph, P.status)) break;
       if (j >= G::NST && !mbar_wait(&empty[s], sph ^ 1u, P.status)) break;
       const uint32_t slot = saddr(raw + (size_t)rs * G::RSLOT);
-      const uint32_t box = saddr(smem + (size_t)s * G::STAGE + G::ABYTES + tj * 8192);
-      const uint32_t ntl = lds_u32(slot + 8);
-      if (tj < (int)ntl) {
-        const uint32_t mw = slot + G::RMETA + tj * kTileBytes;  // the tile's 64 row words
-        const uint32_t sv = slot + G::RMETA + G::RMASK;          // staged values (bf16)
-        // values of the tile's rows before this warp's 16
+      const uint32_t box = saddr(smem + (size_t)s * G::STAGE + G::ABYTES);
+      if (lds_u32(slot + 8)) {
+        const uint32_t mw = slot + G::RMETA;           // the tile's 64 row words
+        const uint32_t sv = slot + G::RMETA + G::RMASK;  // staged values (bf16)
+        // values of the tile's rows before this warp's 8
         uint32_t before = 0;
-        if (qq) {
+        if (e) {
           const uint64_t wa = lds_u64(mw + 8 * lane), wb = lds_u64(mw + 8 * (32 + lane));
           before = (lane < r0 ? (uint32_t)__popcll(wa) : 0u) +
                    (lane + 32 < r0 ? (uint32_t)__popcll(wb) : 0u);
           before = __reduce_add_sync(0xFFFFFFFFu, before);
         }
-        // lanes l and l + 16 hold row r0 + l: its word and first value's slot position
-        const uint64_t my = lds_u64(mw + 8 * (r0 + (lane & 15)));
+        // lanes l, l + 8, l + 16, l + 24 hold row r0 + l: its word and the
+        // slot position of its first value
+        const uint64_t my = lds_u64(mw + 8 * (r0 + (lane & 7)));
         const uint32_t cnt = (uint32_t)__popcll(my);
         uint32_t inc = cnt;
 #pragma unroll
-        for (int d = 1; d < 16; d <<= 1) {
-          const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, d, 16);
-          if ((lane & 15) >= d) inc += v;
+        for (int d = 1; d < 8; d <<= 1) {
+          const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, inc, d, 8);
+          if ((lane & 7) >= d) inc += v;
         }
-        const uint32_t rowbase =
-            lds_u32(slot) + (tj ? lds_u32(slot + 4) : 0u) + before + inc - cnt;
+        const uint32_t rowbase = lds_u32(slot) + before + inc - cnt;
         const uint32_t mlo = (uint32_t)my, mhi = (uint32_t)(my >> 32);
         const int c = lane & 7;
 #pragma unroll
-        for (int st = 0; st < 4; ++st) {
-          const int rl = 4 * st + (lane >> 3);  // row within this warp's 16
+        for (int st = 0; st < 2; ++st) {
+          const int rl = 4 * st + (lane >> 3);  // row within this warp's 8
           const uint32_t wlo = __shfl_sync(0xFFFFFFFFu, mlo, rl);
           const uint32_t whi = __shfl_sync(0xFFFFFFFFu, mhi, rl);
           uint32_t p = __shfl_sync(0xFFFFFFFFu, rowbase, rl);
@@ -1059,13 +1134,13 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         }
       } else {  // no tile here (right edge of h): zero columns
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sts_v4(box + r0 * 128 + (i * 32 + lane) * 16, 0, 0, 0, 0);
+        for (int i = 0; i < 2; ++i) sts_v4(box + r0 * 128 + (i * 32 + lane) * 16, 0, 0, 0, 0);
       }
       fence_proxy_async_smem();  // B writes (and slot reads) before the async proxy's use
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_local(&rempty[rs]);
-        mbar_arrive_cluster(full_leader + (uint32_t)(8 * s));
+        mbar_arrive_local(leader ? &full[s] : &pfull[s]);
       }
       if (++s == G::NST) { s = 0; sph ^= 1u; }
       if (++rs == G::RS) { rs = 0; rph ^= 1u; }
@@ -1076,9 +1151,22 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(2 * kTmemCols)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512)
                  : "memory");
+  }
+}
+
+// Split K: C = bf16(sum over the splits, in order, of the fp32 partials).
+__global__ void __launch_bounds__(256) dw_reduce_kernel(const float *part, int ks, int64_t M,
+                                                         int64_t N, uint8_t *C, int64_t ldc) {
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = part[i];
+    for (int k = 1; k < ks; ++k) acc += part[(int64_t)k * total + i];
+    const int64_t m = i / N, n = i - m * N;
+    reinterpret_cast<uint16_t *>(C + (m * ldc + n) * 2)[0] =
+        (uint16_t)bf16x2_rn(__float_as_uint(acc), 0u);
   }
 }
 
@@ -1291,30 +1379,64 @@ extern "C" int bs_gemm_fp8_relu2(const void *A, int64_t lda, const void *Bt, int
 
 namespace bs {
 namespace {
-template <bool RELU2>
-int launch_dw(const CUtensorMap &ta, const CUtensorMap &tc, const DwParams &P, cudaStream_t st) {
-  using G = DwCfg;
-  static_assert(G::SMEM <= 227 * 1024, "shared memory of one CTA");
-  auto kernel = dw_unpack_kernel<RELU2>;
+// The K5 plan: NMB m-blocks per pair tile (as many as TMEM holds, spread
+// evenly over the m-groups), the pair tiles, and a K split when the tiles
+// alone leave SM pairs idle (at least 16 K blocks per split).
+struct DwPlan {
+  int nmb, ks, kspan, nk;
+  int64_t mt, nt;
+};
+DwPlan dw_plan(int64_t T, int64_t D, int64_t H, int sms) {
+  DwPlan p{};
+  const int64_t mb = (D + 2 * kBM - 1) / (2 * kBM);
+  p.mt = (mb + 3) / 4;
+  p.nmb = (int)((mb + p.mt - 1) / p.mt);
+  p.nt = (H + kDwBN - 1) / kDwBN;
+  p.nk = (int)((T + kBK - 1) / kBK);
+  const int64_t tiles = p.mt * p.nt, pairs = sms / 2;
+  int64_t ks = 1;
+  if (tiles < pairs && p.nk >= 32) {
+    ks = pairs / tiles;
+    if (ks > p.nk / 16) ks = p.nk / 16;
+    if (ks < 1) ks = 1;
+  }
+  p.kspan = (int)((p.nk + ks - 1) / ks);
+  p.ks = p.kspan ? (p.nk + p.kspan - 1) / p.kspan : 1;  // no empty split
+  return p;
+}
+int dev_sms() {
   constexpr int kMaxDev = 64;
-  static std::mutex mu;
   static int sms_of[kMaxDev] = {};
   int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 0;
+  if (!sms_of[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    sms_of[dev] = n;  // benign race: every writer stores the same value
+  }
+  return sms_of[dev];
+}
+template <int NMB, bool RELU2>
+int launch_dw(const CUtensorMap &ta, const CUtensorMap &tc, const DwParams &P, int sms,
+              cudaStream_t st) {
+  using G = DwCfg<NMB>;
+  static_assert(G::SMEM <= 227 * 1024, "shared memory of one CTA");
+  auto kernel = dw_unpack_kernel<NMB, RELU2>;
+  constexpr int kMaxDev = 64;
+  static std::mutex mu;
+  static bool set_on[kMaxDev] = {};
+  int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return BS_ERR_LAUNCH;
-  int sms;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (!sms_of[dev]) {
-      int n = 0;
+    if (!set_on[dev]) {
       if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)G::SMEM) != cudaSuccess ||
-          cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+                               (int)G::SMEM) != cudaSuccess)
         return BS_ERR_LAUNCH;
-      sms_of[dev] = n;
+      set_on[dev] = true;
     }
-    sms = sms_of[dev];
   }
-  const int64_t tiles = ((P.M + G::BM - 1) / G::BM) * ((P.N + kBN - 1) / kBN);
+  const int64_t tiles = P.mt * P.nt * P.ks;
   const int64_t slots = sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * (tiles < slots ? tiles : slots)));
@@ -1331,14 +1453,32 @@ int launch_dw(const CUtensorMap &ta, const CUtensorMap &tc, const DwParams &P, c
   if (cudaLaunchKernelEx(&cfg, kernel, ta, tc, P) != cudaSuccess) return BS_ERR_LAUNCH;
   return BS_OK;
 }
+template <bool RELU2>
+int launch_dw_nmb(int nmb, const CUtensorMap &ta, const CUtensorMap &tc, const DwParams &P,
+                  int sms, cudaStream_t st) {
+  switch (nmb) {
+    case 1: return launch_dw<1, RELU2>(ta, tc, P, sms, st);
+    case 2: return launch_dw<2, RELU2>(ta, tc, P, sms, st);
+    case 3: return launch_dw<3, RELU2>(ta, tc, P, sms, st);
+    default: return launch_dw<4, RELU2>(ta, tc, P, sms, st);
+  }
+}
 }  // namespace
 }  // namespace bs
+
+extern "C" size_t bs_gemm_unpack_dw_workspace_bytes(int64_t T, int64_t D, int64_t H) {
+  if (T <= 0 || D <= 0 || H <= 0) return 0;
+  const int sms = dev_sms();
+  if (sms <= 0) return 0;
+  const DwPlan p = dw_plan(T, D, H, sms);
+  return p.ks > 1 ? (size_t)p.ks * (size_t)D * (size_t)H * sizeof(float) : 0;
+}
 
 extern "C" int bs_gemm_unpack_dw(const void *g, int64_t ldg, int64_t T, int64_t D,
                                  const void *vals, const uint8_t *bitmask,
                                  const uint32_t *prefix, const int64_t *vals_offset, int64_t H,
-                                 int relu2, float k, void *C, int64_t ldc, int32_t *status,
-                                 void *stream) {
+                                 int relu2, float k, void *C, int64_t ldc, void *workspace,
+                                 size_t workspace_bytes, int32_t *status, void *stream) {
   if (T < 0 || D < 0 || H < 0) return BS_ERR_SHAPE;
   if (D == 0 || H == 0) return BS_OK;
   // (vals may be null when the tensor holds no values)
@@ -1358,9 +1498,22 @@ extern "C" int bs_gemm_unpack_dw(const void *g, int64_t ldg, int64_t T, int64_t 
         return BS_ERR_LAUNCH;
     return BS_OK;
   }
+  const int sms = dev_sms();
+  if (sms < 2) return BS_ERR_LAUNCH;
+  const DwPlan plan = dw_plan(T, D, H, sms);
   DwParams P{};
+  if (plan.ks > 1) {
+    const size_t need = (size_t)plan.ks * (size_t)D * (size_t)H * sizeof(float);
+    if (!workspace || workspace_bytes < need) return BS_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return BS_ERR_ALIGN;
+    P.part = static_cast<float *>(workspace);
+  }
   P.C = static_cast<uint8_t *>(C);
   P.M = D; P.N = H; P.K = T; P.ldc = ldc;
+  P.ks = plan.ks;
+  P.kspan = plan.kspan;
+  P.mt = plan.mt;
+  P.nt = plan.nt;
   P.vals = static_cast<const uint8_t *>(vals);
   P.bitmask = bitmask;
   P.prefix = prefix;
@@ -1372,5 +1525,13 @@ extern "C" int bs_gemm_unpack_dw(const void *g, int64_t ldg, int64_t T, int64_t 
   if (!make_map(&ta, g, T, D, ldg, 64, 64)) return BS_ERR_ALIGN;
   if (P.c_tma && !make_map(&tc, C, D, H, ldc, 64, 32)) P.c_tma = 0;
   if (!P.c_tma) tc = ta;  // unused
-  return relu2 ? launch_dw<true>(ta, tc, P, st) : launch_dw<false>(ta, tc, P, st);
+  int rc = relu2 ? launch_dw_nmb<true>(plan.nmb, ta, tc, P, sms, st)
+                 : launch_dw_nmb<false>(plan.nmb, ta, tc, P, sms, st);
+  if (rc != BS_OK || plan.ks == 1) return rc;
+  const int64_t total = D * H;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > (int64_t)sms * 8) blocks = (int64_t)sms * 8;
+  dw_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(P.part, plan.ks, D, H,
+                                                      static_cast<uint8_t *>(C), ldc);
+  return cudaGetLastError() == cudaSuccess ? BS_OK : BS_ERR_LAUNCH;
 }

@@ -366,10 +366,15 @@ def matmul_unpack_dw(a: Tensor, sparse: BitsparseTensor, relu2: bool = False) ->
         return None
     H = sparse.shape[1]
     out = torch.empty((D, H), device=a.device, dtype=torch.bfloat16)
-    rc = _lib.load().bs_gemm_unpack_dw(
+    lib = _lib.load()
+    with torch.cuda.device(a.device):
+        wsb = int(lib.bs_gemm_unpack_dw_workspace_bytes(T, D, H))
+    ws = torch.empty(wsb // 4 + 4, device=a.device, dtype=torch.float32) if wsb else None
+    rc = lib.bs_gemm_unpack_dw(
         a.data_ptr(), a.stride(1), T, D, sparse.vals.data_ptr(), sparse.bitmask.data_ptr(),
         sparse.prefix.data_ptr(), sparse.vals_offset.data_ptr(), H, int(relu2),
-        float(RELU2_SCALE), out.data_ptr(), H, R.status_word(a.device).data_ptr(), _stream(a))
+        float(RELU2_SCALE), out.data_ptr(), H, R.ptr(ws), wsb, R.status_word(a.device).data_ptr(),
+        _stream(a))
     if rc == _lib.BS_ERR_ALIGN:
         return None
     _lib.check(rc, "bs_gemm_unpack_dw")

@@ -350,13 +350,21 @@ int bs_gemm_fp8_relu2(const void *A, int64_t lda, const void *Bt, int64_t ldb, v
  * storage, 64 x 64 tiles); C: bf16 [D, H] (row stride ldc).  Each 64 x 64
  * tile of h is expanded from its compressed form straight into the tensor
  * cores' shared-memory operand; the dense h is never written.  fp32
- * accumulation, C rounded to bf16 once.  status: as bs_compress (bounded
- * waits).  BS_ERR_ALIGN when g, vals or bitmask cannot be read by TMA /
- * bulk copies. */
+ * accumulation (over K splits: fp32 partials summed in order), C rounded to
+ * bf16 once.  workspace: bs_gemm_unpack_dw_workspace_bytes(T, D, H) bytes,
+ * 16-byte aligned (may be null when that is 0; BS_ERR_WORKSPACE when short).
+ * status: as bs_compress (bounded waits).  BS_ERR_ALIGN when g, vals or
+ * bitmask cannot be read by TMA / bulk copies. */
 int bs_gemm_unpack_dw(const void *g, int64_t ldg, int64_t T, int64_t D, const void *vals,
                       const uint8_t *bitmask, const uint32_t *prefix,
                       const int64_t *vals_offset, int64_t H, int relu2, float k, void *C,
-                      int64_t ldc, int32_t *status, void *stream);
+                      int64_t ldc, void *workspace, size_t workspace_bytes, int32_t *status,
+                      void *stream);
+
+/* Bytes of workspace bs_gemm_unpack_dw needs for these sizes on the current
+ * device: when the output has too few tiles to occupy every SM pair, K is
+ * split and the fp32 partials (splits x D x H) live there; 0 otherwise. */
+size_t bs_gemm_unpack_dw_workspace_bytes(int64_t T, int64_t D, int64_t H);
 
 /* Per-tile FP8 scale mode -- an extension: the reference's to_fp8 uses one
  * scale per tensor (lib_sparse/fp8.py:123-129).  A bf16 [M, N] tensor (row
