@@ -651,18 +651,18 @@ __global__ void __launch_bounds__(kThreadsG, 1)
 //               each); the tile's bitmask and value run (one 16-byte aligned
 //               superset) by 1-D bulk copies into a compressed-data slot, the
 //               tile prefixes read ahead through a cp.async ring;
-//   warp 1      leader CTA: MMA issuer; peer CTA: relay (below);
+//   warp 1      MMA issuer (leader CTA);
 //   warps 2..5  epilogue: TMEM -> bf16 -> TMA store, or fp32 partials;
 //   warps 6..13 expanders: warp 6 + e expands rows 8e .. 8e + 7 of the tile
 //               -- lane = (row, 8-column chunk): the chunk's mask byte, its
 //               first rank from a scan of the row counts, the ranks of its 8
 //               positions from one nibble-packed prefix sum, the set values
 //               read from the staged run, one 16-byte swizzled store -- then
-//               fence.proxy.async and a CTA-local arrive.
-// Stage completion: the leader's TMA bytes and its expanders' arrivals land on
-// the leader's barrier; the peer's expanders arrive on a barrier of their own
-// CTA and the peer's warp 1 relays one cluster-scope arrival per stage (a
-// cluster-scope release costs ~0.6 us, too much for every expander warp).
+//               fence.proxy.async and the stage arrival (below).
+// Stage completion: the leader's TMA bytes and its expanders' local arrivals
+// land on the leader's barrier; each of the peer's expander warps completes 4
+// transaction bytes on it with st.async (asynchronous, released at cluster
+// scope) -- a blocking cluster-scope arrive costs 0.6-1 us per warp.
 // All waits are bounded (BS_STATUS_TIMEOUT); copies in flight are waited for
 // before the CTA exits; TMEM is always freed.
 constexpr int kThreadsD = 448;  // 14 warps
@@ -782,13 +782,13 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   uint8_t *raw = epi + kDwEpiBytes;
   uint32_t *pref = reinterpret_cast<uint32_t *>(raw + (size_t)G::RS * G::RSLOT);  // [LA][4]
   uint64_t *full = reinterpret_cast<uint64_t *>(pref + 4 * G::LA);
-  uint64_t *pfull = full + G::NST;  // peer CTA: its expanders' arrivals (relayed)
-  uint64_t *empty = pfull + G::NST;
+  uint64_t *empty = full + G::NST;
   uint64_t *rfull = empty + G::NST;
   uint64_t *rempty = rfull + G::RS;
   uint64_t *acc_full = rempty + G::RS;
   uint64_t *acc_empty = acc_full + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  uint32_t *sig = tmem_slot + 4;  // [8] the peer expanders' st.async targets (values unused)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -800,9 +800,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     for (int s = 0; s < G::NST; ++s) {
-      // leader: its A arrival + its 8 expander warps + the peer's relayed arrival
-      mbar_init(&full[s], 1 + 8 + 1);
-      mbar_init(&pfull[s], 8);
+      // leader: its A arrival + its 8 expander warps (the peer's expanders
+      // complete transaction bytes on it with st.async)
+      mbar_init(&full[s], 1 + 8);
       mbar_init(&empty[s], 1);
     }
     for (int r = 0; r < G::RS; ++r) {
@@ -887,7 +887,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
           break;
         }
         uint8_t *a = smem + (size_t)s * G::STAGE;
-        if (leader) mbar_expect_tx(&full[s], 2 * G::ABYTES);
+        if (leader) mbar_expect_tx(&full[s], 2 * G::ABYTES + 8 * 4);
         const uint32_t bar = map_rank(saddr(&full[s]), 0);
 #pragma unroll
         for (int mi = 0; mi < NMB; ++mi) {
@@ -977,17 +977,6 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         mma_commit_to<CG>(map_rank(saddr(&acc_full[buf]), 1));
         ++jt;
       }
-    } else if (lane == 0) {
-      // peer relay: one cluster-scope arrival on the leader's stage barrier
-      // per stage, once this CTA's expanders have arrived locally
-      const uint32_t full_leader = map_rank(saddr(full), 0);
-      int s = 0;
-      uint32_t sph = 0;
-      for (int64_t j = 0; j < nsteps; ++j) {
-        if (!mbar_wait(&pfull[s], sph, P.status)) break;
-        mbar_arrive_cluster(full_leader + (uint32_t)(8 * s));
-        if (++s == G::NST) { s = 0; sph ^= 1u; }
-      }
     }
   } else if (warp < 6) {
     // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (this CTA's rows)
@@ -1070,6 +1059,8 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     // expanders: warp 6 + e -> rows 8e .. 8e + 7 of this CTA's tile
     const int e = warp - 6;
     const int r0 = 8 * e;
+    const uint32_t full_leader = map_rank(saddr(full), 0);
+    const uint32_t sig_leader = map_rank(saddr(sig), 0);
     int s = 0, rs = 0;
     uint32_t sph = 0, rph = 0;
     for (int64_t j = 0; j < nsteps; ++j) {
@@ -1140,7 +1131,18 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_local(&rempty[rs]);
-        mbar_arrive_local(leader ? &full[s] : &pfull[s]);
+        if (leader) {
+          mbar_arrive_local(&full[s]);
+        } else {
+          // 4 bytes into the leader's signal word with a complete-tx on its
+          // stage barrier: asynchronous, released at cluster scope, so this
+          // warp does not wait for the cluster-wide visibility of its tile
+          asm volatile(
+              "st.async.shared::cluster.mbarrier::complete_tx::bytes.u32 [%0], %1, [%2];" ::"r"(
+                  sig_leader + (uint32_t)(4 * e)),
+              "r"((uint32_t)j), "r"(full_leader + (uint32_t)(8 * s))
+              : "memory");
+        }
       }
       if (++s == G::NST) { s = 0; sph ^= 1u; }
       if (++rs == G::RS) { rs = 0; rph ^= 1u; }
@@ -1389,7 +1391,15 @@ struct DwPlan {
 DwPlan dw_plan(int64_t T, int64_t D, int64_t H, int sms) {
   DwPlan p{};
   const int64_t mb = (D + 2 * kBM - 1) / (2 * kBM);
-  p.mt = (mb + 3) / 4;
+  // at most 4 m-blocks per pair tile (TMEM); BS_DW_MAX_NMB lowers the cap
+  // for measurements (more stages fit with fewer m-blocks, at the cost of
+  // expanding each tile for more m-groups: 3 and 4 measure alike, 2 slower)
+  static const int max_nmb = [] {
+    const char *e = getenv("BS_DW_MAX_NMB");
+    const int v = e ? atoi(e) : 4;
+    return v < 1 ? 1 : (v > 4 ? 4 : v);
+  }();
+  p.mt = (mb + max_nmb - 1) / max_nmb;
   p.nmb = (int)((mb + p.mt - 1) / p.mt);
   p.nt = (H + kDwBN - 1) / kDwBN;
   p.nk = (int)((T + kBK - 1) / kBK);
