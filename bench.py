@@ -918,11 +918,16 @@ def kernel_cases(which: str):
                 torch.cuda.synchronize()
                 return e0.elapsed_time(e1) / k * 1e3
             SM.FUSED_DW = False
-            fused = ev(lambda: matmul_unpack_dw(go.T, sp))
-            unf = ev(lambda: SM.AspB(go.T, sp))
-            cub = ev(lambda: go.T @ h)
-            print(f"dW {D}x{T}x{H}: fused {fused:.1f} us, unpack + cuBLAS {unf:.1f} us, "
-                  f"cuBLAS alone {cub:.1f} us")
+            for (T2, D2, H2) in ((T, D, H), (8192, 1024, 4096), (16384, 4096, 16384)):
+                if (T2, D2, H2) != (T, D, H):
+                    go = torch.randn(T2, D2, generator=g, device=dev).to(torch.bfloat16)
+                    h = torch.randn(T2, H2, generator=g, device=dev).relu().to(torch.bfloat16)
+                    sp = dense_to_tilesparse(h, None)
+                fused = ev(lambda: matmul_unpack_dw(go.T, sp))
+                unf = ev(lambda: SM.AspB(go.T, sp))
+                cub = ev(lambda: go.T @ h)
+                print(f"dW {D2}x{T2}x{H2}: fused {fused:.1f} us, unpack + cuBLAS {unf:.1f} us, "
+                      f"cuBLAS alone {cub:.1f} us")
     elif which == "tile_scaled":
         # per-tile FP8 scale mode: one pass (tile amax, quantise, compress)
         # against the per-tensor path (amax pass + quantise + compress), and
