@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(kThreads) relu2_grad_kernel(const UnpackParams
 // zeroed 32-byte row of `scratch` and written out with one 32-byte store
 // (element stores at the right edge).  `trips`: the largest count of any
 // lane of the warp (the loop runs in step across the warp).
-template <int SDT, bool PACK>
+template <int SDT, bool PACK, bool SQ = false>
 __device__ __forceinline__ void scatter_chunk(const uint8_t *stg, uint32_t first, uint32_t r,
                                            uint32_t mm, uint32_t trips, uint8_t *scratch,
                                            uint8_t *dst, bool vec, int valid) {
@@ -550,7 +550,11 @@ __device__ __forceinline__ void scatter_chunk(const uint8_t *stg, uint32_t first
     }
   }
   const uint4 lo = *q0, hi = *q1;
-  const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  if constexpr (SQ) {  // ReLU^2 of bf16 storage, k = 1: bf16(v * v)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = bf16x2_mul(w[i], w[i]);
+  }
   if (vec) {
     st_v8(dst, w);
   } else {
@@ -577,8 +581,12 @@ constexpr int kPipeMaskBytes = kUT * kTileBytes;
 // BS_STATUS_TIMEOUT when a bounded wait gave up.  Read with bs_unpack_status.
 __device__ int32_t g_unpack_status = 0;
 
-template <int SDT, bool PACK>
+// SQ: the ReLU^2 reconstruct of bf16 storage with k = 1 (RELU2_SCALE): each
+// output word squared with one bf16x2 product, the rounding of the
+// reference's bf16 `v * v` (triton_kernels.py:238).
+template <int SDT, bool PACK, bool SQ = false>
 __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParams P) {
+  static_assert(!SQ || SDT == BS_BF16, "the fused square is for bf16 storage");
   constexpr int SB = Elt<SDT>::bytes;
   using G = Chunk<SB>;
   __shared__ __align__(128) uint8_t stage[2][kStageBytes];
@@ -690,7 +698,7 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
         const int64_t grow = tr * kTileM + row;
         const int64_t gcol = tc * kTileN + colc * G::VEC;
         if (grow >= P.batch_rows) continue;
-        scatter_chunk<SDT, PACK>(stg, first, ex[s], m[s], most, scratch,
+        scatter_chunk<SDT, PACK, SQ>(stg, first, ex[s], m[s], most, scratch,
                                  P.out + (grow * P.out_ld + gcol) * SB,
                                  P.out_v32 && gcol + G::VEC <= P.K, (int)(P.K - gcol));
       }
@@ -726,6 +734,10 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
         if constexpr (SB == 1) w[e >> 2] |= v << (8 * (e & 3));
         else w[e >> 1] |= v << (16 * (e & 1));
       }
+      if constexpr (SQ) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = bf16x2_mul(w[i], w[i]);
+      }
       if (P.out_v32 && gcol + G::VEC <= P.K) {
         st_v8(dst, w);
       } else {
@@ -753,7 +765,7 @@ bool aligned(const void *p, int a) { return (reinterpret_cast<uintptr_t>(p) & (a
 unsigned ctas(int64_t ntiles) { return (unsigned)((ntiles + kUT - 1) / kUT); }
 
 // Resident CTAs of the pipelined kernel on the current device (cached).
-template <int SDT, bool PACK>
+template <int SDT, bool PACK, bool SQ = false>
 int pipe_resident() {
   constexpr int kMaxDev = 64;
   static int cache[kMaxDev] = {};
@@ -762,7 +774,7 @@ int pipe_resident() {
   if (!cache[dev]) {
     int sms = 0, per_sm = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, unpack_pipe_kernel<SDT, PACK>,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, unpack_pipe_kernel<SDT, PACK, SQ>,
                                                       kThreads, 0) != cudaSuccess)
       return 0;
     cache[dev] = sms * per_sm;  // benign race: every writer stores the same value
@@ -780,6 +792,18 @@ int unpack_disp2(const UnpackParams &P, int relu2, bool scale, cudaStream_t st) 
       unpack_pipe_kernel<SDT, PACK>
           <<<(unsigned)(npairs < res ? npairs : res), kThreads, 0, st>>>(P);
       return launch_err();
+    }
+  }
+  if constexpr (SDT == BS_BF16) {  // ReLU^2 of bf16 storage (k = 1, no scale): pipelined too
+    if (relu2 && !scale && P.k == 1.0f && P.vals_v16 && aligned(P.bitmask, 16) &&
+        !getenv("BS_UNPACK_PER_CTA")) {
+      const int res = pipe_resident<SDT, PACK, true>();
+      const int64_t npairs = (P.ntiles + kUT - 1) / kUT;
+      if (res > 0) {
+        unpack_pipe_kernel<SDT, PACK, true>
+            <<<(unsigned)(npairs < res ? npairs : res), kThreads, 0, st>>>(P);
+        return launch_err();
+      }
     }
   }
   if (!relu2) unpack_kernel<SDT, PACK, 0, false><<<g, kThreads, 0, st>>>(P);
