@@ -19,6 +19,7 @@
 // scale passes (output *= scale^2, grad *= scale) are fused, keeping the
 // reference's double rounding.
 #include <cstdlib>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -253,7 +254,10 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
   // each CTA tabulates it once (256 codes, one per thread) and the element
   // loop becomes a table lookup.
   constexpr bool LUT = SDT != BS_BF16 && OUT >= 1;
-  __shared__ uint32_t lut[LUT ? 256 : 1];
+  // OUT 2 tabulates 8-bit codes: a byte table spreads its 256 entries over
+  // 64 words, so random lookups of a warp collide in fewer banks
+  using LutT = typename std::conditional<OUT == 2, uint8_t, uint32_t>::type;
+  __shared__ LutT lut[LUT ? 256 : 1];
   static_assert(!LUT || kThreads == 256, "one table entry per thread");
 
   const int64_t pid0 = (int64_t)blockIdx.x * kUT;
@@ -262,7 +266,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const UnpackParams P) 
   const int tid = threadIdx.x;
   if constexpr (LUT) {
     if constexpr (OUT == 3) lut[tid] = __float_as_uint(store_bits_to_f32<SDT>((uint32_t)tid));
-    else lut[tid] = relu2_out<SDT, OUT, SCALE>(P, tid);
+    else lut[tid] = (LutT)relu2_out<SDT, OUT, SCALE>(P, tid);
   }
   uint32_t m[G::S], cnt[G::S], ex[G::S];
 #pragma unroll
