@@ -733,16 +733,20 @@ __device__ __forceinline__ void emit_words(const CompressParams &P, const uint8_
 }
 
 // Mask of 8 bf16 (4 words): bit i set iff element i > 0 (a bf16x2 compare
-// per word: NaN, -0 and +0 give 0).
+// per word: NaN, -0 and +0 give 0).  The compares give 0xFFFF per positive
+// halfword; two byte permutes keep one byte per element (element k of the
+// first four in byte k of a, of the last four in byte k of b), a mask per
+// byte keeps bit k of a's byte k and bit 4 + k of b's, and one multiply by
+// 0x01010101 sums the four (disjoint) bytes into the top byte.
 __device__ __forceinline__ uint32_t mask_bf16x8(const uint32_t (&w)[4]) {
   const __nv_bfloat162 zero = __float2bfloat162_rn(0.f);
-  uint32_t q = 0;
+  uint32_t h[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t h = __hgt2_mask(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]), zero);
-    q |= (h & 0x80008000u) >> (15 - 2 * i);
-  }
-  return (q & 0x5555u) | ((q >> 15) & 0xAAAAu);
+  for (int i = 0; i < 4; ++i) h[i] = __hgt2_mask(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]), zero);
+  const uint32_t a = __byte_perm(h[0], h[1], 0x6420);
+  const uint32_t b = __byte_perm(h[2], h[3], 0x6420);
+  const uint32_t y = (a & 0x08040201u) | (b & 0x80402010u);
+  return (y * 0x01010101u) >> 24;
 }
 
 // Inclusive warp scan: shfl.up's in-range predicate guards each add (no
