@@ -462,6 +462,34 @@ def _fused_compress(fn, name: str, head: tuple, dev, stream: int, stored, M: int
     return vals, vals_offset
 
 
+def _fused_exact(fn, name: str, head: tuple, dev, stream: int, dense_vals: Tensor, M: int,
+                 N: int, grid_n: int, T: int, bitmask: Tensor, prefix: Tensor, pack_sbit: bool,
+                 flags: tuple = ()):
+    """Standalone storage of a fused compress in the reference's order: the
+    fused kernel with no value storage (bitmask, prefix, the dense side
+    output and the total), one host sync for the total, an exactly sized
+    allocation, then ``bs_compact_vals`` from ``dense_vals`` -- the dense
+    side output, which holds exactly the values being stored.  No
+    dense-sized transient.  Returns (vals, vals_offset) or None (alignment)."""
+    ws = R.workspace(dev, T, stream)
+    status = R.status_word(dev)
+    nnz_t = torch.empty((), device=dev, dtype=torch.int64)
+    rc = fn(*head, bitmask.data_ptr(), prefix.data_ptr(), None, 0, int(pack_sbit), None, None,
+            nnz_t.data_ptr(), ws.data_ptr(), ws.numel(), *flags, status.data_ptr(), stream)
+    if rc == _lib.BS_ERR_ALIGN:
+        return None
+    _lib.check(rc, name)
+    nnz = int(nnz_t.item())  # host sync (triton_operators.py:50)
+    if pack_sbit:
+        vals = torch.zeros(packed_storage_nbytes(nnz, bits_per_value(dense_vals.dtype)),
+                           device=dev, dtype=torch.uint8)
+    else:
+        vals = torch.empty(nnz, device=dev, dtype=dense_vals.dtype)
+    vals_offset = torch.zeros((), device=dev, dtype=torch.int64)
+    return compact_vals(dense_vals, bitmask, prefix, vals, vals_offset, M, N, grid_n, T,
+                        _BM, _BN, _BM * _BN, pack_sbit)
+
+
 def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: bool = False):
     """Fused ``h = relu(z + bias)`` + compress of h in one pass over z (bf16).
 
@@ -494,9 +522,14 @@ def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: boo
     bitmask = torch.empty(T * (_BM * _BN // 8), device=dev, dtype=torch.uint8)
     prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
     st = R.stream_handle(dev)
-    out = _fused_compress(_lib.load().bs_compress_bias_relu, "bs_compress_bias_relu",
-                          (z.data_ptr(), M, N, ld, bias.data_ptr(), h.data_ptr(), N), dev, st,
-                          torch.bfloat16, M, N, T, bitmask, prefix, sparse_data, pack_sbit)
+    head = (z.data_ptr(), M, N, ld, bias.data_ptr(), h.data_ptr(), N)
+    fn = _lib.load().bs_compress_bias_relu
+    if sparse_data is None and EXACT_STANDALONE:
+        out = _fused_exact(fn, "bs_compress_bias_relu", head, dev, st, h, M, N, grid_n, T,
+                           bitmask, prefix, pack_sbit)
+    else:
+        out = _fused_compress(fn, "bs_compress_bias_relu", head, dev, st, torch.bfloat16, M, N,
+                              T, bitmask, prefix, sparse_data, pack_sbit)
     if out is None:
         return None
     vals, vals_offset = out
@@ -541,11 +574,17 @@ def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit:
     side = torch.empty((M, N), device=dev, dtype=torch.float8_e4m3fn)
     bitmask = torch.empty(T * TB, device=dev, dtype=torch.uint8)
     prefix = torch.empty(T + 1, device=dev, dtype=torch.uint32)
-    out = _fused_compress(lib.bs_compress_bias_relu_fp8, "bs_compress_bias_relu_fp8",
-                          (z.data_ptr(), M, N, ld, bias.data_ptr(), scale_h.data_ptr(),
-                           R.ptr(scale_s), side.data_ptr()), dev, st,
-                          torch.float8_e4m3fn, M, N, T, bitmask, prefix, sparse_data, pack_sbit,
-                          flags=(fp8_flags(),))
+    head = (z.data_ptr(), M, N, ld, bias.data_ptr(), scale_h.data_ptr(), R.ptr(scale_s),
+            side.data_ptr())
+    fn = lib.bs_compress_bias_relu_fp8
+    if sparse_data is None and EXACT_STANDALONE and not square:
+        # side = to_fp8(h): exactly the stored codes
+        out = _fused_exact(fn, "bs_compress_bias_relu_fp8", head, dev, st, side, M, N,
+                           grid_n, T, bitmask, prefix, pack_sbit, flags=(fp8_flags(),))
+    else:
+        out = _fused_compress(fn, "bs_compress_bias_relu_fp8", head, dev, st,
+                              torch.float8_e4m3fn, M, N, T, bitmask, prefix, sparse_data,
+                              pack_sbit, flags=(fp8_flags(),))
     if out is None:
         return None
     vals, vals_offset = out

@@ -592,4 +592,22 @@ def test_standalone_exact_allocation_equals_one_pass(monkeypatch, pack):
         assert torch.equal(a.prefix.view(torch.int32), b.prefix.view(torch.int32))
         assert a.vals.numel() == b.vals.numel()
         assert torch.equal(a.vals.view(torch.uint8), b.vals.view(torch.uint8))
+    # the fused bias + ReLU forms (bf16 storage, and e4m3 storage of to_fp8(h))
+    from bitsparse_b200.src.operators import compress_bias_relu, compress_bias_relu_fp8
+    for M, N in ((1024, 3072), (192, 256)):
+        z = torch.randn(M, N, generator=g, device="cuda").to(torch.bfloat16)
+        bias = (0.3 * torch.randn(N, generator=g, device="cuda") - 0.5).to(torch.bfloat16)
+        for fused in (lambda: compress_bias_relu(z, bias, None, pack),
+                      lambda: compress_bias_relu_fp8(z, bias, None, pack)):
+            monkeypatch.setattr(OP, "EXACT_STANDALONE", False)
+            ra = fused()
+            monkeypatch.setattr(OP, "EXACT_STANDALONE", True)
+            rb = fused()
+            a, b = ra[-1], rb[-1]
+            assert torch.equal(ra[0].view(torch.uint8), rb[0].view(torch.uint8))
+            assert torch.equal(a.bitmask, b.bitmask)
+            assert torch.equal(a.prefix.view(torch.int32), b.prefix.view(torch.int32))
+            assert a.vals.numel() == b.vals.numel()
+            assert torch.equal(a.vals.view(torch.uint8), b.vals.view(torch.uint8))
+            assert int(b.vals_offset.reshape(-1)[0]) == 0
     B.check_status()
