@@ -1056,13 +1056,19 @@ __global__ void __launch_bounds__(NW * 32, MINB)
         const uint32_t t = lane < warp ? meta[lane] : 0u;
         const uint32_t wex = __reduce_add_sync(0xFFFFFFFFu, t);
         const uint32_t base_addr = smem_addr(stage);
+        // The placement stores are volatile asm (kept in program order), so
+        // the S steps' independent address chains are interleaved here:
+        // element i of every step, then element i + 1 -- each chain's
+        // dependent add is S stores behind its predecessor.
+        uint32_t a[S];
 #pragma unroll
-        for (int s4 = 0; s4 < S; ++s4) {
-          uint32_t a = base_addr + (wex + ex[s4]) * C::SB;
+        for (int s4 = 0; s4 < S; ++s4) a[s4] = base_addr + (wex + ex[s4]) * C::SB;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if constexpr (C::SB == 2) place16(a, m[s4], 1u << i, v[s4][i >> 1] >> (16 * (i & 1)));
-            else place8(a, m[s4], 1u << i, v[s4][i >> 2] >> (8 * (i & 3)));
+        for (int i = 0; i < 8; ++i) {
+#pragma unroll
+          for (int s4 = 0; s4 < S; ++s4) {
+            if constexpr (C::SB == 2) place16(a[s4], m[s4], 1u << i, v[s4][i >> 1] >> (16 * (i & 1)));
+            else place8(a[s4], m[s4], 1u << i, v[s4][i >> 2] >> (8 * (i & 3)));
           }
         }
       }
