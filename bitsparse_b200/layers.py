@@ -59,32 +59,26 @@ class ReluLinear(Function):
         ctx.dtype = dtype
         ctx.has_bias = bias is not None
         ctx.save_for_backward(W)
-        # fused forms: the compressed tensor is finished after the second
-        # GEMM is queued (standalone storage waits on the host for its value
-        # count; the GEMM keeps the GPU busy meanwhile)
         fused = None
         if bias is not None and is_fp8(dtype):
-            fused = compress_bias_relu_fp8(z, bias, sparse_data, pack_sbit, defer=True)
+            fused = compress_bias_relu_fp8(z, bias, sparse_data, pack_sbit)
             if fused is not None:
-                h, scale, pending = fused
+                h, scale, h_sparse = fused
         elif bias is not None:
-            fused = compress_bias_relu(z, bias, sparse_data, pack_sbit, defer=True)
+            fused = compress_bias_relu(z, bias, sparse_data, pack_sbit)
             if fused is not None:
-                h, pending = fused
+                h, h_sparse = fused
                 scale = None
-        if fused is not None:
-            y = matmul(h, W.T, is_fp8(dtype), a_scale=scale)
-            ctx.h_sparse = pending()
-            return y
-        if bias is not None:
-            z = z + bias
-        h = z.relu_()
-        if is_fp8(dtype):
-            h, h_sparse = relu_to_tilesparse_fp8(h, sparse_data, pack_sbit)
-            scale = h_sparse.scale
-        else:
-            scale = None
-            h_sparse = dense_to_tilesparse(h, scale, sparse_data, pack_sbit)
+        if fused is None:
+            if bias is not None:
+                z = z + bias
+            h = z.relu_()
+            if is_fp8(dtype):
+                h, h_sparse = relu_to_tilesparse_fp8(h, sparse_data, pack_sbit)
+                scale = h_sparse.scale
+            else:
+                scale = None
+                h_sparse = dense_to_tilesparse(h, scale, sparse_data, pack_sbit)
         ctx.h_sparse = h_sparse
         return matmul(h, W.T, is_fp8(dtype), a_scale=scale)
 

@@ -464,20 +464,13 @@ def _fused_compress(fn, name: str, head: tuple, dev, stream: int, stored, M: int
 
 def _fused_exact(fn, name: str, head: tuple, dev, stream: int, dense_vals: Tensor, M: int,
                  N: int, grid_n: int, T: int, bitmask: Tensor, prefix: Tensor, pack_sbit: bool,
-                 flags: tuple = (), defer: bool = False):
+                 flags: tuple = ()):
     """Standalone storage of a fused compress in the reference's order: the
     fused kernel with no value storage (bitmask, prefix, the dense side
-    output and the total), one host wait for the total, an exactly sized
+    output and the total), one host sync for the total, an exactly sized
     allocation, then ``bs_compact_vals`` from ``dense_vals`` -- the dense
     side output, which holds exactly the values being stored.  No
-    dense-sized transient.  Returns (vals, vals_offset), or None
-    (alignment).
-
-    ``defer``: the total goes to pinned host memory behind an event and a
-    zero-argument callable is returned instead; calling it waits for that
-    event only (not for work queued after the compress, e.g. the FFN's
-    second GEMM, which keeps the GPU busy meanwhile), then allocates and
-    queues the compaction.  ``dense_vals`` must not be modified in between."""
+    dense-sized transient.  Returns (vals, vals_offset) or None (alignment)."""
     ws = R.workspace(dev, T, stream)
     status = R.status_word(dev)
     nnz_t = torch.empty((), device=dev, dtype=torch.int64)
@@ -486,33 +479,18 @@ def _fused_exact(fn, name: str, head: tuple, dev, stream: int, dense_vals: Tenso
     if rc == _lib.BS_ERR_ALIGN:
         return None
     _lib.check(rc, name)
-
-    def finish(nnz: int):
-        if pack_sbit:
-            vals = torch.zeros(packed_storage_nbytes(nnz, bits_per_value(dense_vals.dtype)),
-                               device=dev, dtype=torch.uint8)
-        else:
-            vals = torch.empty(nnz, device=dev, dtype=dense_vals.dtype)
-        vals_offset = torch.zeros((), device=dev, dtype=torch.int64)
-        return compact_vals(dense_vals, bitmask, prefix, vals, vals_offset, M, N, grid_n, T,
-                            _BM, _BN, _BM * _BN, pack_sbit)
-
-    if not defer:
-        return finish(int(nnz_t.item()))  # host sync (triton_operators.py:50)
-    host = torch.empty((), dtype=torch.int64, pin_memory=True)
-    host.copy_(nnz_t, non_blocking=True)
-    done = torch.cuda.Event()
-    done.record(torch.cuda.current_stream(dev))
-
-    def deferred():
-        done.synchronize()  # the compress and the copy of its total only
-        return finish(int(host))
-
-    return deferred
+    nnz = int(nnz_t.item())  # host sync (triton_operators.py:50)
+    if pack_sbit:
+        vals = torch.zeros(packed_storage_nbytes(nnz, bits_per_value(dense_vals.dtype)),
+                           device=dev, dtype=torch.uint8)
+    else:
+        vals = torch.empty(nnz, device=dev, dtype=dense_vals.dtype)
+    vals_offset = torch.zeros((), device=dev, dtype=torch.int64)
+    return compact_vals(dense_vals, bitmask, prefix, vals, vals_offset, M, N, grid_n, T,
+                        _BM, _BN, _BM * _BN, pack_sbit)
 
 
-def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: bool = False,
-                       defer: bool = False):
+def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: bool = False):
     """Fused ``h = relu(z + bias)`` + compress of h in one pass over z (bf16).
 
     Returns ``(h, BitsparseTensor)`` -- h dense (the FFN's second GEMM needs
@@ -520,11 +498,6 @@ def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: boo
     when the one-pass kernel cannot read these tensors (alignment), in which
     case the caller runs the steps separately.  Same storage modes as
     ``compress`` (standalone, or a TensorBuffer arena).
-
-    ``defer`` (standalone storage): the second element is a zero-argument
-    callable returning the BitsparseTensor; the caller queues work that
-    does not need it (the second GEMM) first, so the host's wait for the
-    value count overlaps that work.  h must not be modified before the call.
     """
     if z.dtype != torch.bfloat16 or bias.dtype != torch.bfloat16:
         return None
@@ -551,27 +524,21 @@ def compress_bias_relu(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: boo
     st = R.stream_handle(dev)
     head = (z.data_ptr(), M, N, ld, bias.data_ptr(), h.data_ptr(), N)
     fn = _lib.load().bs_compress_bias_relu
-    exact = sparse_data is None and EXACT_STANDALONE
-    if exact:
+    if sparse_data is None and EXACT_STANDALONE:
         out = _fused_exact(fn, "bs_compress_bias_relu", head, dev, st, h, M, N, grid_n, T,
-                           bitmask, prefix, pack_sbit, defer=defer)
+                           bitmask, prefix, pack_sbit)
     else:
         out = _fused_compress(fn, "bs_compress_bias_relu", head, dev, st, torch.bfloat16, M, N,
                               T, bitmask, prefix, sparse_data, pack_sbit)
     if out is None:
         return None
-
-    def make(vo):
-        return BitsparseTensor(vo[0], bitmask, prefix, (M, N), torch.bfloat16, grid_m, grid_n,
-                               _BM, _BN, vals_offset=vo[1], pack_sbit=pack_sbit)
-
-    if defer:
-        return h, ((lambda: make(out())) if exact else (lambda: make(out)))
-    return h, make(out)
+    vals, vals_offset = out
+    return h, BitsparseTensor(vals, bitmask, prefix, (M, N), torch.bfloat16, grid_m, grid_n,
+                              _BM, _BN, vals_offset=vals_offset, pack_sbit=pack_sbit)
 
 
 def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit: bool = False,
-                           square: bool = False, defer: bool = False):
+                           square: bool = False):
     """FP8 form of ``compress_bias_relu``: h = relu(z + bias) is stored as
     ``to_fp8(h)`` (lib_sparse/layers.py:32-37, 112-117) and compressed, in two
     passes over z (the amax of h, then quantise + compress).
@@ -579,8 +546,7 @@ def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit:
     Returns ``(side, side_scale, BitsparseTensor)``: ``side`` is the dense
     e4m3 operand of the FFN's second GEMM -- ``to_fp8(h)`` or, with
     ``square``, ``to_fp8(h * h)`` (Relu2Linear, RELU2_SCALE = 1) -- or
-    ``None`` when the one-pass kernel cannot read the tensors.  ``defer``:
-    as in ``compress_bias_relu`` (the third element becomes a callable).
+    ``None`` when the one-pass kernel cannot read the tensors.
     """
     from ..config import RELU2_SCALE
     from ..fp8 import fp8_flags
@@ -611,27 +577,20 @@ def compress_bias_relu_fp8(z: Tensor, bias: Tensor, sparse_data=None, pack_sbit:
     head = (z.data_ptr(), M, N, ld, bias.data_ptr(), scale_h.data_ptr(), R.ptr(scale_s),
             side.data_ptr())
     fn = lib.bs_compress_bias_relu_fp8
-    exact = sparse_data is None and EXACT_STANDALONE and not square
-    if exact:  # side = to_fp8(h): exactly the stored codes
+    if sparse_data is None and EXACT_STANDALONE and not square:
+        # side = to_fp8(h): exactly the stored codes
         out = _fused_exact(fn, "bs_compress_bias_relu_fp8", head, dev, st, side, M, N,
-                           grid_n, T, bitmask, prefix, pack_sbit, flags=(fp8_flags(),),
-                           defer=defer)
+                           grid_n, T, bitmask, prefix, pack_sbit, flags=(fp8_flags(),))
     else:
         out = _fused_compress(fn, "bs_compress_bias_relu_fp8", head, dev, st,
                               torch.float8_e4m3fn, M, N, T, bitmask, prefix, sparse_data,
                               pack_sbit, flags=(fp8_flags(),))
     if out is None:
         return None
-
-    def make(vo):
-        return BitsparseTensor(vo[0], bitmask, prefix, (M, N), torch.float8_e4m3fn, grid_m,
-                               grid_n, _BM, _BN, scale=scale_h, vals_offset=vo[1],
-                               pack_sbit=pack_sbit)
-
-    side_scale = scale_s if square else scale_h
-    if defer:
-        return side, side_scale, ((lambda: make(out())) if exact else (lambda: make(out)))
-    return side, side_scale, make(out)
+    vals, vals_offset = out
+    sp = BitsparseTensor(vals, bitmask, prefix, (M, N), torch.float8_e4m3fn, grid_m, grid_n,
+                         _BM, _BN, scale=scale_h, vals_offset=vals_offset, pack_sbit=pack_sbit)
+    return side, (scale_s if square else scale_h), sp
 
 
 # ---------------------------------------------------------------------------
