@@ -101,6 +101,8 @@ struct CompressParams {
   // per-tile scale mode: scale of each tile (amax_t / 448), written by the
   // one-pass kernel
   float *tile_scales;
+  // one-pass kernel: the 3-D tile-column map is valid (N % 64 == 0)
+  int box3;
 };
 
 template <int DT_IN, bool QUANT, int TPP>
@@ -634,6 +636,17 @@ __device__ __forceinline__ void tma_load_tile(void *dst, const CUtensorMap *map,
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
       : "memory");
 }
+// 3-D tiled TMA load through the tile-column view {64 columns, M rows, N / 64
+// tile columns}: a box {64, 64, n} is n horizontally adjacent tiles, landing
+// tile-major in shared memory (no multicast).
+__device__ __forceinline__ void tma_load_tiles3(void *dst, const CUtensorMap *map, int y, int z,
+                                                uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -782,7 +795,8 @@ __device__ __forceinline__ void place8(uint32_t &a, uint32_t m, uint32_t bit, ui
 template <int DT_IN, bool QUANT, bool PACK, int TPP_, int NW, int D, int A, int MINB,
           bool BIAS = false, bool QC = false, bool TS = false>
 __global__ void __launch_bounds__(NW * 32, MINB)
-    onepass_kernel(const __grid_constant__ CUtensorMap tmap, const CompressParams P) {
+    onepass_kernel(const __grid_constant__ CUtensorMap tmap,
+                   const __grid_constant__ CUtensorMap tmap3, const CompressParams P) {
   using O = Onepass<DT_IN, QUANT, TPP_, NW, D, A>;
   using C = typename O::C;
   constexpr int TPP = O::TPP, RW = O::RW, NS = O::NS;
@@ -803,6 +817,10 @@ __global__ void __launch_bounds__(NW * 32, MINB)
     const int nt = (int)min((long long)TPP, P.num_tiles - (long long)t0);
     mbar_expect_tx(&bars[st], (uint32_t)(nt * kTileNumel * O::EB));
     uint32_t tm = t0 / gn, tn = t0 - tm * gn;
+    if (P.box3 && nt == TPP && tn + TPP <= gn) {  // one box: the partition's tiles share a tile row
+      tma_load_tiles3(dst, &tmap3, (int)(tm * kTileM), (int)tn, &bars[st]);
+      return;
+    }
     for (int j = 0; j < nt; ++j) {
       tma_load_tile(dst + j * kTileNumel * O::EB, &tmap, (int)(tn * kTileN), (int)(tm * kTileM),
                     &bars[st]);
@@ -1220,11 +1238,28 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
   const cuuint32_t estr[2] = {1, 1};
   const CUtensorMapDataType ty =
       O::EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
   if (encode(&map, ty, 2, const_cast<uint8_t *>(P.dense), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, promo,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return kNotApplicable;
+  // The tile-column view {64 columns, M rows, N / 64 tile columns} with
+  // strides (row, tile column) = (row_bytes, 64 elements), for whole tile
+  // columns only: a partition whose tiles share a tile row is then one TMA
+  // box instead of TPP (measured 2-4% faster at 50-99% sparsity on 8192 x
+  // 14336 bf16; the four-tile loads remain for partitions that wrap a row).
+  CUtensorMap map3 = map;
+  int box3 = 0;
+  if (P.N % kTileN == 0) {
+    const cuuint64_t dims3[3] = {(cuuint64_t)kTileN, (cuuint64_t)P.M, (cuuint64_t)(P.N / kTileN)};
+    const cuuint64_t strides3[2] = {(cuuint64_t)row_bytes, (cuuint64_t)(kTileN * O::EB)};
+    const cuuint32_t box3d[3] = {kTileN, kTileM, (cuuint32_t)O::TPP};
+    const cuuint32_t estr3[3] = {1, 1, 1};
+    box3 = encode(&map3, ty, 3, const_cast<uint8_t *>(P.dense), dims3, strides3, box3d, estr3,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, promo,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (!box3) map3 = map;
+  }
   auto kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS, false, TS>;
   if constexpr (QUANT && !TS) {  // the compiled to_fp8's quantiser: its own instantiation
     if (P.qcompiled) kernel = onepass_kernel<DT_IN, QUANT, PACK, TPP, NW, D, A, MINB, BIAS, true>;
@@ -1235,6 +1270,7 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
   if (resident > O::CV * NW * 32 + 1) resident = O::CV * NW * 32 + 1;
   CompressParams Q = P;
   Q.num_parts = (P.num_tiles + O::TPP - 1) / O::TPP;
+  Q.box3 = box3;
   // counts are published as 64-bit epoch-tagged words (no clearing needed);
   // a partition holds at least four tiles, so they fit in the 2 bytes per
   // tile that bs_compress_workspace_bytes provides
@@ -1251,7 +1287,7 @@ static int launch_onepass(const CompressParams &P, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kernel, map, Q) != cudaSuccess) return BS_ERR_LAUNCH;
+  if (cudaLaunchKernelEx(&cfg, kernel, map, map3, Q) != cudaSuccess) return BS_ERR_LAUNCH;
   return BS_OK;
 }
 
