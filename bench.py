@@ -766,14 +766,14 @@ def mlp_suite(dev):
     return {
             "config2_gpt2_small_relu_bf16": mlp_bench(
                 {"tokens": 8 * 1024, "d": 768, "H": 3072, "relu2": False,
-                 "storage": torch.bfloat16, "bias_sigma": 1.0}, 10, 3, dev),
+                 "storage": torch.bfloat16, "bias_sigma": 1.0}, 50, 10, dev),
             "config2_relu_bf16_90pct_sparse": mlp_bench(
                 {"tokens": 8 * 1024, "d": 768, "H": 3072, "relu2": False,
-                 "storage": torch.bfloat16, "bias_sigma": 1.2816}, 10, 3, dev),
+                 "storage": torch.bfloat16, "bias_sigma": 1.2816}, 50, 10, dev),
             # the nanoGPT MLP's own activation (ReLU^2), bf16 storage
             "config2_gpt2_small_relu2_bf16": mlp_bench(
                 {"tokens": 8 * 1024, "d": 768, "H": 3072, "relu2": True,
-                 "storage": torch.bfloat16, "bias_sigma": 1.0}, 10, 3, dev),
+                 "storage": torch.bfloat16, "bias_sigma": 1.0}, 50, 10, dev),
             "config4_nemotron_relu2_fp8": mlp_bench(
                 {"tokens": 16384, "d": 4096, "H": 16384, "relu2": True,
                  "storage": torch.float8_e4m3fn, "bias_sigma": 0.0}, 5, 2, dev),

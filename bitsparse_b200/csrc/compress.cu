@@ -874,13 +874,16 @@ __global__ void __launch_bounds__(NW * 32, MINB)
       if (pf < nparts) fetch(pf, (int)((r + A) % NS));
     }
     // 2. counts of the partitions between this CTA's last flushed one and q
-    //    (G - 1 of them; a thread reads at most kCv)
+    //    (G - 1 of them; a thread reads at most kCv).  The raw words are
+    //    only decoded at the flush: a use here would hold every warp for an
+    //    L2 round trip (~1.7k cycles per round, measured) before compaction.
     constexpr int kCv = O::CV;
-    uint32_t cv[kCv];
+    const unsigned long long kOne = ((unsigned long long)epoch << 32) | 1u;  // "count 0"
+    unsigned long long cw[kCv];
 #pragma unroll
     for (int i = 0; i < kCv; ++i) {
       const long long ci = known + 1 + tid + (long long)i * NW * 32;
-      cv[i] = (q >= 0 && ci < q) ? count_of(ld_relaxed_u64(cnt64 + ci), epoch) : 1u;
+      cw[i] = (q >= 0 && ci < q) ? ld_relaxed_u64(cnt64 + ci) : kOne;
     }
     // 3. compact partition p in place
     if (p < nparts) {
@@ -1098,6 +1101,9 @@ __global__ void __launch_bounds__(NW * 32, MINB)
       const uint32_t *meta = s_meta + slot * O::META;  // written before an earlier barrier
       bool late = false;
       uint32_t sum = 0;
+      uint32_t cv[kCv];
+#pragma unroll
+      for (int i = 0; i < kCv; ++i) cv[i] = count_of(cw[i], epoch);
 #pragma unroll
       for (int i = 0; i < kCv; ++i) {
         const long long ci = known + 1 + tid + (long long)i * NW * 32;
