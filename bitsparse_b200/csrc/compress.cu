@@ -888,34 +888,17 @@ __global__ void __launch_bounds__(NW * 32, MINB)
     // 3. compact partition p in place
     if (p < nparts) {
       const int st = (int)(r % NS);
-      {
-        bool ok = false;
-        for (uint32_t n = 0; n < kMaxPolls && !(ok = mbar_try_wait(&bars[st], (uint32_t)((r / NS) & 1))); ++n) {
-        }
-        if (!ok && tid == 0) status_or(P.status, BS_STATUS_TIMEOUT);
-      }
-      uint8_t *stage = smem_dyn + (size_t)st * O::IN_BYTES;
-      uint32_t *meta = s_meta + st * O::META;
       const int rho0 = warp * RW;  // first partition row of this warp
       const int j = rho0 / kTileM;  // its tile
       const long long tile = p * TPP + j;
-      // lane: 8 consecutive elements (16 B of bf16 / 8 B of fp8) of row
-      // rho0 + 4s + lane / 8 in step s; its 8 mask bits are exactly one
-      // bitmask byte.  All of a warp's rows are read before the barrier
-      // below, after which values are written in place at their
-      // partition-wide positions (never past the element they came from).
-      constexpr int S = RW / 4;
-      constexpr int VW = O::EB == 2 ? 4 : 2;  // input words per lane and step
-      uint32_t v[S][VW], m[S], ex[S];
-      uint32_t wtot = 0;
       const int sub = lane >> 3, c8 = lane & 7;
       const bool valid = tile < P.num_tiles;  // warp-uniform
-      if (valid) {
-        uint8_t *bm = P.bitmask + (p * TPP * kTileM + rho0 + sub) * 8 + c8;
-        // bias + ReLU mode: this lane's 8 columns are the same in every step
-        uint32_t bw[4] = {0, 0, 0, 0};
-        int64_t brow0 = 0, bcol = 0;
-        if constexpr (BIAS) {
+      // bias + ReLU mode: this lane's 8 columns are the same in every step;
+      // the bias is loaded before the stage wait (its latency overlaps it)
+      uint32_t bw[4] = {0, 0, 0, 0};
+      int64_t brow0 = 0, bcol = 0;
+      if constexpr (BIAS) {
+        if (valid) {
           const int64_t tm = tile / P.grid_n, tn = tile - tm * P.grid_n;
           brow0 = tm * kTileM + (rho0 - j * kTileM) + sub;
           bcol = tn * kTileN + 8 * c8;
@@ -929,6 +912,26 @@ __global__ void __launch_bounds__(NW * 32, MINB)
                               << (16 * (i & 1));
           }
         }
+      }
+      {
+        bool ok = false;
+        for (uint32_t n = 0; n < kMaxPolls && !(ok = mbar_try_wait(&bars[st], (uint32_t)((r / NS) & 1))); ++n) {
+        }
+        if (!ok && tid == 0) status_or(P.status, BS_STATUS_TIMEOUT);
+      }
+      uint8_t *stage = smem_dyn + (size_t)st * O::IN_BYTES;
+      uint32_t *meta = s_meta + st * O::META;
+      // lane: 8 consecutive elements (16 B of bf16 / 8 B of fp8) of row
+      // rho0 + 4s + lane / 8 in step s; its 8 mask bits are exactly one
+      // bitmask byte.  All of a warp's rows are read before the barrier
+      // below, after which values are written in place at their
+      // partition-wide positions (never past the element they came from).
+      constexpr int S = RW / 4;
+      constexpr int VW = O::EB == 2 ? 4 : 2;  // input words per lane and step
+      uint32_t v[S][VW], m[S], ex[S];
+      uint32_t wtot = 0;
+      if (valid) {
+        uint8_t *bm = P.bitmask + (p * TPP * kTileM + rho0 + sub) * 8 + c8;
 #pragma unroll
         for (int s4 = 0; s4 < S; ++s4) {
           const uint8_t *src = stage + ((rho0 + 4 * s4 + sub) * kTileN + 8 * c8) * O::EB;
