@@ -145,28 +145,41 @@ __device__ __forceinline__ uint32_t staged_value(const uint8_t *stage, uint32_t 
 }
 
 // Block-wide exclusive scan of S per-thread counts in (slot, warp, lane) order.
+// One barrier: after it every warp reads all S * 8 warp totals and adds up
+// those before its own (slot, warp) with one warp reduction per slot (no
+// second-level scan by one warp, no second barrier).  The caller passes a
+// barrier before s_wt is written again.
 template <int S>
 __device__ __forceinline__ void block_excl_scan(const uint32_t (&cnt)[S], uint32_t (&ex)[S],
                                                 uint32_t *s_wt) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int NW = S * 8;
+  static_assert(NW <= 32, "a warp holds the warp totals");
   uint32_t lex[S];
+  if constexpr (S == 2) {
+    // both slots in one scan: 16-bit fields (a warp's slot total is at most
+    // 32 chunks x 32 values, so the low field never carries)
+    const uint32_t packed = cnt[0] | (cnt[1] << 16);
+    const uint32_t inc = warp_incl_scan(packed);
+    lex[0] = (inc & 0xFFFFu) - cnt[0];
+    lex[1] = (inc >> 16) - cnt[1];
+    if (lane == 31) {
+      s_wt[warp] = inc & 0xFFFFu;
+      s_wt[8 + warp] = inc >> 16;
+    }
+  } else {
 #pragma unroll
-  for (int s = 0; s < S; ++s) {
-    const uint32_t inc = warp_incl_scan(cnt[s]);
-    lex[s] = inc - cnt[s];
-    if (lane == 31) s_wt[s * 8 + warp] = inc;
+    for (int s = 0; s < S; ++s) {
+      const uint32_t inc = warp_incl_scan(cnt[s]);
+      lex[s] = inc - cnt[s];
+      if (lane == 31) s_wt[s * 8 + warp] = inc;
+    }
   }
   __syncthreads();
-  if (warp == 0) {
-    constexpr int NW = S * 8;
-    static_assert(NW <= 32, "one warp scans the warp totals");
-    const uint32_t v = lane < NW ? s_wt[lane] : 0;
-    const uint32_t inc = warp_incl_scan(v);
-    if (lane < NW) s_wt[lane] = inc - v;
-  }
-  __syncthreads();
+  const uint32_t t = lane < NW ? s_wt[lane] : 0u;
 #pragma unroll
-  for (int s = 0; s < S; ++s) ex[s] = s_wt[s * 8 + warp] + lex[s];
+  for (int s = 0; s < S; ++s)
+    ex[s] = __reduce_add_sync(0xFFFFFFFFu, lane < s * 8 + warp ? t : 0u) + lex[s];
 }
 
 // Chunk geometry for 32-byte chunks of OB-byte elements.
