@@ -416,6 +416,39 @@ def test_large_arena_odd_offsets(dtype, pack):
     B.check_status()
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("pack", [False, True])
+def test_partitions_across_tile_rows(dtype, pack):
+    """Whole 64-column tile columns whose count per tile row is not a
+    multiple of the one-pass kernel's tiles per partition (4 bf16 / 8 fp8):
+    partitions inside one tile row are loaded as one 3-D box, those that
+    wrap into the next tile row tile by tile, in the same launch.  Exact
+    against the oracle; the fused quantising compress of the same data
+    equals compressing its to_fp8 output."""
+    odt = {torch.bfloat16: O.DT_BF16, torch.float8_e4m3fn: O.DT_E4M3}[dtype]
+    g = torch.Generator().manual_seed(23)
+    shapes = ((200, 64 * 5), (129, 64 * 7), (1000, 64 * 6), (4096, 64 * 9), (300, 64 * 13))
+    for i, (M, N) in enumerate(shapes):
+        h = (torch.randn(M, N, generator=g) + 0.4 * (i - 2)).relu()
+        x = h.to(dtype)
+        sp = dense_to_tilesparse(x.cuda(), None, None, pack)
+        osp = O.dense_to_tilesparse(bits(x), odt, None, pack)
+        np.testing.assert_array_equal(bits(sp.bitmask), osp.bitmask)
+        np.testing.assert_array_equal(bits(sp.prefix), osp.prefix)
+        np.testing.assert_array_equal(bits(sp.vals), osp.vals)
+        if dtype == torch.float8_e4m3fn and not pack:
+            hb = h.to(torch.bfloat16).cuda()
+            q, fsp = relu_to_tilesparse_fp8(hb)
+            q2, _ = to_fp8(hb)
+            assert torch.equal(q.view(torch.uint8), q2.view(torch.uint8))
+            ref = dense_to_tilesparse(q2, None, None, False)
+            assert torch.equal(fsp.bitmask, ref.bitmask)
+            assert torch.equal(fsp.prefix, ref.prefix)
+            n = int(ref.prefix[-1].item())
+            assert torch.equal(fsp.vals[:n].view(torch.uint8), ref.vals[:n].view(torch.uint8))
+    B.check_status()
+
+
 @pytest.mark.parametrize("M, N", [(512, 1024), (200, 3000), (8192, 3072), (64, 64)])
 @pytest.mark.parametrize("pack", [False, True])
 def test_compress_bias_relu_equals_separate_steps(M, N, pack):
