@@ -735,6 +735,18 @@ __global__ void __launch_bounds__(kThreads) unpack_pipe_kernel(const UnpackParam
       const uint32_t mm = m[s];
       uint32_t r = ex[s];
       uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if constexpr (!PACK && SB == 2) {
+        // two elements per output word, joined by one byte permute
+#pragma unroll
+        for (int e = 0; e < G::VEC; e += 2) {
+          const uint32_t b0 = (mm >> e) & 1u, b1 = (mm >> (e + 1)) & 1u;
+          const uint32_t v0 = staged_value<SDT, PACK>(stg, first, r) & (0u - b0);
+          r += b0;
+          const uint32_t v1 = staged_value<SDT, PACK>(stg, first, r) & (0u - b1);
+          r += b1;
+          w[e >> 1] = __byte_perm(v0, v1, 0x5410);
+        }
+      } else
 #pragma unroll
       for (int e = 0; e < G::VEC; ++e) {
         uint32_t v;
